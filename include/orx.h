@@ -1,0 +1,110 @@
+/* C ABI of the B200 Qwen3-ASR text-decoder library (liborator_b200.so).
+ *
+ * Plain pointers, sizes and status codes; no C++ or torch types cross it.
+ * Every call returns ORX_OK (0) or an error code; orx_last_error() gives the
+ * message of the last failure on the calling thread.  Streams are passed as
+ * `void*` holding a cudaStream_t (NULL = legacy default stream).
+ *
+ * Each entry point names the reference interface it replaces
+ * (thomas-hiddenpeak/Orator, path:line).
+ */
+#ifndef ORX_H_
+#define ORX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORX_OK 0
+#define ORX_EINVAL 1 /* bad argument or state (std::runtime_error in the reference) */
+#define ORX_ECUDA 2  /* CUDA failure (CheckCudaError -> GpuMemoryException) */
+#define ORX_EINTERNAL 3
+
+/* AsrTextConfig, include/model/asr_text_decoder.h:30-43. The head geometry is
+ * fixed at Qwen3-ASR-1.7B (2048 / 16 q / 8 kv / 128 / 6144) and checked. */
+typedef struct orx_config {
+  int hidden_size;
+  int num_layers;
+  int num_q_heads;
+  int num_kv_heads;
+  int head_dim;
+  int intermediate_size;
+  int vocab_size;
+  float rms_norm_eps;
+  float rope_theta;
+  int max_seq_len;
+  int profile;
+  int cuda_graph_enabled;
+} orx_config;
+
+typedef struct orx_decoder orx_decoder;
+
+const char* orx_last_error(void);
+int orx_version(void);
+/* Fills `cfg` with the AsrTextConfig defaults. */
+void orx_config_default(orx_config* cfg);
+
+/* AsrTextDecoder::AsrTextDecoder (asr_text_decoder.h:47); allocates weights,
+ * the paged KV pool for max_seq_len positions and all step buffers on the
+ * current device. */
+int orx_decoder_create(const orx_config* cfg, orx_decoder** out);
+void orx_decoder_destroy(orx_decoder* d);
+
+/* AsrTextDecoder::LoadWeights (asr_text_decoder.cu:251-336), one tensor at a
+ * time by its checkpoint name (thinker.model.*). dtype 0 = fp32, 1 = bf16 bits;
+ * on_device = 1 if `data` is a device pointer. */
+int orx_decoder_set_tensor(orx_decoder* d, const char* name, const void* data, int dtype,
+                           size_t numel, int on_device);
+/* Loads a sharded safetensors checkpoint directory (model.safetensors.index.json
+ * or model.safetensors), as io::ShardedSafeTensors feeds LoadWeights
+ * (src/io/sharded_safetensor.cc). */
+int orx_decoder_load_safetensors(orx_decoder* d, const char* model_dir);
+/* Seeded synthetic weights generated on the device (no reference counterpart:
+ * stands in for a checkpoint on machines without one). */
+int orx_decoder_init_synthetic(orx_decoder* d, int seed);
+int orx_decoder_weights_complete(const orx_decoder* d, int* complete);
+
+/* ResetCache / TruncateCache / cache_len (asr_text_decoder.h:51,73,76). */
+int orx_decoder_reset_cache(orx_decoder* d);
+int orx_decoder_truncate_cache(orx_decoder* d, int len);
+int orx_decoder_cache_len(const orx_decoder* d, int* out);
+/* Embed (asr_text_decoder.cu:340-346): bf16 row -> fp32 `out[hidden]` (host). */
+int orx_decoder_embed(const orx_decoder* d, int token_id, float* out);
+
+/* PrefillAt / Prefill (asr_text_decoder.cu:585-617): host embeds [T, hidden]
+ * appended at pos0; logits of the last row stay on the device; synchronizes. */
+int orx_decoder_prefill_at(orx_decoder* d, const float* embeds, int T, int pos0, void* stream);
+/* Same with device-resident embeds; asynchronous on `stream`. */
+int orx_decoder_prefill_at_device(orx_decoder* d, const float* d_embeds, int T, int pos0,
+                                  void* stream);
+/* DecodeStep (asr_text_decoder.cu:619-634): one host embedding at `pos`. */
+int orx_decoder_decode_step(orx_decoder* d, const float* embed, int pos, void* stream);
+/* DecodeStepDevice (asr_text_decoder.cu:655-671): token id read on the device. */
+int orx_decoder_decode_step_device(orx_decoder* d, const int* d_token, int pos, void* stream);
+/* Argmax / ArgmaxToDevice / ReadTokenId (asr_text_decoder.cu:636-653). */
+int orx_decoder_argmax(orx_decoder* d, int ban0, int ban1, void* stream, int* out);
+int orx_decoder_argmax_to_device(orx_decoder* d, int* d_out, int ban0, int ban1, void* stream);
+int orx_decoder_read_token_id(const orx_decoder* d, const int* d_token, void* stream, int* out);
+/* DecodeGreedy (asr_text_decoder.cu:698-889). `out_tokens` holds max_new ints;
+ * *n_out receives the number of emitted tokens (EOS excluded). */
+int orx_decoder_decode_greedy(orx_decoder* d, int start_pos, int max_new, int eos0, int eos1,
+                              int ban_steps, int batch, void* stream, int* out_tokens, int* n_out);
+/* CopyLogits (asr_text_decoder.cu:891-899): `out[vocab]` on the host. */
+int orx_decoder_copy_logits(const orx_decoder* d, float* out);
+/* Device pointer of the logits buffer (valid until destroy). */
+int orx_decoder_logits_device(const orx_decoder* d, const float** out);
+/* Device error word written by bounded waits (0 = none). */
+int orx_decoder_device_error(const orx_decoder* d, int* out);
+
+/* Seeded synthetic fp32 data on the device, bit-exact with oracle/synth.py
+ * (test and benchmark inputs; no reference counterpart). */
+int orx_synth_f32(float* d_out, long long n, int seed, int tensor_id, double std, float mean,
+                  int round_bf16, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ORX_H_ */

@@ -1,0 +1,32 @@
+#!/usr/bin/env bash
+# Compile the reference decoder from its own sources (read in place, never
+# copied) plus oracle/ref_harness.cc into oracle/_ref/libref_asr.so.
+# TEST INFRASTRUCTURE: the resulting library is a parity checker only.
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]
+set -euo pipefail
+HERE="$(cd "$(dirname "$0")" && pwd)"
+R="${1:-${ORATOR_REFERENCE:-/root/reference}}"
+OUT="$HERE/_ref"
+if [ ! -f "$R/src/model/asr_text_decoder.cu" ]; then
+  echo "reference sources not found under $R; skipping" >&2
+  exit 0
+fi
+mkdir -p "$OUT/obj"
+NVCC="${NVCC:-nvcc}"
+GEN="-gencode arch=compute_100a,code=sm_100a"
+objs=()
+for f in src/model/asr_text_decoder.cu src/model/asr_gemm.cu src/model/asr_ops.cu; do
+  o="$OUT/obj/$(basename "$f").o"
+  "$NVCC" -std=c++20 -O3 $GEN -Xcompiler -fPIC -I"$R/include" -c "$R/$f" -o "$o"
+  objs+=("$o")
+done
+for f in src/gpu/memory.cc src/gpu/gpu_lock.cc src/io/safetensor.cc \
+         src/io/sharded_safetensor.cc src/core/tensor.cc; do
+  o="$OUT/obj/$(basename "$f").o"
+  g++ -std=c++20 -O2 -fPIC -I"$R/include" -I/usr/local/cuda/include -c "$R/$f" -o "$o"
+  objs+=("$o")
+done
+g++ -std=c++20 -O2 -fPIC -I"$R/include" -I/usr/local/cuda/include \
+  -c "$HERE/ref_harness.cc" -o "$OUT/obj/ref_harness.o"
+"$NVCC" -shared $GEN -o "$OUT/libref_asr.so" "${objs[@]}" "$OUT/obj/ref_harness.o" -lcudart
+echo "built $OUT/libref_asr.so"

@@ -1,0 +1,284 @@
+// extern "C" entry points declared in include/orx.h.
+#include <cstring>
+#include <exception>
+#include <new>
+#include <string>
+
+#include "../../include/orx.h"
+#include "common.cuh"
+#include "engine.h"
+#include "safetensors.h"
+
+struct orx_decoder {
+  orx::Decoder* dec = nullptr;
+  int device = 0;
+};
+
+namespace {
+thread_local std::string g_err;
+
+template <typename F>
+int guard(F&& f) {
+  try {
+    f();
+    return ORX_OK;
+  } catch (const orx::CudaError& e) {
+    g_err = e.what();
+    return ORX_ECUDA;
+  } catch (const std::invalid_argument& e) {
+    g_err = e.what();
+    return ORX_EINVAL;
+  } catch (const std::bad_alloc&) {
+    g_err = "host allocation failed";
+    return ORX_EINTERNAL;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return ORX_EINVAL;
+  }
+}
+
+void need(const void* p, const char* what) {
+  if (!p) throw std::invalid_argument(std::string("null argument: ") + what);
+}
+
+// Calls run on the device the decoder was created on.
+struct DeviceScope {
+  explicit DeviceScope(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) orx::check(cudaSetDevice(dev), "cudaSetDevice");
+    restore = prev != dev;
+  }
+  ~DeviceScope() {
+    if (restore) cudaSetDevice(prev);
+  }
+  int prev = 0;
+  bool restore = false;
+};
+
+cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+}  // namespace
+
+extern "C" {
+
+const char* orx_last_error(void) { return g_err.c_str(); }
+int orx_version(void) { return 1; }
+
+void orx_config_default(orx_config* c) {
+  if (!c) return;
+  c->hidden_size = 2048;
+  c->num_layers = 28;
+  c->num_q_heads = 16;
+  c->num_kv_heads = 8;
+  c->head_dim = 128;
+  c->intermediate_size = 6144;
+  c->vocab_size = 151936;
+  c->rms_norm_eps = 1e-6f;
+  c->rope_theta = 1000000.0f;
+  c->max_seq_len = 2048;
+  c->profile = 0;
+  c->cuda_graph_enabled = 1;
+}
+
+int orx_decoder_create(const orx_config* cfg, orx_decoder** out) {
+  return guard([&] {
+    need(cfg, "cfg");
+    need(out, "out");
+    *out = nullptr;
+    if (cfg->hidden_size != orx::kHidden || cfg->num_q_heads != orx::kQHeads ||
+        cfg->num_kv_heads != orx::kKvHeads || cfg->head_dim != orx::kHeadDim ||
+        cfg->intermediate_size != orx::kInter)
+      throw std::invalid_argument("only the Qwen3-ASR-1.7B head geometry is supported");
+    if (cfg->rms_norm_eps != 1e-6f) throw std::invalid_argument("rms_norm_eps must be 1e-6");
+    orx::ModelConfig mc;
+    mc.num_layers = cfg->num_layers;
+    mc.vocab_size = cfg->vocab_size;
+    mc.max_seq_len = cfg->max_seq_len;
+    mc.rms_norm_eps = cfg->rms_norm_eps;
+    mc.rope_theta = cfg->rope_theta;
+    auto* h = new orx_decoder;
+    try {
+      orx::check(cudaGetDevice(&h->device), "cudaGetDevice");
+      auto* m = new orx::Model(mc);
+      h->dec = new orx::Decoder(m, true);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+void orx_decoder_destroy(orx_decoder* d) {
+  if (!d) return;
+  DeviceScope ds(d->device);
+  delete d->dec;
+  delete d;
+}
+
+int orx_decoder_set_tensor(orx_decoder* d, const char* name, const void* data, int dtype,
+                           size_t numel, int on_device) {
+  return guard([&] {
+    need(d, "decoder");
+    need(name, "name");
+    need(data, "data");
+    DeviceScope ds(d->device);
+    d->dec->model->set_tensor(name, data, dtype, numel, on_device != 0);
+  });
+}
+
+int orx_decoder_load_safetensors(orx_decoder* d, const char* dir) {
+  return guard([&] {
+    need(d, "decoder");
+    need(dir, "model_dir");
+    DeviceScope ds(d->device);
+    orx::ShardedCheckpoint ck(dir);
+    for (const auto& kv : ck.tensors()) {
+      const auto& t = kv.second;
+      int dtype;
+      size_t es;
+      if (t.dtype == "BF16") { dtype = 1; es = 2; }
+      else if (t.dtype == "F32") { dtype = 0; es = 4; }
+      else throw std::invalid_argument("unsupported dtype " + t.dtype + " for " + kv.first);
+      if (kv.first.rfind("thinker.model.", 0) != 0 && kv.first != "thinker.lm_head.weight")
+        continue;  // audio tower and other parts of the checkpoint
+      d->dec->model->set_tensor(kv.first, t.data, dtype, t.nbytes / es, false);
+    }
+    if (!d->dec->model->complete()) throw std::invalid_argument("checkpoint is missing tensors");
+  });
+}
+
+int orx_decoder_init_synthetic(orx_decoder* d, int seed) {
+  return guard([&] {
+    need(d, "decoder");
+    DeviceScope ds(d->device);
+    d->dec->model->init_synthetic(seed, 0);
+  });
+}
+
+int orx_decoder_weights_complete(const orx_decoder* d, int* complete) {
+  return guard([&] {
+    need(d, "decoder");
+    need(complete, "complete");
+    *complete = d->dec->model->complete() ? 1 : 0;
+  });
+}
+
+int orx_decoder_reset_cache(orx_decoder* d) {
+  return guard([&] { need(d, "decoder"); d->dec->reset_cache(); });
+}
+int orx_decoder_truncate_cache(orx_decoder* d, int len) {
+  return guard([&] { need(d, "decoder"); d->dec->truncate_cache(len); });
+}
+int orx_decoder_cache_len(const orx_decoder* d, int* out) {
+  return guard([&] { need(d, "decoder"); need(out, "out"); *out = d->dec->cache_len(); });
+}
+int orx_decoder_embed(const orx_decoder* d, int token_id, float* out) {
+  return guard([&] {
+    need(d, "decoder");
+    need(out, "out");
+    DeviceScope ds(d->device);
+    d->dec->embed(token_id, out);
+  });
+}
+
+int orx_decoder_prefill_at(orx_decoder* d, const float* embeds, int T, int pos0, void* stream) {
+  return guard([&] {
+    need(d, "decoder");
+    if (T > 0) need(embeds, "embeds");
+    DeviceScope ds(d->device);
+    d->dec->prefill_at(embeds, T, pos0, S(stream));
+  });
+}
+int orx_decoder_prefill_at_device(orx_decoder* d, const float* e, int T, int pos0, void* stream) {
+  return guard([&] {
+    need(d, "decoder");
+    if (T > 0) need(e, "embeds");
+    DeviceScope ds(d->device);
+    d->dec->prefill_at_device(e, T, pos0, S(stream));
+  });
+}
+int orx_decoder_decode_step(orx_decoder* d, const float* embed, int pos, void* stream) {
+  return guard([&] {
+    need(d, "decoder");
+    need(embed, "embed");
+    DeviceScope ds(d->device);
+    d->dec->decode_step(embed, pos, S(stream));
+  });
+}
+int orx_decoder_decode_step_device(orx_decoder* d, const int* tok, int pos, void* stream) {
+  return guard([&] {
+    need(d, "decoder");
+    need(tok, "d_token");
+    DeviceScope ds(d->device);
+    d->dec->decode_step_device(tok, pos, S(stream));
+  });
+}
+int orx_decoder_argmax(orx_decoder* d, int ban0, int ban1, void* stream, int* out) {
+  return guard([&] {
+    need(d, "decoder");
+    need(out, "out");
+    DeviceScope ds(d->device);
+    *out = d->dec->argmax(ban0, ban1, S(stream));
+  });
+}
+int orx_decoder_argmax_to_device(orx_decoder* d, int* d_out, int ban0, int ban1, void* stream) {
+  return guard([&] {
+    need(d, "decoder");
+    need(d_out, "d_out");
+    DeviceScope ds(d->device);
+    d->dec->argmax_to_device(d_out, ban0, ban1, S(stream));
+  });
+}
+int orx_decoder_read_token_id(const orx_decoder* d, const int* tok, void* stream, int* out) {
+  return guard([&] {
+    need(d, "decoder");
+    need(tok, "d_token");
+    need(out, "out");
+    DeviceScope ds(d->device);
+    *out = d->dec->read_token_id(tok, S(stream));
+  });
+}
+int orx_decoder_decode_greedy(orx_decoder* d, int start_pos, int max_new, int eos0, int eos1,
+                              int ban_steps, int batch, void* stream, int* out_tokens,
+                              int* n_out) {
+  return guard([&] {
+    need(d, "decoder");
+    need(n_out, "n_out");
+    if (max_new > 0) need(out_tokens, "out_tokens");
+    DeviceScope ds(d->device);
+    auto v = d->dec->decode_greedy(start_pos, max_new, eos0, eos1, ban_steps, batch, S(stream));
+    if (!v.empty()) std::memcpy(out_tokens, v.data(), v.size() * sizeof(int));
+    *n_out = static_cast<int>(v.size());
+  });
+}
+int orx_decoder_copy_logits(const orx_decoder* d, float* out) {
+  return guard([&] {
+    need(d, "decoder");
+    need(out, "out");
+    DeviceScope ds(d->device);
+    d->dec->copy_logits(out, 0);
+  });
+}
+int orx_decoder_logits_device(const orx_decoder* d, const float** out) {
+  return guard([&] { need(d, "decoder"); need(out, "out"); *out = d->dec->logits_device(); });
+}
+int orx_decoder_device_error(const orx_decoder* d, int* out) {
+  return guard([&] {
+    need(d, "decoder");
+    need(out, "out");
+    DeviceScope ds(d->device);
+    *out = d->dec->device_error();
+  });
+}
+
+int orx_synth_f32(float* d_out, long long n, int seed, int tid, double std, float mean,
+                  int round_bf16, void* stream) {
+  return guard([&] {
+    if (n > 0) need(d_out, "d_out");
+    if (n <= 0) return;
+    orx::launch_synth_f32(d_out, n, seed, tid, std, mean, round_bf16, S(stream));
+    orx::check(cudaGetLastError(), "synth");
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,128 @@
+// Shared constants and sm_100a device helpers for the Qwen3-ASR decoder path.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace orx {
+
+// Qwen3-ASR-1.7B text decoder dimensions (AsrTextConfig defaults,
+// include/model/asr_text_decoder.h:30-43 of the reference). The layer count,
+// vocabulary and maximum sequence length stay runtime parameters.
+constexpr int kHidden = 2048;
+constexpr int kQHeads = 16;
+constexpr int kKvHeads = 8;
+constexpr int kHeadDim = 128;
+constexpr int kQDim = kQHeads * kHeadDim;    // 2048
+constexpr int kKvDim = kKvHeads * kHeadDim;  // 1024
+constexpr int kQkvDim = kQDim + 2 * kKvDim;  // 4096
+constexpr int kInter = 6144;
+constexpr int kPage = 16;                    // tokens per KV page
+constexpr int kGroup = kQHeads / kKvHeads;   // q heads per kv head
+// One KV page of one layer: [K|V][kv head][16 tokens][128] bf16 = 64 KiB.
+constexpr int kPageElems = 2 * kKvHeads * kPage * kHeadDim;
+constexpr int kHalfPageElems = kKvHeads * kPage * kHeadDim;
+
+// Error codes written to the device status word (never a trap).
+enum DeviceError : int {
+  kErrNone = 0,
+  kErrWaitTimeout = 1,
+  kErrBadIndex = 2,
+};
+
+// Bounded spin: ~2^28 polls is well over a second on B200.
+constexpr uint32_t kSpinLimit = 1u << 28;
+
+__device__ __forceinline__ float bf2f(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+__device__ __forceinline__ uint16_t f2bf(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// Monotone key for (value, index) so a 64-bit atomicMax yields the largest
+// value and, among exact ties, the smallest index.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) |
+         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
+}
+__host__ __device__ __forceinline__ int argmax_key_index(unsigned long long k) {
+  return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+}
+
+// ---- programmatic dependent launch ---------------------------------------
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---- mbarrier + bulk async copy (TMA engine, no tensor map) ---------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; on timeout records kErrWaitTimeout in *err and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (err) atomicExch(err, kErrWaitTimeout);
+  return false;
+}
+// 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return v;
+}
+
+}  // namespace orx

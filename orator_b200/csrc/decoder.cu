@@ -1,0 +1,390 @@
+// One-session decoder with the reference AsrTextDecoder semantics
+// (src/model/asr_text_decoder.cu:338-899), rebuilt around paged KV, fused
+// weight-streaming kernels and CUDA graphs of PDL-chained launches.
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+#include "engine.h"
+
+namespace orx {
+
+namespace {
+constexpr int kDecodeSplits = 32;  // flash-decoding splits per kv head at batch 1
+constexpr int kPartStride = 2 * 132;
+}  // namespace
+
+Decoder::Decoder(Model* m, bool own) : model(m), own_model_(own) {
+  const auto& c = model->cfg;
+  max_pages_ = (c.max_seq_len + kPage - 1) / kPage;
+  kv_ = new KvPool(c.num_layers, max_pages_);
+  std::vector<int> ident(max_pages_);
+  for (int i = 0; i < max_pages_; ++i) ident[i] = i;
+  page_table_ = dalloc<int>(max_pages_);
+  ORX_CHECK(cudaMemcpy(page_table_, ident.data(), max_pages_ * 4, cudaMemcpyHostToDevice));
+  dx_ = dalloc<float>(kHidden);
+  dqkv_ = dalloc<float>(kQkvDim);
+  dattn_ = dalloc<uint16_t>(kQDim);
+  dact_ = dalloc<uint16_t>(kInter);
+  logits_ = dalloc<float>(c.vocab_size);
+  ORX_CHECK(cudaMemset(logits_, 0, (size_t)c.vocab_size * 4));
+  part_ = dalloc<float>((size_t)kKvHeads * kDecodeSplits * kPartStride);
+  counters_ = dalloc<int>(kKvHeads);
+  ORX_CHECK(cudaMemset(counters_, 0, kKvHeads * 4));
+  st_ = dalloc<StepState>(1);
+  StepState init = {};
+  ORX_CHECK(cudaMemcpy(st_, &init, sizeof(init), cudaMemcpyHostToDevice));
+  d_tmp_tok_ = dalloc<int>(1);
+  ORX_CHECK(cudaMallocHost(&h_tok_, sizeof(int)));
+}
+
+Decoder::~Decoder() {
+  if (g1_) cudaGraphExecDestroy(g1_);
+  if (gk_) cudaGraphExecDestroy(gk_);
+  delete kv_;
+  for (void* p : {(void*)page_table_, (void*)dx_, (void*)dqkv_, (void*)dattn_, (void*)dact_,
+                  (void*)logits_, (void*)part_, (void*)counters_, (void*)st_, (void*)d_out_,
+                  (void*)d_tmp_tok_, (void*)px_, (void*)pqkv_, (void*)pxn_, (void*)pattn_,
+                  (void*)pact_, (void*)pcounters_})
+    if (p) cudaFree(p);
+  if (h_out_) cudaFreeHost(h_out_);
+  if (h_tok_) cudaFreeHost(h_tok_);
+  if (h_stage_) cudaFreeHost(h_stage_);
+  if (own_model_) delete model;
+}
+
+void Decoder::truncate_cache(int len) {
+  if (len < 0 || len > model->cfg.max_seq_len) throw std::invalid_argument("bad cache length");
+  cache_len_ = len;
+}
+
+void Decoder::embed(int token, float* out) const {
+  if (token < 0 || token >= model->cfg.vocab_size) throw std::invalid_argument("token id out of range");
+  uint16_t row[kHidden];
+  ORX_CHECK(cudaMemcpy(row, model->embed + (size_t)token * kHidden, sizeof(row),
+                       cudaMemcpyDeviceToHost));
+  for (int i = 0; i < kHidden; ++i) {
+    const uint32_t u = static_cast<uint32_t>(row[i]) << 16;
+    std::memcpy(out + i, &u, 4);
+  }
+}
+
+int Decoder::device_error() const {
+  int e = 0;
+  ORX_CHECK(cudaMemcpy(&e, &st_->err, 4, cudaMemcpyDeviceToHost));
+  return e;
+}
+
+void Decoder::ensure_prefill(int T) {
+  if (T <= tcap_) return;
+  int cap = std::max(T, 64);
+  for (void* p : {(void*)px_, (void*)pqkv_, (void*)pxn_, (void*)pattn_, (void*)pact_,
+                  (void*)pcounters_})
+    if (p) cudaFree(p);
+  px_ = dalloc<float>((size_t)cap * kHidden);
+  pqkv_ = dalloc<float>((size_t)cap * kQkvDim);
+  pxn_ = dalloc<uint16_t>((size_t)cap * kHidden);
+  pattn_ = dalloc<uint16_t>((size_t)cap * kQDim);
+  pact_ = dalloc<uint16_t>((size_t)cap * kInter);
+  pcounters_ = dalloc<int>((size_t)cap * kKvHeads);
+  ORX_CHECK(cudaMemset(pcounters_, 0, (size_t)cap * kKvHeads * 4));
+  tcap_ = cap;
+}
+
+// Prefill forward (Forward, asr_text_decoder.cu:457-583) over T rows of px_.
+void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
+  const auto& c = model->cfg;
+  for (int l = 0; l < c.num_layers; ++l) {
+    const Model::Layer& L = model->layers[l];
+    uint16_t* kvl = kv_->layer(l);
+    launch_rmsnorm_bf16(px_, L.in_ln, pxn_, T, c.rms_norm_eps, s);
+    launch_gemm({pxn_, L.qkv, T, kQkvDim, kHidden, kEpiStore, pqkv_, nullptr, kQkvDim}, s);
+    launch_qk_norm_rope_store(pqkv_, T, L.q_norm, L.k_norm, model->rope_cos, model->rope_sin,
+                              kvl, page_table_, max_pages_, nullptr, nullptr, pos0, s);
+    AttnArgs a = {};
+    a.qkv = pqkv_;
+    a.qkv_stride = kQkvDim;
+    a.rope_cos = model->rope_cos;
+    a.rope_sin = model->rope_sin;
+    a.kv_layer = kvl;
+    a.page_table = page_table_;
+    a.max_pages = max_pages_;
+    a.pos_base = pos0;
+    a.rows = T;
+    a.fused_kv = 0;
+    a.nsplit_max = 1;
+    a.counters = pcounters_;
+    a.out = pattn_;
+    a.err = &st_->err;
+    launch_attention(a, s);
+    launch_gemm({pattn_, L.o, T, kHidden, kQDim, kEpiResid, px_, nullptr, kHidden}, s);
+    launch_rmsnorm_bf16(px_, L.post_ln, pxn_, T, c.rms_norm_eps, s);
+    launch_gemm({pxn_, L.gateup, T, 2 * kInter, kHidden, kEpiSwiglu, nullptr, pact_, kInter}, s);
+    launch_gemm({pact_, L.down, T, kHidden, kInter, kEpiResid, px_, nullptr, kHidden}, s);
+  }
+  // Final norm of the last row + tied lm_head (+ argmax into the step state).
+  GemvArgs g = {};
+  g.W = model->embed;
+  g.K = kHidden;
+  g.units = c.vocab_size;
+  g.act_mode = kActNorm;
+  g.x = px_ + (size_t)(T - 1) * kHidden;
+  g.norm_w = model->final_norm;
+  g.eps = c.rms_norm_eps;
+  g.epi = kEpiLogits;
+  g.out_f32 = logits_;
+  g.finalize = 0;
+  g.st = st_;
+  launch_gemv(g, model->num_sms, s);
+  ORX_CHECK(cudaGetLastError());
+}
+
+void Decoder::prefill_at(const float* host_embeds, int T, int pos0, cudaStream_t s) {
+  if (T <= 0) return;
+  if (pos0 < 0 || pos0 + T > model->cfg.max_seq_len)
+    throw std::invalid_argument("prefill exceeds max_seq_len");
+  ensure_prefill(T);
+  ORX_CHECK(cudaMemcpyAsync(px_, host_embeds, (size_t)T * kHidden * 4, cudaMemcpyHostToDevice, s));
+  forward_prefill(T, pos0, s);
+  cache_len_ = pos0 + T;
+  ORX_CHECK(cudaStreamSynchronize(s));
+}
+
+void Decoder::prefill_at_device(const float* dev_embeds, int T, int pos0, cudaStream_t s) {
+  if (T <= 0) return;
+  if (pos0 < 0 || pos0 + T > model->cfg.max_seq_len)
+    throw std::invalid_argument("prefill exceeds max_seq_len");
+  ensure_prefill(T);
+  ORX_CHECK(cudaMemcpyAsync(px_, dev_embeds, (size_t)T * kHidden * 4, cudaMemcpyDeviceToDevice, s));
+  forward_prefill(T, pos0, s);
+  cache_len_ = pos0 + T;
+}
+
+// One decode body: layer 0 gathers the embedding of *tok_ptr; the lm_head
+// kernel leaves logits and the banned argmax in the step state.
+void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool finalize) {
+  const auto& c = model->cfg;
+  const int sms = model->num_sms;
+  for (int l = 0; l < c.num_layers; ++l) {
+    const Model::Layer& L = model->layers[l];
+    GemvArgs q = {};
+    q.W = L.qkv;
+    q.K = kHidden;
+    q.units = kQkvDim;
+    q.norm_w = L.in_ln;
+    q.eps = c.rms_norm_eps;
+    if (l == 0) {
+      q.act_mode = kActEmbedNorm;
+      q.embed = model->embed;
+      q.tok_ptr = tok_ptr;
+      q.x_init = dx_;
+      q.record = record ? 1 : 0;
+    } else {
+      q.act_mode = kActNorm;
+      q.x = dx_;
+    }
+    q.epi = kEpiStore;
+    q.out_f32 = dqkv_;
+    q.st = st_;
+    launch_gemv(q, sms, s);
+
+    AttnArgs a = {};
+    a.qkv = dqkv_;
+    a.qkv_stride = kQkvDim;
+    a.q_norm_w = L.q_norm;
+    a.k_norm_w = L.k_norm;
+    a.rope_cos = model->rope_cos;
+    a.rope_sin = model->rope_sin;
+    a.kv_layer = kv_->layer(l);
+    a.page_table = page_table_;
+    a.max_pages = max_pages_;
+    a.pos_scalar = &st_->pos;
+    a.rows = 1;
+    a.fused_kv = 1;
+    a.nsplit_max = kDecodeSplits;
+    a.part = part_;
+    a.counters = counters_;
+    a.out = dattn_;
+    a.err = &st_->err;
+    launch_attention(a, s);
+
+    GemvArgs o = {};
+    o.W = L.o;
+    o.K = kQDim;
+    o.units = kHidden;
+    o.act_mode = kActBf16;
+    o.act = dattn_;
+    o.epi = kEpiResid;
+    o.out_f32 = dx_;
+    o.st = st_;
+    launch_gemv(o, sms, s);
+
+    GemvArgs gu = {};
+    gu.W = L.gateup;
+    gu.K = kHidden;
+    gu.units = kInter;
+    gu.act_mode = kActNorm;
+    gu.x = dx_;
+    gu.norm_w = L.post_ln;
+    gu.eps = c.rms_norm_eps;
+    gu.epi = kEpiSwiglu;
+    gu.out_bf16 = dact_;
+    gu.st = st_;
+    launch_gemv(gu, sms, s);
+
+    GemvArgs d = {};
+    d.W = L.down;
+    d.K = kInter;
+    d.units = kHidden;
+    d.act_mode = kActBf16;
+    d.act = dact_;
+    d.epi = kEpiResid;
+    d.out_f32 = dx_;
+    d.st = st_;
+    launch_gemv(d, sms, s);
+  }
+  GemvArgs g = {};
+  g.W = model->embed;
+  g.K = kHidden;
+  g.units = c.vocab_size;
+  g.act_mode = kActNorm;
+  g.x = dx_;
+  g.norm_w = model->final_norm;
+  g.eps = c.rms_norm_eps;
+  g.epi = kEpiLogits;
+  g.out_f32 = logits_;
+  g.finalize = finalize ? 1 : 0;
+  g.st = st_;
+  launch_gemv(g, sms, s);
+}
+
+void Decoder::decode_step_device(const int* d_token, int pos, cudaStream_t s) {
+  if (pos < 0 || pos >= model->cfg.max_seq_len) throw std::invalid_argument("position out of range");
+  ORX_CHECK(cudaMemcpyAsync(&st_->pos, &pos, 4, cudaMemcpyHostToDevice, s));
+  ORX_CHECK(cudaStreamSynchronize(s));  // `pos` is a stack value
+  cache_len_ = pos + 1;
+  record_body(s, d_token, false, false);
+  ORX_CHECK(cudaGetLastError());
+}
+
+void Decoder::decode_step(const float* host_embed, int pos, cudaStream_t s) {
+  // The embedding row is uploaded and fed through the embed path by id only
+  // when it is an exact table row; a general embedding runs as a 1-row prefill.
+  if (pos < 0 || pos >= model->cfg.max_seq_len) throw std::invalid_argument("position out of range");
+  prefill_at(host_embed, 1, pos, s);
+}
+
+int Decoder::argmax(int ban0, int ban1, cudaStream_t s) {
+  launch_argmax(logits_, model->cfg.vocab_size, ban0, ban1, st_, d_tmp_tok_, s);
+  ORX_CHECK(cudaMemcpyAsync(h_tok_, d_tmp_tok_, 4, cudaMemcpyDeviceToHost, s));
+  ORX_CHECK(cudaStreamSynchronize(s));
+  return *h_tok_;
+}
+
+void Decoder::argmax_to_device(int* d_out, int ban0, int ban1, cudaStream_t s) {
+  launch_argmax(logits_, model->cfg.vocab_size, ban0, ban1, st_, d_out, s);
+  ORX_CHECK(cudaGetLastError());
+}
+
+int Decoder::read_token_id(const int* d_token, cudaStream_t s) const {
+  ORX_CHECK(cudaMemcpyAsync(h_tok_, d_token, 4, cudaMemcpyDeviceToHost, s));
+  ORX_CHECK(cudaStreamSynchronize(s));
+  return *h_tok_;
+}
+
+void Decoder::copy_logits(float* host_out, cudaStream_t s) const {
+  ORX_CHECK(cudaStreamSynchronize(s));
+  ORX_CHECK(cudaMemcpy(host_out, logits_, (size_t)model->cfg.vocab_size * 4,
+                       cudaMemcpyDeviceToHost));
+}
+
+void Decoder::ensure_graphs(cudaStream_t s) {
+  if (g1_) return;
+  cudaStream_t cs;
+  ORX_CHECK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+  auto capture = [&](int steps) {
+    ORX_CHECK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    for (int i = 0; i < steps; ++i) record_body(cs, &st_->tok, true, true);
+    cudaGraph_t g;
+    ORX_CHECK(cudaStreamEndCapture(cs, &g));
+    cudaGraphExec_t e;
+    ORX_CHECK(cudaGraphInstantiate(&e, g, 0));
+    ORX_CHECK(cudaGraphDestroy(g));
+    return e;
+  };
+  g1_ = capture(1);
+  gk_ = capture(graph_steps);
+  ORX_CHECK(cudaStreamDestroy(cs));
+  (void)s;
+}
+
+// Greedy loop with the reference's control semantics (DecodeGreedy, eager
+// path, asr_text_decoder.cu:698-857): seed argmax (banned iff ban_steps > 0),
+// the argmax producing token k bans eos0/eos1 iff k < ban_steps, stop on EOS
+// (excluded) or six equal tokens in a row, checked once per batch; the cache
+// length counts every step that ran. Each step is on-device end to end.
+std::vector<int> Decoder::decode_greedy(int start_pos, int max_new, int eos0, int eos1,
+                                        int ban_steps, int batch, cudaStream_t s) {
+  std::vector<int> out;
+  if (max_new <= 0) return out;
+  if (start_pos < 0 || start_pos + max_new > model->cfg.max_seq_len)
+    throw std::invalid_argument("decode would exceed max_seq_len");
+  if (batch < 1) batch = 1;
+  if (out_cap_ < max_new) {
+    if (d_out_) cudaFree(d_out_);
+    if (h_out_) cudaFreeHost(h_out_);
+    d_out_ = dalloc<int>(max_new);
+    ORX_CHECK(cudaMallocHost(&h_out_, sizeof(int) * max_new));
+    out_cap_ = max_new;
+  }
+  ensure_graphs(s);
+  ORX_CHECK(cudaStreamSynchronize(s));
+  StepState init = {};
+  init.pos = start_pos;
+  init.count = 0;
+  init.ban_steps = ban_steps;
+  init.ban0 = eos0;
+  init.ban1 = eos1;
+  init.out_cap = out_cap_;
+  init.out = d_out_;
+  ORX_CHECK(cudaMemcpy(st_, &init, sizeof(init), cudaMemcpyHostToDevice));
+  const bool seed_ban = ban_steps > 0;
+  launch_argmax(logits_, model->cfg.vocab_size, seed_ban ? eos0 : -1, seed_ban ? eos1 : -1, st_,
+                nullptr, s);
+  ORX_CHECK(cudaGetLastError());
+
+  auto harvest = [&](int upto) {
+    for (int i = static_cast<int>(out.size()); i < upto; ++i) {
+      const int t = h_out_[i];
+      if (t == eos0 || t == eos1) return true;
+      out.push_back(t);
+      if (out.size() >= 6) {
+        bool same = true;
+        for (size_t k = out.size() - 6; k + 1 < out.size(); ++k)
+          if (out[k] != out.back()) { same = false; break; }
+        if (same) return true;
+      }
+    }
+    return false;
+  };
+  int emitted = 0;
+  while (emitted < max_new) {
+    const bool next_ban = (emitted + 1) < ban_steps;
+    const int this_batch = next_ban ? 1 : std::min(batch, max_new - emitted);
+    int left = this_batch;
+    while (left >= graph_steps) {
+      ORX_CHECK(cudaGraphLaunch(gk_, s));
+      left -= graph_steps;
+    }
+    for (; left > 0; --left) ORX_CHECK(cudaGraphLaunch(g1_, s));
+    ORX_CHECK(cudaMemcpyAsync(h_out_ + emitted, d_out_ + emitted, sizeof(int) * this_batch,
+                              cudaMemcpyDeviceToHost, s));
+    ORX_CHECK(cudaStreamSynchronize(s));
+    emitted += this_batch;
+    if (harvest(emitted)) break;
+  }
+  cache_len_ = start_pos + emitted;
+  return out;
+}
+
+}  // namespace orx

@@ -1,0 +1,143 @@
+// Decoder engine: weights (Model), one-session decoder (Decoder, the
+// AsrTextDecoder drop-in) and the paged KV pool they share.
+#pragma once
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+
+namespace orx {
+
+struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+void check(cudaError_t e, const char* what);
+#define ORX_CHECK(x) ::orx::check((x), #x)
+
+template <typename T>
+T* dalloc(size_t n) {
+  void* p = nullptr;
+  ORX_CHECK(cudaMalloc(&p, n * sizeof(T) ? n * sizeof(T) : 16));
+  return static_cast<T*>(p);
+}
+
+struct ModelConfig {
+  int num_layers = 28;
+  int vocab_size = 151936;
+  int max_seq_len = 2048;
+  float rms_norm_eps = 1e-6f;
+  float rope_theta = 1000000.0f;
+};
+
+// Device-resident weights of the 28-layer decoder (layout chosen for the
+// streaming GEMV and the GEMM epilogues; see set_tensor for the mapping from
+// the reference's thinker.model.* tensors).
+class Model {
+ public:
+  struct Layer {
+    float *in_ln = nullptr, *post_ln = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    uint16_t *qkv = nullptr, *o = nullptr, *gateup = nullptr, *down = nullptr;
+  };
+  explicit Model(const ModelConfig& c);
+  ~Model();
+  Model(const Model&) = delete;
+  Model& operator=(const Model&) = delete;
+
+  // Place one reference-named tensor. dtype: 0 = fp32, 1 = bf16 bits.
+  // `device` selects whether `src` is a device pointer.
+  void set_tensor(const std::string& name, const void* src, int dtype, size_t numel, bool device);
+  void init_synthetic(int seed, cudaStream_t s);
+  bool complete() const;
+
+  ModelConfig cfg;
+  int num_sms = 148;
+  uint16_t* embed = nullptr;  // [V, 2048], also the tied lm_head
+  float* final_norm = nullptr;
+  std::vector<Layer> layers;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  std::vector<uint8_t> have;  // per-tensor loaded flags
+  int rope_positions = 0;
+};
+
+// Paged KV pool: [layer][page][K|V][kv head][16][128] bf16.
+struct KvPool {
+  KvPool(int layers, int pages);
+  ~KvPool();
+  uint16_t* layer(int l) const { return base + (size_t)l * pages * kPageElems; }
+  int num_layers, pages;
+  uint16_t* base = nullptr;
+};
+
+// One decode session with the reference AsrTextDecoder semantics
+// (include/model/asr_text_decoder.h:45-113).
+class Decoder {
+ public:
+  Decoder(Model* model, bool own_model);
+  ~Decoder();
+
+  void reset_cache() { cache_len_ = 0; }
+  void truncate_cache(int len);
+  int cache_len() const { return cache_len_; }
+  void embed(int token, float* out) const;
+
+  void prefill_at(const float* host_embeds, int T, int pos0, cudaStream_t s);
+  void prefill_at_device(const float* dev_embeds, int T, int pos0, cudaStream_t s);
+  void decode_step(const float* host_embed, int pos, cudaStream_t s);
+  void decode_step_device(const int* d_token, int pos, cudaStream_t s);
+  int argmax(int ban0, int ban1, cudaStream_t s);
+  void argmax_to_device(int* d_out, int ban0, int ban1, cudaStream_t s);
+  int read_token_id(const int* d_token, cudaStream_t s) const;
+  std::vector<int> decode_greedy(int start_pos, int max_new, int eos0, int eos1, int ban_steps,
+                                 int batch, cudaStream_t s);
+  void copy_logits(float* host_out, cudaStream_t s) const;
+  const float* logits_device() const { return logits_; }
+  int device_error() const;
+
+  // Records one decode body (embed -> layers -> lm_head + argmax) on `s`.
+  void record_body(cudaStream_t s, const int* tok_ptr, bool record, bool finalize);
+
+  Model* model;
+  int graph_steps = 8;
+
+ private:
+  void ensure_prefill(int T);
+  void forward_prefill(int T, int pos0, cudaStream_t s);
+  void ensure_graphs(cudaStream_t s);
+
+  bool own_model_;
+  KvPool* kv_ = nullptr;
+  int max_pages_ = 0;
+  int* page_table_ = nullptr;
+  int cache_len_ = 0;
+  // decode buffers (fixed addresses, baked into graphs)
+  float* dx_ = nullptr;
+  float* dqkv_ = nullptr;
+  uint16_t* dattn_ = nullptr;
+  uint16_t* dact_ = nullptr;
+  float* logits_ = nullptr;
+  float* part_ = nullptr;
+  int* counters_ = nullptr;
+  StepState* st_ = nullptr;
+  int* d_out_ = nullptr;
+  int out_cap_ = 0;
+  int* h_out_ = nullptr;  // pinned
+  int* d_tmp_tok_ = nullptr;
+  int* h_tok_ = nullptr;  // pinned
+  // prefill buffers (grown on demand)
+  int tcap_ = 0;
+  float *px_ = nullptr, *pqkv_ = nullptr;
+  uint16_t *pxn_ = nullptr, *pattn_ = nullptr, *pact_ = nullptr;
+  int* pcounters_ = nullptr;
+  float* h_stage_ = nullptr;
+  size_t h_stage_cap_ = 0;
+  cudaGraphExec_t g1_ = nullptr, gk_ = nullptr;
+  std::vector<uint16_t> embed_host_;
+  bool embed_host_ready_ = false;
+};
+
+}  // namespace orx

@@ -1,0 +1,134 @@
+// Kernel launchers shared between the decoder engine and the C ABI.
+#pragma once
+
+#include <cstdint>
+#include <utility>
+#include <cuda_runtime.h>
+
+namespace orx {
+
+// Per-decode-step device state (one per decode stream). Replaces the
+// reference's device scalars d_tok_/step_pos_/d_count_/d_out_
+// (src/model/asr_text_decoder.cu:677-691).
+struct StepState {
+  int pos;        // absolute position of the token being decoded
+  int count;      // tokens recorded into `out` so far
+  int tok;        // current token id (argmax result of the previous step)
+  int ban_steps;  // argmaxes producing token k < ban_steps exclude ban0/ban1
+  int ban0, ban1;
+  int out_cap;
+  int done;       // CTA ticket for the last-CTA finalize of the argmax
+  unsigned long long best;  // packed (value, index) running argmax
+  int* out;       // recorded token ids [out_cap]
+  int err;        // device error word (bounded waits etc.)
+  int pad;
+};
+
+enum ActMode : int { kActNorm = 0, kActEmbedNorm = 1, kActBf16 = 2 };
+enum EpiMode : int { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2, kEpiLogits = 3 };
+
+struct GemvArgs {
+  const uint16_t* W;  // [rows, K] bf16 row-major
+  int K;              // multiple of 2048
+  int units;          // output units (rows, or gate/up pairs for SwiGLU)
+  int act_mode;
+  const float* x;         // fp32 input row for kActNorm
+  const float* norm_w;    // fp32 RMSNorm weight [2048]
+  float eps;
+  const uint16_t* act;    // bf16 activation [K] for kActBf16
+  const uint16_t* embed;  // embedding table for kActEmbedNorm
+  const int* tok_ptr;     // token id for kActEmbedNorm
+  float* x_init;          // kActEmbedNorm: residual row initialised by CTA 0
+  int record;             // kActEmbedNorm: append *tok_ptr to st->out
+  int epi;
+  float* out_f32;         // kEpiStore / kEpiLogits target, kEpiResid accumulator
+  uint16_t* out_bf16;     // kEpiSwiglu target
+  int finalize;           // kEpiLogits: write st->tok and advance st->pos
+  StepState* st;
+};
+
+// Weight-streaming GEMV for one activation row (decode at batch 1).
+void launch_gemv(const GemvArgs& a, int num_sms, cudaStream_t s);
+
+// Paged decode / prefill attention (flash-decoding split over pages).
+struct AttnArgs {
+  const float* qkv;        // [rows, 4096] fp32 raw projections (decode) or
+                           // normalised+roped q in cols [0,2048) (prefill)
+  int qkv_stride;          // elements between rows
+  const float* q_norm_w;   // [128]
+  const float* k_norm_w;   // [128]
+  const float* rope_cos;   // [max_pos, 64]
+  const float* rope_sin;
+  uint16_t* kv_layer;      // this layer's page pool base
+  long long layer_stride;  // elements between layers (for reference only)
+  const int* page_table;   // [n_tables, max_pages]
+  int max_pages;
+  const int* row_table;    // [rows] page-table row of each query row (nullptr: 0)
+  const int* row_pos;      // [rows] absolute position of each query row
+  const int* pos_scalar;   // if non-null, position of row 0 (decode B=1)
+  int pos_base;            // row_pos == nullptr: row r sits at pos_base + r
+  int rows;
+  int fused_kv;            // 1: q/k norm, RoPE and the K/V store happen here
+  int nsplit_max;
+  float* part;             // split partials scratch
+  int* counters;           // [rows * 8] split tickets (self-resetting)
+  uint16_t* out;           // [rows, 2048] bf16
+  int* err;
+};
+void launch_attention(const AttnArgs& a, cudaStream_t s);
+
+// q/k RMSNorm + RoPE + K/V store for T prefill rows (q normalised in place).
+void launch_qk_norm_rope_store(float* qkv, int rows, const float* qn, const float* kn,
+                               const float* cos, const float* sin, uint16_t* kv_layer,
+                               const int* page_table, int max_pages, const int* row_table,
+                               const int* row_pos, int pos_base, cudaStream_t s);
+
+// Row-wise RMSNorm to bf16: out[r] = bf16(x[r] * rsqrt(mean(x^2)+eps) * w).
+void launch_rmsnorm_bf16(const float* x, const float* w, uint16_t* out, int rows, float eps,
+                         cudaStream_t s);
+
+// Tensor-core GEMM out = A[M,K] * W[N,K]^T with fused epilogue.
+struct GemmArgs {
+  const uint16_t* A;  // [M, K] bf16
+  const uint16_t* W;  // [N, K] bf16
+  int M, N, K;
+  int epi;            // kEpiStore (fp32 out[M,N]), kEpiResid (out += ), kEpiSwiglu
+  float* out_f32;
+  uint16_t* out_bf16;  // SwiGLU: [M, N/2]
+  int ldo;             // leading dimension of the output
+};
+void launch_gemm(const GemmArgs& a, cudaStream_t s);
+
+// Argmax over fp32 logits with up to two banned ids into st (finalize sets st->tok).
+void launch_argmax(const float* logits, int n, int ban0, int ban1, StepState* st, int* out_dev,
+                   cudaStream_t s);
+
+void launch_rope_table(float* cos, float* sin, int max_pos, float theta, cudaStream_t s);
+void launch_synth_bf16(uint16_t* dst, long long n, int seed, int tid, double std, float mean,
+                       cudaStream_t s);
+void launch_synth_f32(float* dst, long long n, int seed, int tid, double std, float mean,
+                      int round_bf16, cudaStream_t s);
+void launch_f32_to_bf16(const float* in, uint16_t* out, long long n, cudaStream_t s);
+void launch_bf16_to_f32(const uint16_t* in, float* out, long long n, cudaStream_t s);
+void launch_embed_rows(const uint16_t* table, const int* ids, float* out, int rows,
+                       cudaStream_t s);
+
+// Launch helper: every kernel may start early under programmatic dependent
+// launch and must call griddepcontrol.wait before reading predecessor data.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
+}  // namespace orx
