@@ -99,6 +99,13 @@ int orx_decoder_logits_device(const orx_decoder* d, const float** out);
 /* Device error word written by bounded waits (0 = none). */
 int orx_decoder_device_error(const orx_decoder* d, int* out);
 
+/* Diagnostic (no reference counterpart): average device ms per launch of each
+ * decode kernel class, ms[6] = {qkv GEMV, attention, o GEMV, gate/up GEMV,
+ * down GEMV, lm_head GEMV}, each timed over `iters` back-to-back launches with
+ * CUDA events on `stream`. Clobbers the step buffers and the KV entry at the
+ * current position; call it only between requests. */
+int orx_decoder_profile_kernels(orx_decoder* d, int iters, void* stream, float* ms);
+
 /* Seeded synthetic fp32 data on the device, bit-exact with oracle/synth.py
  * (test and benchmark inputs; no reference counterpart). */
 int orx_synth_f32(float* d_out, long long n, int seed, int tensor_id, double std, float mean,

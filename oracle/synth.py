@@ -19,6 +19,8 @@ streams identical bit for bit.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 
 M64 = np.uint64(0xFFFFFFFFFFFFFFFF)
@@ -58,13 +60,14 @@ def hashes(seed: int, tid: int, start: int, n: int) -> np.ndarray:
 
 
 def normal_f32(seed: int, tid: int, n: int, std: float, mean: float = 0.0,
-               chunk: int = 1 << 24) -> np.ndarray:
+               chunk: int = 1 << 22) -> np.ndarray:
     """Approximately N(mean, std) fp32 values; bit-exact with the CUDA twin."""
     out = np.empty(n, dtype=np.float32)
     scale = np.float32(std / IH_SD)
     m = np.float32(mean)
     f16 = np.uint64(0xFFFF)
-    for s in range(0, n, chunk):
+
+    def fill(s):
         c = min(chunk, n - s)
         h = hashes(seed, tid, s, c)
         tot = ((h & f16) + ((h >> np.uint64(16)) & f16) + ((h >> np.uint64(32)) & f16)
@@ -73,6 +76,15 @@ def normal_f32(seed: int, tid: int, n: int, std: float, mean: float = 0.0,
         if mean != 0.0:
             v = v + m
         out[s:s + c] = v
+
+    starts = range(0, n, chunk)
+    if n > 4 * chunk:
+        from concurrent.futures import ThreadPoolExecutor
+        with ThreadPoolExecutor(max_workers=min(32, os.cpu_count() or 4)) as ex:
+            list(ex.map(fill, starts))
+    else:
+        for s in starts:
+            fill(s)
     return out
 
 

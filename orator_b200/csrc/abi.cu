@@ -271,6 +271,16 @@ int orx_decoder_device_error(const orx_decoder* d, int* out) {
   });
 }
 
+int orx_decoder_profile_kernels(orx_decoder* d, int iters, void* stream, float* ms) {
+  return guard([&] {
+    need(d, "decoder");
+    need(ms, "ms");
+    if (iters < 1) throw std::invalid_argument("iters must be >= 1");
+    DeviceScope ds(d->device);
+    d->dec->profile_kernels(iters, ms, S(stream));
+  });
+}
+
 int orx_synth_f32(float* d_out, long long n, int seed, int tid, double std, float mean,
                   int round_bf16, void* stream) {
   return guard([&] {

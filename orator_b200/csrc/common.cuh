@@ -31,8 +31,8 @@ enum DeviceError : int {
   kErrBadIndex = 2,
 };
 
-// Bounded spin: ~2^28 polls is well over a second on B200.
-constexpr uint32_t kSpinLimit = 1u << 28;
+// Bounded waits: give up after this many nanoseconds of the global timer.
+constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;
 
 __device__ __forceinline__ float bf2f(uint16_t b) {
   return __uint_as_float(static_cast<uint32_t>(b) << 16);
@@ -96,12 +96,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait; on timeout records kErrWaitTimeout in *err and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: returns false after kWaitLimitNs, or at once when another
+// wait already failed (*err != 0), recording `site` in *err. No trap.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          int site = kErrWaitTimeout) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-  if (err) atomicExch(err, kErrWaitTimeout);
-  return false;
+    if ((i & 255) == 0) {
+      if (err && *reinterpret_cast<volatile int*>(err) != 0) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        if (err) atomicExch(err, site);
+        return false;
+      }
+    }
+  }
 }
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
 // Both addresses 16-byte aligned, bytes a multiple of 16.

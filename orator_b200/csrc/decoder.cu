@@ -162,10 +162,12 @@ void Decoder::prefill_at_device(const float* dev_embeds, int T, int pos0, cudaSt
 
 // One decode body: layer 0 gathers the embedding of *tok_ptr; the lm_head
 // kernel leaves logits and the banned argmax in the step state.
-void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool finalize) {
+void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool finalize,
+                          int only) {
   const auto& c = model->cfg;
   const int sms = model->num_sms;
-  for (int l = 0; l < c.num_layers; ++l) {
+  auto on = [&](int k) { return only < 0 || only == k; };
+  for (int l = 0; l < (only < 0 ? c.num_layers : 1); ++l) {
     const Model::Layer& L = model->layers[l];
     GemvArgs q = {};
     q.W = L.qkv;
@@ -173,7 +175,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     q.units = kQkvDim;
     q.norm_w = L.in_ln;
     q.eps = c.rms_norm_eps;
-    if (l == 0) {
+    if (l == 0 && only < 0) {
       q.act_mode = kActEmbedNorm;
       q.embed = model->embed;
       q.tok_ptr = tok_ptr;
@@ -186,7 +188,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     q.epi = kEpiStore;
     q.out_f32 = dqkv_;
     q.st = st_;
-    launch_gemv(q, sms, s);
+    if (on(0)) launch_gemv(q, sms, s);
 
     AttnArgs a = {};
     a.qkv = dqkv_;
@@ -206,7 +208,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     a.counters = counters_;
     a.out = dattn_;
     a.err = &st_->err;
-    launch_attention(a, s);
+    if (on(1)) launch_attention(a, s);
 
     GemvArgs o = {};
     o.W = L.o;
@@ -217,7 +219,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     o.epi = kEpiResid;
     o.out_f32 = dx_;
     o.st = st_;
-    launch_gemv(o, sms, s);
+    if (on(2)) launch_gemv(o, sms, s);
 
     GemvArgs gu = {};
     gu.W = L.gateup;
@@ -230,7 +232,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     gu.epi = kEpiSwiglu;
     gu.out_bf16 = dact_;
     gu.st = st_;
-    launch_gemv(gu, sms, s);
+    if (on(3)) launch_gemv(gu, sms, s);
 
     GemvArgs d = {};
     d.W = L.down;
@@ -241,7 +243,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     d.epi = kEpiResid;
     d.out_f32 = dx_;
     d.st = st_;
-    launch_gemv(d, sms, s);
+    if (on(4)) launch_gemv(d, sms, s);
   }
   GemvArgs g = {};
   g.W = model->embed;
@@ -255,7 +257,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
   g.out_f32 = logits_;
   g.finalize = finalize ? 1 : 0;
   g.st = st_;
-  launch_gemv(g, sms, s);
+  if (on(5)) launch_gemv(g, sms, s);
 }
 
 void Decoder::decode_step_device(const int* d_token, int pos, cudaStream_t s) {
@@ -385,6 +387,31 @@ std::vector<int> Decoder::decode_greedy(int start_pos, int max_new, int eos0, in
   }
   cache_len_ = start_pos + emitted;
   return out;
+}
+
+// Average device time per launch of each decode kernel class (qkv GEMV,
+// attention, o GEMV, gate/up GEMV, down GEMV, lm_head GEMV), each launched
+// `iters` times back to back between CUDA events on `s`. Diagnostic only: it
+// overwrites the step buffers and the KV entry at the current position.
+void Decoder::profile_kernels(int iters, float* ms, cudaStream_t s) {
+  const int pos = cache_len_ > 0 ? cache_len_ - 1 : 0;
+  ORX_CHECK(cudaMemcpyAsync(&st_->pos, &pos, 4, cudaMemcpyHostToDevice, s));
+  ORX_CHECK(cudaStreamSynchronize(s));
+  cudaEvent_t e0, e1;
+  ORX_CHECK(cudaEventCreate(&e0));
+  ORX_CHECK(cudaEventCreate(&e1));
+  for (int k = 0; k < 6; ++k) {
+    record_body(s, &st_->tok, false, false, k);  // warm-up
+    ORX_CHECK(cudaEventRecord(e0, s));
+    for (int i = 0; i < iters; ++i) record_body(s, &st_->tok, false, false, k);
+    ORX_CHECK(cudaEventRecord(e1, s));
+    ORX_CHECK(cudaEventSynchronize(e1));
+    float t = 0.f;
+    ORX_CHECK(cudaEventElapsedTime(&t, e0, e1));
+    ms[k] = t / iters;
+  }
+  ORX_CHECK(cudaEventDestroy(e0));
+  ORX_CHECK(cudaEventDestroy(e1));
 }
 
 }  // namespace orx

@@ -99,7 +99,9 @@ class Decoder {
   int device_error() const;
 
   // Records one decode body (embed -> layers -> lm_head + argmax) on `s`.
-  void record_body(cudaStream_t s, const int* tok_ptr, bool record, bool finalize);
+  void record_body(cudaStream_t s, const int* tok_ptr, bool record, bool finalize,
+                   int only = -1);
+  void profile_kernels(int iters, float* ms, cudaStream_t s);
 
   Model* model;
   int graph_steps = 8;

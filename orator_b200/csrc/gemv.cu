@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(kThreadsGemv, 1) gemv_kernel(GemvArgs a) {
       bool ok = true;
       for (int g = 0; g < total && ok; ++g) {
         const int slot = g % kSlots;
-        if (g >= kSlots) ok = mbar_wait(&sm.empty[slot], ((g / kSlots) - 1) & 1, err);
+        if (g >= kSlots) ok = mbar_wait(&sm.empty[slot], ((g / kSlots) - 1) & 1, err, 11);
         if (!ok) break;
         const int lu = g / cpu, rem = g % cpu, r = rem / cpr, c = rem % cpr;
         const long long row = unit_row(a.epi, static_cast<int>(u0) + lu, r);
@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kThreadsGemv, 1) gemv_kernel(GemvArgs a) {
       }
       // Drain: do not exit while copies into this CTA's ring are in flight.
       for (int g = (total > kSlots ? total - kSlots : 0); g < total; ++g)
-        mbar_wait(&sm.full[g % kSlots], (g / kSlots) & 1, err);
+        mbar_wait(&sm.full[g % kSlots], (g / kSlots) & 1, err, 12);
     }
     return;
   }
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kThreadsGemv, 1) gemv_kernel(GemvArgs a) {
       for (int c = 0; c < cpr; ++c) {
         const int g = lu * cpu + r * cpr + c;
         const int slot = g % kSlots;
-        mbar_wait(&sm.full[slot], (g / kSlots) & 1, err);
+        mbar_wait(&sm.full[slot], (g / kSlots) & 1, err, 13);
         const uint4* wp = reinterpret_cast<const uint4*>(sm.ring[slot]);
         const uint4* xp = reinterpret_cast<const uint4*>(sm.xs + c * kChunk);
 #pragma unroll

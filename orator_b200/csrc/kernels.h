@@ -113,6 +113,9 @@ void launch_bf16_to_f32(const uint16_t* in, float* out, long long n, cudaStream_
 void launch_embed_rows(const uint16_t* table, const int* ids, float* out, int rows,
                        cudaStream_t s);
 
+// Programmatic dependent launch is on unless ORX_NO_PDL=1 is set.
+bool pdl_enabled();
+
 // Launch helper: every kernel may start early under programmatic dependent
 // launch and must call griddepcontrol.wait before reading predecessor data.
 template <typename... KArgs, typename... Args>
@@ -127,7 +130,7 @@ inline cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
 

@@ -1,4 +1,5 @@
 // Model weights on the device and their placement from reference tensors.
+#include <cstdlib>
 #include <cstring>
 #include <regex>
 
@@ -10,6 +11,14 @@ namespace orx {
 void check(cudaError_t e, const char* what) {
   if (e != cudaSuccess)
     throw CudaError(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("ORX_NO_PDL");
+    return !(v && v[0] == '1');
+  }();
+  return on;
 }
 
 namespace {

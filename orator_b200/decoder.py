@@ -179,6 +179,12 @@ class AsrTextDecoder:
         call("orx_decoder_logits_device", self._h, C.byref(p))
         return p.value
 
+    def profile_kernels(self, iters: int = 20, stream=None) -> dict:
+        ms = np.zeros(6, np.float32)
+        call("orx_decoder_profile_kernels", self._h, iters, _stream(stream),
+             ms.ctypes.data_as(C.c_void_p))
+        return dict(zip(["qkv", "attention", "o", "gateup", "down", "lm_head"], ms.tolist()))
+
     def device_error(self) -> int:
         v = C.c_int()
         call("orx_decoder_device_error", self._h, C.byref(v))
