@@ -19,6 +19,7 @@ namespace {
 
 constexpr int kAttnThreads = 128;
 constexpr int kPartStride = 2 * 132;  // per split: 2 heads x (128 acc, m, l, pad)
+constexpr int kMaxSplits = 64;       // nsplit_max limit (2 * kMaxSplits <= 128 threads)
 
 __device__ __forceinline__ float block_sum128(float v, float* red, int t) {
   v = warp_sum(v);
@@ -196,19 +197,33 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   __syncthreads();
   if (!sm_last) return;
   __threadfence();
+  // Combine the splits: per-split (m, l) staged in shared memory, then every
+  // thread sums its own output dimension over the splits (independent loads).
+  __shared__ float sw[2][kMaxSplits];
+  __shared__ float sl[2];
+  if (t < 2 * nsplit) {
+    const int k = t / nsplit, s2 = t % nsplit;
+    sw[k][s2] = __ldcg(a.part + (slot + s2) * kPartStride + k * 132 + 128);
+  }
+  __syncthreads();
+  if (t < 2) {
+    float mm = -INFINITY;
+    for (int s2 = 0; s2 < nsplit; ++s2) mm = fmaxf(mm, sw[t][s2]);
+    float ll = 0.f;
+    for (int s2 = 0; s2 < nsplit; ++s2) {
+      const float e = expf(sw[t][s2] - mm);
+      ll += __ldcg(a.part + (slot + s2) * kPartStride + t * 132 + 129) * e;
+      sw[t][s2] = e;
+    }
+    sl[t] = ll;
+  }
+  __syncthreads();
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
-    float mm = -INFINITY;
+    float aa = 0.f;
     for (int s2 = 0; s2 < nsplit; ++s2)
-      mm = fmaxf(mm, __ldcg(a.part + (slot + s2) * kPartStride + k * 132 + 128));
-    float ll = 0.f, aa = 0.f;
-    for (int s2 = 0; s2 < nsplit; ++s2) {
-      const float* ps = a.part + (slot + s2) * kPartStride + k * 132;
-      const float e = expf(__ldcg(ps + 128) - mm);
-      ll += __ldcg(ps + 129) * e;
-      aa += __ldcg(ps + t) * e;
-    }
-    orow[k * kHeadDim] = f2bf(aa * (1.0f / ll));
+      aa += __ldcg(a.part + (slot + s2) * kPartStride + k * 132 + t) * sw[k][s2];
+    orow[k * kHeadDim] = f2bf(aa * (1.0f / sl[k]));
   }
   if (t == 0) a.counters[row * kKvHeads + h] = 0;
 }
@@ -267,7 +282,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_store_kernel(
 }  // namespace
 
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
-  launch_pdl(attn_kernel, dim3(a.nsplit_max, kKvHeads, a.rows), dim3(kAttnThreads), 0, s, a);
+  launch_pdl(attn_kernel, dim3(a.nsplit_max < kMaxSplits ? a.nsplit_max : kMaxSplits, kKvHeads, a.rows),
+             dim3(kAttnThreads), 0, s, a);
 }
 
 void launch_qk_norm_rope_store(float* qkv, int rows, const float* qn, const float* kn,

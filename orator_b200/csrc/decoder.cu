@@ -10,7 +10,7 @@
 namespace orx {
 
 namespace {
-constexpr int kDecodeSplits = 32;  // flash-decoding splits per kv head at batch 1
+constexpr int kDecodeSplits = 8;  // flash-decoding splits per kv head at batch 1
 constexpr int kPartStride = 2 * 132;
 }  // namespace
 

@@ -5,16 +5,18 @@
 // src/model/asr_text_decoder.cu:404-438, src/model/asr_ops.cu:199-333) with a
 // single kernel per projection:
 //
-//  * one CTA per SM; a producer warp streams 4 KiB weight chunks (2048 bf16 of
-//    one row) with 1-D bulk async copies (TMA engine) into a 16-slot shared
-//    ring guarded by mbarriers;
-//  * the producer starts BEFORE griddepcontrol.wait: weights never depend on
-//    the previous kernel, so under programmatic dependent launch the next
-//    projection's weights are in flight while the previous kernel finishes;
-//  * 8 consumer warps build the bf16 activation in shared memory (fused RMSNorm
-//    or embedding gather + RMSNorm, with the reference's bf16 rounding point),
-//    then each warp reduces whole rows: fp32 FMA over bf16 operands, warp
-//    shuffle reduction;
+//  * one CTA per SM, 8 warps; every warp streams its own 4 KiB weight chunks
+//    (2048 bf16 of one row) with 1-D bulk async copies (TMA engine) into its
+//    own kDepth-slot shared ring guarded by mbarriers, so no warp waits on
+//    another's progress;
+//  * the first kDepth chunks of every warp are issued BEFORE
+//    griddepcontrol.wait: weights never depend on the previous kernel, so
+//    under programmatic dependent launch the next projection's weights are in
+//    flight while the previous kernel finishes;
+//  * the warps then build the bf16 activation in shared memory (fused RMSNorm
+//    or embedding gather + RMSNorm, with the reference's bf16 rounding point)
+//    and reduce whole rows: fp32 FMA over bf16 operands, warp shuffle
+//    reduction;
 //  * fused epilogues: fp32 store, residual add, SwiGLU + bf16 cast, or logits
 //    with a fused banned argmax (per-CTA best -> 64-bit atomicMax -> last CTA
 //    publishes the token and advances the position).
@@ -28,17 +30,17 @@ namespace {
 
 constexpr int kChunk = 2048;             // bf16 elements per ring slot
 constexpr int kChunkBytes = kChunk * 2;  // 4 KiB
-constexpr int kSlots = 16;
 constexpr int kConsumerWarps = 8;
+constexpr int kDepth = 3;  // chunks in flight per warp
+constexpr int kSlots = kConsumerWarps * kDepth;
 constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreadsGemv = kConsumers + 32;
+constexpr int kThreadsGemv = kConsumers;
 constexpr int kMaxK = kInter;  // 6144
 
 struct GemvSmem {
   alignas(128) uint8_t ring[kSlots][kChunkBytes];
   alignas(16) uint16_t xs[kMaxK];
   uint64_t full[kSlots];
-  uint64_t empty[kSlots];
   float red[kConsumerWarps];
   unsigned long long best[kConsumerWarps];
   int last;
@@ -55,7 +57,7 @@ __device__ __forceinline__ long long unit_row(int epi, int u, int r) {
   return u;
 }
 
-__global__ void __launch_bounds__(kThreadsGemv, 1) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kThreadsGemv, 2) gemv_kernel(GemvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   GemvSmem& sm = *reinterpret_cast<GemvSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -68,41 +70,30 @@ __global__ void __launch_bounds__(kThreadsGemv, 1) gemv_kernel(GemvArgs a) {
   const int rpu = (a.epi == kEpiSwiglu) ? 2 : 1;
   const int cpr = a.K / kChunk;
   const int cpu = rpu * cpr;
-  const int total = my_units * cpu;
   int* err = a.st ? &a.st->err : nullptr;
+  // This warp's chunk sequence: units warp, warp+8, ...; per unit its rows
+  // and K-chunks in order.
+  const int my_w_units = my_units > warp ? (my_units - warp + kConsumerWarps - 1) / kConsumerWarps : 0;
+  const int n_w = my_w_units * cpu;
+  uint64_t* full = &sm.full[warp * kDepth];
+  uint8_t(*ring)[kChunkBytes] = &sm.ring[warp * kDepth];
+  auto issue = [&](int j) {
+    const int lu = warp + (j / cpu) * kConsumerWarps, rem = j % cpu;
+    const int r = rem / cpr, c = rem % cpr;
+    const long long row = unit_row(a.epi, static_cast<int>(u0) + lu, r);
+    const int slot = j % kDepth;
+    mbar_arrive_expect_tx(&full[slot], kChunkBytes);
+    bulk_g2s(ring[slot], a.W + row * a.K + (long long)c * kChunk, kChunkBytes, &full[slot]);
+  };
 
-  if (tid == 0) {
-    for (int i = 0; i < kSlots; ++i) {
-      mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1);
-    }
+  if (lane == 0) {
+    for (int i = 0; i < kDepth; ++i) mbar_init(&full[i], 1);
     fence_mbar_init();
+    for (int j = 0; j < kDepth && j < n_w; ++j) issue(j);
   }
-  __syncthreads();
+  __syncwarp();
   pdl_trigger();
 
-  if (warp == kConsumerWarps) {
-    // ---------------- producer: stream weight chunks -----------------------
-    if (lane == 0) {
-      bool ok = true;
-      for (int g = 0; g < total && ok; ++g) {
-        const int slot = g % kSlots;
-        if (g >= kSlots) ok = mbar_wait(&sm.empty[slot], ((g / kSlots) - 1) & 1, err, 11);
-        if (!ok) break;
-        const int lu = g / cpu, rem = g % cpu, r = rem / cpr, c = rem % cpr;
-        const long long row = unit_row(a.epi, static_cast<int>(u0) + lu, r);
-        mbar_arrive_expect_tx(&sm.full[slot], kChunkBytes);
-        bulk_g2s(sm.ring[slot], a.W + row * a.K + (long long)c * kChunk, kChunkBytes,
-                 &sm.full[slot]);
-      }
-      // Drain: do not exit while copies into this CTA's ring are in flight.
-      for (int g = (total > kSlots ? total - kSlots : 0); g < total; ++g)
-        mbar_wait(&sm.full[g % kSlots], (g / kSlots) & 1, err, 12);
-    }
-    return;
-  }
-
-  // ---------------- consumers -------------------------------------------------
   pdl_wait();
   if (a.act_mode == kActBf16) {
     const uint4* src = reinterpret_cast<const uint4*>(a.act);
@@ -169,20 +160,30 @@ __global__ void __launch_bounds__(kThreadsGemv, 1) gemv_kernel(GemvArgs a) {
   }
   unsigned long long best = 0ull;
 
+  int jw = 0;  // chunks this warp has consumed
   for (int lu = warp; lu < my_units; lu += kConsumerWarps) {
     float accs[2] = {0.f, 0.f};
     for (int r = 0; r < rpu; ++r) {
-      float acc = 0.f;
+      float acc4[4] = {0.f, 0.f, 0.f, 0.f};
       for (int c = 0; c < cpr; ++c) {
-        const int g = lu * cpu + r * cpr + c;
-        const int slot = g % kSlots;
-        mbar_wait(&sm.full[slot], (g / kSlots) & 1, err, 13);
-        const uint4* wp = reinterpret_cast<const uint4*>(sm.ring[slot]);
+        const int slot = jw % kDepth;
+        mbar_wait(&full[slot], (jw / kDepth) & 1, err, 13);
+        const uint4* wp = reinterpret_cast<const uint4*>(ring[slot]);
         const uint4* xp = reinterpret_cast<const uint4*>(sm.xs + c * kChunk);
+        uint4 wv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wv[j] = wp[j * 32 + lane];
+        __syncwarp();
+        // the slot is free again: refill it with this warp's chunk jw + kDepth
+        if (lane == 0 && jw + kDepth < n_w) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue(jw + kDepth);
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const uint4 w = wp[j * 32 + lane];
+          const uint4 w = wv[j];
           const uint4 x = xp[j * 32 + lane];
+          float& acc = acc4[j & 3];
           acc = fmaf(bf_lo(w.x), bf_lo(x.x), acc);
           acc = fmaf(bf_hi(w.x), bf_hi(x.x), acc);
           acc = fmaf(bf_lo(w.y), bf_lo(x.y), acc);
@@ -192,9 +193,9 @@ __global__ void __launch_bounds__(kThreadsGemv, 1) gemv_kernel(GemvArgs a) {
           acc = fmaf(bf_lo(w.w), bf_lo(x.w), acc);
           acc = fmaf(bf_hi(w.w), bf_hi(x.w), acc);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        ++jw;
       }
+      const float acc = (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
       accs[r] = warp_sum(acc);
     }
     if (lane == 0) {
