@@ -17,138 +17,208 @@
 namespace orx {
 namespace {
 
-constexpr int kAttnThreads = 128;
-constexpr int kPartStride = 2 * 132;  // per split: 2 heads x (128 acc, m, l, pad)
-constexpr int kMaxSplits = 64;       // nsplit_max limit (2 * kMaxSplits <= 128 threads)
+constexpr int kAttnWarps = 8;          // one page per warp per group
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kPartStride = 2 * 132;   // per split: 2 heads x (128 acc, m, l, pad)
+constexpr int kMaxSplits = 128;        // 2 * kMaxSplits <= threads
+constexpr int kKRow = kHeadDim * 2 + 16;  // padded K row in shared memory (bytes)
+constexpr int kKTile = kPage * kKRow;     // 4352
+constexpr int kVTile = kPage * kHeadDim * 2;  // 4096
+constexpr int kGroupBytes = kAttnWarps * (kKTile + kVTile);
+constexpr int kAttnSmem = kGroupBytes + 128;
 
-__device__ __forceinline__ float block_sum128(float v, float* red, int t) {
-  v = warp_sum(v);
-  __syncthreads();
-  if ((t & 31) == 0) red[t >> 5] = v;
-  __syncthreads();
-  return red[0] + red[1] + red[2] + red[3];
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n cp.async.wait_all;" ::: "memory");
 }
 
-__global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
+// RMSNorm (eps 1e-6) + rotate-half RoPE of one 128-wide head held by a warp:
+// lane holds d = lane + 32*i, so the RoPE partner d +/- 64 is in the same lane.
+__device__ __forceinline__ void head_norm_rope(float v[4], const float* w, const float* cosT,
+                                               const float* sinT, int pos, int lane) {
+  const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+  const float inv = rsqrtf(ss / kHeadDim + 1e-6f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = v[i] * inv * w[lane + 32 * i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int j = lane + 32 * i;
+    const float c = cosT[pos * 64 + j], s = sinT[pos * 64 + j];
+    const float lo = v[i], hi = v[i + 2];
+    v[i] = lo * c - hi * s;
+    v[i + 2] = hi * c + lo * s;
+  }
+}
+
+// Stage pages [g0, g1) (at most kAttnWarps) of kv head h into shared memory.
+__device__ __forceinline__ void stage_pages(uint8_t* sm, const uint16_t* kv, const int* pt,
+                                            int h, int g0, int g1, int t) {
+  const int n = (g1 - g0) * 2 * kPage * 16;  // 16-byte pieces (K and V)
+  for (int i = t; i < n; i += kAttnThreads) {
+    const int pg = i / (2 * kPage * 16), rem = i % (2 * kPage * 16);
+    const int isv = rem / (kPage * 16), r = (rem / 16) % kPage, c = rem % 16;
+    const uint16_t* src = kv + (long long)pt[g0 + pg] * kPageElems + (isv ? kHalfPageElems : 0) +
+                          (h * kPage + r) * kHeadDim + c * 8;
+    uint8_t* base = sm + pg * (kKTile + kVTile);
+    const uint32_t dst = smem_u32(isv ? base + kKTile + r * kHeadDim * 2 + c * 16
+                                      : base + r * kKRow + c * 16);
+    cp_async16(dst, src);
+  }
+}
+
+// Flash-decoding over a paged cache. Grid (splits, kv heads, rows); split s
+// covers pages [s*P, (s+1)*P) of its row's page table (P = pages_per_split).
+// In decode mode (fused_kv) the first page group is prefetched BEFORE
+// griddepcontrol.wait using a speculative read of the position: cache entries
+// older than the current position never change, and the one page that may be
+// missing (when the position just crossed a page) is fetched after the wait.
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
+  extern __shared__ uint8_t attn_smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(attn_smem_raw) + 127) & ~uintptr_t(127));
   const int split = blockIdx.x, h = blockIdx.y, row = blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  pdl_trigger();
-  pdl_wait();
-  const int pos = a.pos_scalar ? *a.pos_scalar : (a.row_pos ? a.row_pos[row] : a.pos_base + row);
+  const int P = a.pages_per_split;
   const int tab = a.row_table ? a.row_table[row] : 0;
   const int* pt = a.page_table + (long long)tab * a.max_pages;
+  const int* pos_ptr = a.pos_scalar ? a.pos_scalar : (a.row_pos ? a.row_pos + row : nullptr);
+  const int pb = split * P;
+  int staged_end = pb;  // pages [pb, staged_end) already requested
+  if (a.fused_kv && pos_ptr) {
+    const int pos_g = *reinterpret_cast<const volatile int*>(pos_ptr);
+    int e = (pos_g + kPage) / kPage;
+    e = e < pb + P ? e : pb + P;
+    e = e < pb + kAttnWarps ? e : pb + kAttnWarps;
+    if (e > pb && e <= a.max_pages) {
+      stage_pages(sm, a.kv_layer, pt, h, pb, e, t);
+      staged_end = e;
+    }
+  }
+  pdl_trigger();
+  pdl_wait();
+  const int pos = pos_ptr ? *pos_ptr : a.pos_base + row;
   const int npages = (pos + kPage) / kPage;  // pages holding positions [0, pos]
-  const int nsplit = npages < a.nsplit_max ? npages : a.nsplit_max;
-  if (split >= nsplit) return;
-  const int p_begin = split * npages / nsplit;
-  const int p_end = (split + 1) * npages / nsplit;
+  const int nsplit = (npages + P - 1) / P;
+  if (split >= nsplit) {
+    cp_async_wait_all();
+    return;
+  }
+  const int pe = pb + P < npages ? pb + P : npages;
 
   __shared__ float qs[2][kHeadDim];
-  __shared__ float tmp[3][kHeadDim];
-  __shared__ float red[8];
-  __shared__ float sm_m[4][2], sm_l[4][2];
-  __shared__ float sm_acc[4][2][kHeadDim];
+  __shared__ float sm_m[kAttnWarps][2], sm_l[kAttnWarps][2];
+  __shared__ float sm_acc[kAttnWarps][2][kHeadDim];
   __shared__ int sm_last;
 
   const float* qrow = a.qkv + (long long)row * a.qkv_stride;
-  if (a.fused_kv) {
-    // q_norm / k_norm (RMSNorm over head_dim) then rotate-half RoPE.
-    const bool owner = (p_end == npages);  // this split holds position `pos`
-    float q0 = qrow[(2 * h) * kHeadDim + t];
-    float q1 = qrow[(2 * h + 1) * kHeadDim + t];
-    const float qw = a.q_norm_w[t];
-    float s0 = block_sum128(q0 * q0, red, t);
-    float s1 = block_sum128(q1 * q1, red + 4, t);
-    tmp[0][t] = q0 * rsqrtf(s0 / kHeadDim + 1e-6f) * qw;
-    tmp[1][t] = q1 * rsqrtf(s1 / kHeadDim + 1e-6f) * qw;
-    float kval = 0.f, vval = 0.f;
-    if (owner) {
-      kval = qrow[kQDim + h * kHeadDim + t];
-      vval = qrow[kQDim + kKvDim + h * kHeadDim + t];
-      const float sk = block_sum128(kval * kval, red, t);
-      tmp[2][t] = kval * rsqrtf(sk / kHeadDim + 1e-6f) * a.k_norm_w[t];
+  const bool owner = a.fused_kv && pe == npages;  // this split holds position `pos`
+  float knew[4], vnew[4];
+  if (warp < 2) {
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = qrow[(2 * h + warp) * kHeadDim + lane + 32 * i];
+    if (a.fused_kv) head_norm_rope(v, a.q_norm_w, a.rope_cos, a.rope_sin, pos, lane);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qs[warp][lane + 32 * i] = v[i];
+  } else if (warp == 2 && owner) {
+    // normalise, rotate and store K; store V (bf16, as the reference cache)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      knew[i] = qrow[kQDim + h * kHeadDim + lane + 32 * i];
+      vnew[i] = qrow[kQDim + kKvDim + h * kHeadDim + lane + 32 * i];
     }
-    __syncthreads();
-    const int j = t & 63;
-    const float c = a.rope_cos[pos * 64 + j], sn = a.rope_sin[pos * 64 + j];
-    auto rope = [&](const float* x) {
-      return t < 64 ? x[t] * c - x[t + 64] * sn : x[t] * c + x[t - 64] * sn;
-    };
-    qs[0][t] = rope(tmp[0]);
-    qs[1][t] = rope(tmp[1]);
-    if (owner) {
-      const float kr = rope(tmp[2]);
-      const int page = pt[pos / kPage];
-      uint16_t* base = a.kv_layer + (long long)page * kPageElems +
-                       (h * kPage + pos % kPage) * kHeadDim + t;
-      base[0] = f2bf(kr);
-      base[kHalfPageElems] = f2bf(vval);
+    head_norm_rope(knew, a.k_norm_w, a.rope_cos, a.rope_sin, pos, lane);
+    uint16_t* dst = a.kv_layer + (long long)pt[pos / kPage] * kPageElems +
+                    (h * kPage + pos % kPage) * kHeadDim;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      dst[lane + 32 * i] = f2bf(knew[i]);
+      dst[kHalfPageElems + lane + 32 * i] = f2bf(vnew[i]);
     }
-  } else {
-    qs[0][t] = qrow[(2 * h) * kHeadDim + t];
-    qs[1][t] = qrow[(2 * h + 1) * kHeadDim + t];
   }
-  __syncthreads();
 
   const float scale = 0.08838834764831845f;  // 1/sqrt(128) as float
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   const int r = lane & 15, hh = lane >> 4;
-  for (int p = p_begin + warp; p < p_end; p += 4) {
-    const int page = pt[p];
-    const uint16_t* K = a.kv_layer + (long long)page * kPageElems + h * kPage * kHeadDim;
-    const uint16_t* V = K + kHalfPageElems;
-    const uint4* krow = reinterpret_cast<const uint4*>(K + r * kHeadDim);
-    float dot = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint4 w = krow[i];
-      const float* q = &qs[hh][i * 8];
-      dot = fmaf(q[0], bf_lo(w.x), dot);
-      dot = fmaf(q[1], bf_hi(w.x), dot);
-      dot = fmaf(q[2], bf_lo(w.y), dot);
-      dot = fmaf(q[3], bf_hi(w.y), dot);
-      dot = fmaf(q[4], bf_lo(w.z), dot);
-      dot = fmaf(q[5], bf_hi(w.z), dot);
-      dot = fmaf(q[6], bf_lo(w.w), dot);
-      dot = fmaf(q[7], bf_hi(w.w), dot);
+  for (int g0 = pb; g0 < pe; g0 += kAttnWarps) {
+    const int g1 = g0 + kAttnWarps < pe ? g0 + kAttnWarps : pe;
+    if (g0 != pb) __syncthreads();  // previous group fully consumed
+    if (g0 != pb || staged_end < g1) {
+      const int from = (g0 == pb) ? staged_end : g0;
+      stage_pages(sm + (from - g0) * (kKTile + kVTile), a.kv_layer, pt, h, from, g1, t);
     }
-    const bool valid = p * kPage + r <= pos;
-    const float s = valid ? dot * scale : -INFINITY;
-    float mx = s;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float mx_other = __shfl_xor_sync(0xffffffffu, mx, 16);
-    const float mxh[2] = {hh ? mx_other : mx, hh ? mx : mx_other};
-    float mnew[2], corr[2];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      mnew[k] = fmaxf(m[k], mxh[k]);
-      corr[k] = expf(m[k] - mnew[k]);
-    }
-    const float pl = valid ? expf(s - mnew[hh]) : 0.f;
-    float ps = pl;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-    const float ps_other = __shfl_xor_sync(0xffffffffu, ps, 16);
-    const float psh[2] = {hh ? ps_other : ps, hh ? ps : ps_other};
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      l[k] = l[k] * corr[k] + psh[k];
-      m[k] = mnew[k];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[k][i] *= corr[k];
-    }
-#pragma unroll 4
-    for (int r2 = 0; r2 < kPage; ++r2) {
-      const uint2 vv = reinterpret_cast<const uint2*>(V + r2 * kHeadDim)[lane];
-      const float p0 = __shfl_sync(0xffffffffu, pl, r2);
-      const float p1 = __shfl_sync(0xffffffffu, pl, 16 + r2);
-      const float v4[4] = {bf_lo(vv.x), bf_hi(vv.x), bf_lo(vv.y), bf_hi(vv.y)};
+    cp_async_wait_all();
+    __syncthreads();  // every thread's copies of this group have landed
+    if (owner && warp == 2 && g1 == pe) {
+      // the staged copy of the newest slot may predate this step: patch it
+      uint8_t* base = sm + (pos / kPage - g0) * (kKTile + kVTile);
+      uint16_t* kd = reinterpret_cast<uint16_t*>(base + (pos % kPage) * kKRow);
+      uint16_t* vd = reinterpret_cast<uint16_t*>(base + kKTile + (pos % kPage) * kHeadDim * 2);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        acc[0][i] = fmaf(p0, v4[i], acc[0][i]);
-        acc[1][i] = fmaf(p1, v4[i], acc[1][i]);
+        kd[lane + 32 * i] = f2bf(knew[i]);
+        vd[lane + 32 * i] = f2bf(vnew[i]);
+      }
+    }
+    __syncthreads();
+    const int p = g0 + warp;
+    if (p < g1) {
+      const uint8_t* base = sm + warp * (kKTile + kVTile);
+      const uint4* krow = reinterpret_cast<const uint4*>(base + r * kKRow);
+      const uint16_t* V = reinterpret_cast<const uint16_t*>(base + kKTile);
+      float d4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint4 w = krow[i];
+        const float* q = &qs[hh][i * 8];
+        float& dot = d4[i & 3];
+        dot = fmaf(q[0], bf_lo(w.x), dot);
+        dot = fmaf(q[1], bf_hi(w.x), dot);
+        dot = fmaf(q[2], bf_lo(w.y), dot);
+        dot = fmaf(q[3], bf_hi(w.y), dot);
+        dot = fmaf(q[4], bf_lo(w.z), dot);
+        dot = fmaf(q[5], bf_hi(w.z), dot);
+        dot = fmaf(q[6], bf_lo(w.w), dot);
+        dot = fmaf(q[7], bf_hi(w.w), dot);
+      }
+      const float dot = (d4[0] + d4[1]) + (d4[2] + d4[3]);
+      const bool valid = p * kPage + r <= pos;
+      const float s = valid ? dot * scale : -INFINITY;
+      float mx = s;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mx_other = __shfl_xor_sync(0xffffffffu, mx, 16);
+      const float mx0 = hh ? mx_other : mx, mx1 = hh ? mx : mx_other;
+      const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
+      const float c0 = expf(m[0] - mn0), c1 = expf(m[1] - mn1);
+      const float pl = valid ? expf(s - (hh ? mn1 : mn0)) : 0.f;
+      float ps = pl;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      const float ps_other = __shfl_xor_sync(0xffffffffu, ps, 16);
+      l[0] = l[0] * c0 + (hh ? ps_other : ps);
+      l[1] = l[1] * c1 + (hh ? ps : ps_other);
+      m[0] = mn0;
+      m[1] = mn1;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[0][i] *= c0;
+        acc[1][i] *= c1;
+      }
+#pragma unroll
+      for (int r2 = 0; r2 < kPage; ++r2) {
+        const uint2 vv = reinterpret_cast<const uint2*>(V + r2 * kHeadDim)[lane];
+        const float p0 = __shfl_sync(0xffffffffu, pl, r2);
+        const float p1 = __shfl_sync(0xffffffffu, pl, 16 + r2);
+        const float v4[4] = {bf_lo(vv.x), bf_hi(vv.x), bf_lo(vv.y), bf_hi(vv.y)};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[0][i] = fmaf(p0, v4[i], acc[0][i]);
+          acc[1][i] = fmaf(p1, v4[i], acc[1][i]);
+        }
       }
     }
   }
@@ -161,32 +231,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) sm_acc[warp][k][lane * 4 + i] = acc[k][i];
   __syncthreads();
-
-  float A[2], M[2], L[2];
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    float mm = -INFINITY;
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, sm_m[w][k]);
-    float ll = 0.f, aa = 0.f;
-    for (int w = 0; w < 4; ++w) {
-      const float e = sm_l[w][k] > 0.f ? expf(sm_m[w][k] - mm) : 0.f;
-      ll += sm_l[w][k] * e;
-      aa += sm_acc[w][k][t] * e;
+  const bool own = t < 2 * kHeadDim;  // threads 0..255 own (head kk, dim d)
+  const int kk = (t >> 7) & 1, d = t & 127;
+  float mm = -INFINITY, ll = 0.f, aa = 0.f;
+  if (own) {
+    for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, sm_m[w][kk]);
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float e = sm_l[w][kk] > 0.f ? expf(sm_m[w][kk] - mm) : 0.f;
+      ll += sm_l[w][kk] * e;
+      aa += sm_acc[w][kk][d] * e;
     }
-    A[k] = aa; M[k] = mm; L[k] = ll;
   }
-  uint16_t* orow = a.out + (long long)row * kQDim + (2 * h) * kHeadDim + t;
+  uint16_t* orow = a.out + (long long)row * kQDim + (2 * h + kk) * kHeadDim + d;
   if (nsplit == 1) {
-    orow[0] = f2bf(A[0] * (1.0f / L[0]));
-    orow[kHeadDim] = f2bf(A[1] * (1.0f / L[1]));
+    if (own) *orow = f2bf(aa * (1.0f / ll));
     return;
   }
   const long long slot = ((long long)row * kKvHeads + h) * a.nsplit_max;
-  float* part = a.part + (slot + split) * kPartStride;
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    part[k * 132 + t] = A[k];
-    if (t == 0) { part[k * 132 + 128] = M[k]; part[k * 132 + 129] = L[k]; }
+  if (own) {
+    float* part = a.part + (slot + split) * kPartStride + kk * 132;
+    part[d] = aa;
+    if (d == 0) { part[128] = mm; part[129] = ll; }
   }
   __threadfence();
   __syncthreads();
@@ -198,7 +263,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   if (!sm_last) return;
   __threadfence();
   // Combine the splits: per-split (m, l) staged in shared memory, then every
-  // thread sums its own output dimension over the splits (independent loads).
+  // owning thread sums its output dimension over the splits.
   __shared__ float sw[2][kMaxSplits];
   __shared__ float sl[2];
   if (t < 2 * nsplit) {
@@ -207,23 +272,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   }
   __syncthreads();
   if (t < 2) {
-    float mm = -INFINITY;
-    for (int s2 = 0; s2 < nsplit; ++s2) mm = fmaxf(mm, sw[t][s2]);
-    float ll = 0.f;
+    float m2 = -INFINITY;
+    for (int s2 = 0; s2 < nsplit; ++s2) m2 = fmaxf(m2, sw[t][s2]);
+    float l2 = 0.f;
     for (int s2 = 0; s2 < nsplit; ++s2) {
-      const float e = expf(sw[t][s2] - mm);
-      ll += __ldcg(a.part + (slot + s2) * kPartStride + t * 132 + 129) * e;
+      const float e = expf(sw[t][s2] - m2);
+      l2 += __ldcg(a.part + (slot + s2) * kPartStride + t * 132 + 129) * e;
       sw[t][s2] = e;
     }
-    sl[t] = ll;
+    sl[t] = l2;
   }
   __syncthreads();
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    float aa = 0.f;
+  if (own) {
+    float a2 = 0.f;
     for (int s2 = 0; s2 < nsplit; ++s2)
-      aa += __ldcg(a.part + (slot + s2) * kPartStride + k * 132 + t) * sw[k][s2];
-    orow[k * kHeadDim] = f2bf(aa * (1.0f / sl[k]));
+      a2 += __ldcg(a.part + (slot + s2) * kPartStride + kk * 132 + d) * sw[kk][s2];
+    *orow = f2bf(a2 * (1.0f / sl[kk]));
   }
   if (t == 0) a.counters[row * kKvHeads + h] = 0;
 }
@@ -282,8 +346,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_store_kernel(
 }  // namespace
 
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+    configured = true;
+  }
   launch_pdl(attn_kernel, dim3(a.nsplit_max < kMaxSplits ? a.nsplit_max : kMaxSplits, kKvHeads, a.rows),
-             dim3(kAttnThreads), 0, s, a);
+             dim3(kAttnThreads), kAttnSmem, s, a);
 }
 
 void launch_qk_norm_rope_store(float* qkv, int rows, const float* qn, const float* kn,

@@ -43,6 +43,17 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// acc += lo(a)*lo(b) + hi(a)*hi(b) for packed bf16 pairs, with the mixed
+// precision FMA (bf16 operands, fp32 accumulate; each product exact in fp32,
+// one rounding per FMA, the same arithmetic as fmaf on upcast operands).
+__device__ __forceinline__ float fma2_bf16(uint32_t a, uint32_t b, float acc) {
+  asm("{\n .reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %1;\n mov.b32 {bl, bh}, %2;\n"
+      " fma.rn.f32.bf16 %0, al, bl, %0;\n fma.rn.f32.bf16 %0, ah, bh, %0;\n}"
+      : "+f"(acc)
+      : "r"(a), "r"(b));
+  return acc;
+}
+
 // Monotone key for (value, index) so a 64-bit atomicMax yields the largest
 // value and, among exact ties, the smallest index.
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {

@@ -10,7 +10,7 @@
 namespace orx {
 
 namespace {
-constexpr int kDecodeSplits = 8;  // flash-decoding splits per kv head at batch 1
+constexpr int kDecodePagesPerSplit = 8;  // flash-decoding split size at batch 1
 constexpr int kPartStride = 2 * 132;
 }  // namespace
 
@@ -28,7 +28,7 @@ Decoder::Decoder(Model* m, bool own) : model(m), own_model_(own) {
   dact_ = dalloc<uint16_t>(kInter);
   logits_ = dalloc<float>(c.vocab_size);
   ORX_CHECK(cudaMemset(logits_, 0, (size_t)c.vocab_size * 4));
-  part_ = dalloc<float>((size_t)kKvHeads * kDecodeSplits * kPartStride);
+  part_ = dalloc<float>((size_t)kKvHeads * ((max_pages_ + kDecodePagesPerSplit - 1) / kDecodePagesPerSplit) * kPartStride);
   counters_ = dalloc<int>(kKvHeads);
   ORX_CHECK(cudaMemset(counters_, 0, kKvHeads * 4));
   st_ = dalloc<StepState>(1);
@@ -113,6 +113,7 @@ void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
     a.rows = T;
     a.fused_kv = 0;
     a.nsplit_max = 1;
+    a.pages_per_split = max_pages_;
     a.counters = pcounters_;
     a.out = pattn_;
     a.err = &st_->err;
@@ -203,7 +204,8 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     a.pos_scalar = &st_->pos;
     a.rows = 1;
     a.fused_kv = 1;
-    a.nsplit_max = kDecodeSplits;
+    a.nsplit_max = (max_pages_ + kDecodePagesPerSplit - 1) / kDecodePagesPerSplit;
+    a.pages_per_split = kDecodePagesPerSplit;
     a.part = part_;
     a.counters = counters_;
     a.out = dattn_;

@@ -184,14 +184,10 @@ __global__ void __launch_bounds__(kThreadsGemv, 2) gemv_kernel(GemvArgs a) {
           const uint4 w = wv[j];
           const uint4 x = xp[j * 32 + lane];
           float& acc = acc4[j & 3];
-          acc = fmaf(bf_lo(w.x), bf_lo(x.x), acc);
-          acc = fmaf(bf_hi(w.x), bf_hi(x.x), acc);
-          acc = fmaf(bf_lo(w.y), bf_lo(x.y), acc);
-          acc = fmaf(bf_hi(w.y), bf_hi(x.y), acc);
-          acc = fmaf(bf_lo(w.z), bf_lo(x.z), acc);
-          acc = fmaf(bf_hi(w.z), bf_hi(x.z), acc);
-          acc = fmaf(bf_lo(w.w), bf_lo(x.w), acc);
-          acc = fmaf(bf_hi(w.w), bf_hi(x.w), acc);
+          acc = fma2_bf16(w.x, x.x, acc);
+          acc = fma2_bf16(w.y, x.y, acc);
+          acc = fma2_bf16(w.z, x.z, acc);
+          acc = fma2_bf16(w.w, x.w, acc);
         }
         ++jw;
       }

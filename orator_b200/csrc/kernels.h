@@ -69,7 +69,8 @@ struct AttnArgs {
   int pos_base;            // row_pos == nullptr: row r sits at pos_base + r
   int rows;
   int fused_kv;            // 1: q/k norm, RoPE and the K/V store happen here
-  int nsplit_max;
+  int nsplit_max;           // grid splits; >= ceil(pages / pages_per_split)
+  int pages_per_split;
   float* part;             // split partials scratch
   int* counters;           // [rows * 8] split tickets (self-resetting)
   uint16_t* out;           // [rows, 2048] bf16

@@ -1,0 +1,49 @@
+"""ctypes access to the reference decoder built by oracle/build_ref.sh
+(oracle/_ref/libref_asr.so). Test infrastructure: a checker, never the product."""
+import ctypes as C
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(ROOT, "oracle", "_ref", "libref_asr.so")
+
+
+def available() -> bool:
+    return os.path.exists(LIB)
+
+
+class RefDecoder:
+    def __init__(self, model_dir: str, num_layers: int, vocab: int, max_seq: int = 2048):
+        L = C.CDLL(LIB)
+        L.ref_create.restype = C.c_void_p
+        L.ref_create.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int]
+        L.ref_last_error.restype = C.c_char_p
+        for f in ["ref_prefill_at", "ref_copy_logits", "ref_decode_step_token", "ref_argmax",
+                  "ref_destroy", "ref_truncate", "ref_cache_len", "ref_decode_greedy"]:
+            getattr(L, f).argtypes = None
+        self.L, self.vocab = L, vocab
+        h = L.ref_create(model_dir.encode(), num_layers, vocab, max_seq)
+        if not h:
+            raise RuntimeError(L.ref_last_error().decode())
+        self.h = C.c_void_p(h)
+
+    def prefill_at(self, x, pos0):
+        x = np.ascontiguousarray(x, np.float32)
+        assert self.L.ref_prefill_at(self.h, x.ctypes.data_as(C.c_void_p), C.c_int(x.shape[0]),
+                                     C.c_int(pos0)) == 0
+        return self.logits()
+
+    def logits(self):
+        out = np.empty(self.vocab, np.float32)
+        assert self.L.ref_copy_logits(self.h, out.ctypes.data_as(C.c_void_p)) == 0
+        return out
+
+    def decode_step(self, tok, pos):
+        assert self.L.ref_decode_step_token(self.h, C.c_int(tok), C.c_int(pos)) == 0
+        return self.logits()
+
+    def close(self):
+        if self.h:
+            self.L.ref_destroy(self.h)
+            self.h = None

@@ -1,0 +1,89 @@
+"""Side-by-side parity with the reference decoder itself (oracle/_ref build of
+src/model/asr_text_decoder.cu and friends) on identical seeded weights and
+inputs: ours, the reference and the CPU oracle.
+
+The reference's own deviation from the oracle sets the scale: ours must stay
+within 1.25x of it (+2e-3), and greedy argmax must match the reference wherever
+the reference's top-2 margin is at least 2e-2.
+"""
+import numpy as np
+import pytest
+
+import refharness
+from oracle import decoder_oracle as D
+from oracle import st_writer, synth
+
+pytestmark = pytest.mark.gpu
+
+LAYERS, SEED, VOCAB = 2, 1, 151936
+
+
+@pytest.fixture(scope="module")
+def trio(cuda, tmp_path_factory):
+    if not refharness.available():
+        pytest.skip("reference build oracle/_ref/libref_asr.so not present")
+    from orator_b200 import AsrTextConfig, AsrTextDecoder
+    d = str(tmp_path_factory.mktemp("ref_model"))
+    st_writer.write_synthetic_model(d, SEED, LAYERS, VOCAB)
+    ref = refharness.RefDecoder(d, LAYERS, VOCAB, 512)
+    ours = AsrTextDecoder(AsrTextConfig(num_layers=LAYERS, vocab_size=VOCAB, max_seq_len=512))
+    ours.load_weights(d)  # the same checkpoint files through the safetensors loader
+    cfg = D.Config(num_layers=LAYERS, vocab_size=VOCAB, max_seq_len=512)
+    orc = D.OracleDecoder.synthetic(cfg, SEED)
+    yield ours, ref, orc
+    ours.close()
+    ref.close()
+
+
+def margin(lg):
+    t = np.partition(lg, -2)[-2:]
+    return float(t[1] - t[0])
+
+
+def dev(a, b):
+    return float(np.abs(a - b).max())
+
+
+def test_prefill_and_decode_vs_reference(trio):
+    import torch
+    ours, ref, orc = trio
+    x = synth.audio_rows(SEED, 36, 2048)
+    lo = orc.prefill_at(x, 0)
+    lr = ref.prefill_at(x, 0)
+    ours.ResetCache()
+    ours.Prefill(x)
+    lg = ours.CopyLogits()
+    assert dev(lg, lo) <= 1.25 * dev(lr, lo) + 2e-3, (dev(lg, lo), dev(lr, lo))
+    if margin(lr) >= 2e-2:
+        assert int(np.argmax(lg)) == int(np.argmax(lr))
+    d_tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    tok = int(np.argmax(lr))
+    worst_ours = worst_ref = 0.0
+    for s in range(20):  # crosses the position-48 page boundary
+        pos = 36 + s
+        a = orc.decode_step(tok, pos)
+        b = ref.decode_step(tok, pos)
+        d_tok.fill_(tok)
+        torch.cuda.synchronize()
+        ours.DecodeStepDevice(d_tok.data_ptr(), pos)
+        c = ours.CopyLogits()
+        worst_ours = max(worst_ours, dev(c, a))
+        worst_ref = max(worst_ref, dev(b, a))
+        if margin(b) >= 2e-2:
+            assert int(np.argmax(c)) == int(np.argmax(b)), s
+        tok = int(np.argmax(b))
+    assert worst_ours <= 1.25 * worst_ref + 2e-3, (worst_ours, worst_ref)
+
+
+def test_loader_matches_synthetic_init(trio, cuda):
+    """load_weights(safetensors dir) and init_synthetic(seed) give the same model."""
+    from orator_b200 import AsrTextConfig, AsrTextDecoder
+    ours, _, _ = trio
+    other = AsrTextDecoder(AsrTextConfig(num_layers=LAYERS, vocab_size=VOCAB, max_seq_len=512))
+    other.init_synthetic(SEED)
+    x = synth.audio_rows(SEED, 8, 2048)
+    ours.ResetCache()
+    ours.Prefill(x)
+    other.Prefill(x)
+    assert np.array_equal(ours.CopyLogits(), other.CopyLogits())
+    other.close()
