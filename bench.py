@@ -31,7 +31,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-PROMPT_ROWS, AUDIO_ROWS, NEW_TOKENS, SEED = 400, 375, 128, 1
+PROMPT_ROWS, AUDIO_ROWS, SEED = 400, 375, 1
+NEW_TOKENS = 128
 HIDDEN, LAYERS, VOCAB = 2048, 28, 151936
 # bytes streamed per decode token: bf16 matrices (incl. tied lm_head) + fp32 norms
 WEIGHT_BYTES = 3_440_902_144 + 495_616
@@ -280,7 +281,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-sample", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=128,
+                    help="decode tokens per step (128 = config 2; smaller only for profiler runs)")
     args = ap.parse_args()
+    global NEW_TOKENS
+    NEW_TOKENS = args.tokens
     if args.impl == "reference":
         run_reference(args)
     else:
