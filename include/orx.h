@@ -106,6 +106,24 @@ int orx_decoder_device_error(const orx_decoder* d, int* out);
  * current position; call it only between requests. */
 int orx_decoder_profile_kernels(orx_decoder* d, int iters, void* stream, float* ms);
 
+/* Allocation-free banned argmax (no counterpart in the reference; same result
+ * as orx_decoder_argmax_to_device / asr_ops::ArgmaxBanned on the same logits).
+ * For callers that cannot allocate device memory: code inside a stream capture
+ * it does not own, real-time threads that must not take the driver's
+ * allocation locks, or processes whose device memory is reserved by another
+ * allocator. Writes the index of the largest of `n` fp32 device logits,
+ * skipping ban0/ban1 (-1 = none; exact ties -> lowest index), to the device
+ * int `d_out`, asynchronously on `stream`. Its only scratch is a fixed 8,200-byte
+ * array compiled into the library (held by every GPU that loads it until exit),
+ * so n is limited to 8,388,608; larger n is rejected with ORX_EINVAL. The first
+ * call on each device (with that device current) looks up the array's address;
+ * make that first call before any stream capture. All calls on one device share
+ * the array and it keeps the last call's contents: calls that overlap on the
+ * GPU (e.g. on concurrent streams) race and must be serialized by the caller.
+ * Allocates nothing. */
+int orx_argmax_banned_noalloc(const float* d_logits, int n, int ban0, int ban1, int* d_out,
+                              void* stream);
+
 /* Seeded synthetic fp32 data on the device, bit-exact with oracle/synth.py
  * (test and benchmark inputs; no reference counterpart). */
 int orx_synth_f32(float* d_out, long long n, int seed, int tensor_id, double std, float mean,

@@ -58,6 +58,10 @@ struct DeviceScope {
 cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
 }  // namespace
 
+namespace orx {
+void set_last_error(const char* msg) { g_err = msg; }
+}  // namespace orx
+
 extern "C" {
 
 const char* orx_last_error(void) { return g_err.c_str(); }
