@@ -106,6 +106,14 @@ int orx_decoder_device_error(const orx_decoder* d, int* out);
  * current position; call it only between requests. */
 int orx_decoder_profile_kernels(orx_decoder* d, int iters, void* stream, float* ms);
 
+/* Diagnostic (no reference counterpart): runs `steps` decode steps from the
+ * current cache end, feeding back its own greedy tokens, and writes per kernel
+ * launch {first block start, last block past its dependency wait, last block
+ * end} in GPU global-timer nanoseconds to out[steps * L * 3], L = 5 * layers + 1
+ * (returned in *launches_per_step). Advances cache_len by `steps`. */
+int orx_decoder_trace_decode(orx_decoder* d, int steps, void* stream, unsigned long long* out,
+                             int* launches_per_step);
+
 /* Allocation-free banned argmax (no counterpart in the reference; same result
  * as orx_decoder_argmax_to_device / asr_ops::ArgmaxBanned on the same logits).
  * For callers that cannot allocate device memory: code inside a stream capture

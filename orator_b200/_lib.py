@@ -69,6 +69,8 @@ _SIGS = {
     "orx_decoder_profile_kernels": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "orx_argmax_banned_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                             C.c_void_p]),
+    "orx_decoder_trace_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                           C.POINTER(C.c_int)]),
     "orx_synth_f32": (C.c_int, [C.c_void_p, C.c_longlong, C.c_int, C.c_int, C.c_double,
                                 C.c_float, C.c_int, C.c_void_p]),
 }

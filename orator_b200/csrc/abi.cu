@@ -285,6 +285,18 @@ int orx_decoder_profile_kernels(orx_decoder* d, int iters, void* stream, float* 
   });
 }
 
+int orx_decoder_trace_decode(orx_decoder* d, int steps, void* stream,
+                             unsigned long long* out, int* launches_per_step) {
+  return guard([&] {
+    need(d, "decoder");
+    need(out, "out");
+    if (steps < 1) throw std::invalid_argument("steps must be >= 1");
+    DeviceScope ds(d->device);
+    const int per = d->dec->trace_decode(steps, out, S(stream));
+    if (launches_per_step) *launches_per_step = per;
+  });
+}
+
 int orx_synth_f32(float* d_out, long long n, int seed, int tid, double std, float mean,
                   int round_bf16, void* stream) {
   return guard([&] {

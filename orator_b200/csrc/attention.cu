@@ -81,6 +81,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
   const int split = blockIdx.x, h = blockIdx.y, row = blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int P = a.pages_per_split;
+  trace_mark(a.trace, 0);
   const int tab = a.row_table ? a.row_table[row] : 0;
   const int* pt = a.page_table + (long long)tab * a.max_pages;
   const int* pos_ptr = a.pos_scalar ? a.pos_scalar : (a.row_pos ? a.row_pos + row : nullptr);
@@ -98,6 +99,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
   }
   pdl_trigger();
   pdl_wait();
+  trace_mark(a.trace, 1);
   const int pos = pos_ptr ? *pos_ptr : a.pos_base + row;
   const int npages = (pos + kPage) / kPage;  // pages holding positions [0, pos]
   const int nsplit = (npages + P - 1) / P;
@@ -245,6 +247,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
   uint16_t* orow = a.out + (long long)row * kQDim + (2 * h + kk) * kHeadDim + d;
   if (nsplit == 1) {
     if (own) *orow = f2bf(aa * (1.0f / ll));
+    trace_mark(a.trace, 2);
     return;
   }
   const long long slot = ((long long)row * kKvHeads + h) * a.nsplit_max;
@@ -260,7 +263,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
     sm_last = (ticket == nsplit - 1);
   }
   __syncthreads();
-  if (!sm_last) return;
+  if (!sm_last) {
+    trace_mark(a.trace, 2);
+    return;
+  }
   __threadfence();
   // Combine the splits: per-split (m, l) staged in shared memory, then every
   // owning thread sums its output dimension over the splits.
@@ -290,6 +296,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
     *orow = f2bf(a2 * (1.0f / sl[kk]));
   }
   if (t == 0) a.counters[row * kKvHeads + h] = 0;
+  trace_mark(a.trace, 2);
 }
 
 // Prefill: one CTA per token row, warp per head. Lane holds d = lane + 32*i,

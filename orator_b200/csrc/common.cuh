@@ -112,6 +112,15 @@ __device__ __forceinline__ unsigned long long global_ns() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+// Debug timeline: slot[0] = earliest CTA start, slot[1] = latest CTA past
+// griddepcontrol.wait, slot[2] = latest CTA end (global timer, ns).
+__device__ __forceinline__ void trace_mark(unsigned long long* slot, int k) {
+  if (slot && threadIdx.x == 0) {
+    const unsigned long long t = global_ns();
+    if (k == 0) atomicMin(slot, t); else atomicMax(slot + k, t);
+  }
+}
+
 // Bounded wait: returns false after kWaitLimitNs, or at once when another
 // wait already failed (*err != 0), recording `site` in *err. No trap.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,

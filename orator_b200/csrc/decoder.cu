@@ -2,6 +2,7 @@
 // (src/model/asr_text_decoder.cu:338-899), rebuilt around paged KV, fused
 // weight-streaming kernels and CUDA graphs of PDL-chained launches.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -36,6 +37,24 @@ Decoder::Decoder(Model* m, bool own) : model(m), own_model_(own) {
   ORX_CHECK(cudaMemcpy(st_, &init, sizeof(init), cudaMemcpyHostToDevice));
   d_tmp_tok_ = dalloc<int>(1);
   ORX_CHECK(cudaMallocHost(&h_tok_, sizeof(int)));
+  // persistent decode kernel: usable when one CTA per SM fits and the context
+  // stays within its attention split table
+  const char* nomk = std::getenv("ORX_NO_MK");
+  use_mk_ = !(nomk && nomk[0] == '1') && max_pages_ <= kMkMaxSplit * 8 &&
+            decode_mk_max_grid() > 0;
+  cudaGetLastError();
+  if (use_mk_) {
+    std::vector<MkLayerW> lw(c.num_layers);
+    for (int l = 0; l < c.num_layers; ++l) {
+      const Model::Layer& L = model->layers[l];
+      lw[l] = {L.qkv, L.o, L.gateup, L.down, L.in_ln, L.post_ln, L.q_norm, L.k_norm};
+    }
+    mk_layers_ = dalloc<MkLayerW>(c.num_layers);
+    ORX_CHECK(cudaMemcpy(mk_layers_, lw.data(), sizeof(MkLayerW) * c.num_layers,
+                         cudaMemcpyHostToDevice));
+    mk_part_ = dalloc<float>((size_t)kKvHeads * kMkMaxSplit * kMkPart);
+    mk_sync_ = dalloc<unsigned long long>(4);
+  }
 }
 
 Decoder::~Decoder() {
@@ -45,7 +64,8 @@ Decoder::~Decoder() {
   for (void* p : {(void*)page_table_, (void*)dx_, (void*)dqkv_, (void*)dattn_, (void*)dact_,
                   (void*)logits_, (void*)part_, (void*)counters_, (void*)st_, (void*)d_out_,
                   (void*)d_tmp_tok_, (void*)px_, (void*)pqkv_, (void*)pxn_, (void*)pattn_,
-                  (void*)pact_, (void*)pcounters_})
+                  (void*)pact_, (void*)pcounters_, (void*)mk_layers_, (void*)mk_part_,
+                  (void*)mk_sync_})
     if (p) cudaFree(p);
   if (h_out_) cudaFreeHost(h_out_);
   if (h_tok_) cudaFreeHost(h_tok_);
@@ -168,6 +188,8 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
   const auto& c = model->cfg;
   const int sms = model->num_sms;
   auto on = [&](int k) { return only < 0 || only == k; };
+  int tslot = 0;
+  auto tr = [&]() { return trace_ ? trace_ + 4 * (tslot++) : nullptr; };
   for (int l = 0; l < (only < 0 ? c.num_layers : 1); ++l) {
     const Model::Layer& L = model->layers[l];
     GemvArgs q = {};
@@ -189,6 +211,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     q.epi = kEpiStore;
     q.out_f32 = dqkv_;
     q.st = st_;
+    q.trace = tr();
     if (on(0)) launch_gemv(q, sms, s);
 
     AttnArgs a = {};
@@ -210,6 +233,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     a.counters = counters_;
     a.out = dattn_;
     a.err = &st_->err;
+    a.trace = tr();
     if (on(1)) launch_attention(a, s);
 
     GemvArgs o = {};
@@ -221,6 +245,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     o.epi = kEpiResid;
     o.out_f32 = dx_;
     o.st = st_;
+    o.trace = tr();
     if (on(2)) launch_gemv(o, sms, s);
 
     GemvArgs gu = {};
@@ -234,6 +259,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     gu.epi = kEpiSwiglu;
     gu.out_bf16 = dact_;
     gu.st = st_;
+    gu.trace = tr();
     if (on(3)) launch_gemv(gu, sms, s);
 
     GemvArgs d = {};
@@ -245,6 +271,7 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     d.epi = kEpiResid;
     d.out_f32 = dx_;
     d.st = st_;
+    d.trace = tr();
     if (on(4)) launch_gemv(d, sms, s);
   }
   GemvArgs g = {};
@@ -259,14 +286,58 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
   g.out_f32 = logits_;
   g.finalize = finalize ? 1 : 0;
   g.st = st_;
+  g.trace = tr();
   if (on(5)) launch_gemv(g, sms, s);
+}
+
+// One cooperative launch decoding `steps` tokens from `pos0` (see decode_mk.cu).
+void Decoder::launch_mk(const int* tok_ptr, int steps, int pos0, int count0, bool record,
+                        bool finalize, int ban_steps, int ban0, int ban1, cudaStream_t s) {
+  const auto& c = model->cfg;
+  ORX_CHECK(cudaMemsetAsync(mk_sync_, 0, 4 * sizeof(unsigned long long), s));
+  MkArgs a = {};
+  a.layers = mk_layers_;
+  a.L = c.num_layers;
+  a.embed = model->embed;
+  a.final_norm = model->final_norm;
+  a.vocab = c.vocab_size;
+  a.rope_cos = model->rope_cos;
+  a.rope_sin = model->rope_sin;
+  a.kv = kv_->base;
+  a.kv_layer_stride = (long long)kv_->pages * kPageElems;
+  a.page_table = page_table_;
+  a.max_pages = max_pages_;
+  a.st = st_;
+  a.tok_ptr = tok_ptr;
+  a.steps = steps;
+  a.record = record ? 1 : 0;
+  a.finalize = finalize ? 1 : 0;
+  a.pos0 = pos0;
+  a.count0 = count0;
+  a.ban_steps = ban_steps;
+  a.ban0 = ban0;
+  a.ban1 = ban1;
+  a.x = dx_;
+  a.qkv = dqkv_;
+  a.part = mk_part_;
+  a.act_g = dact_;
+  a.logits = logits_;
+  a.best2 = mk_sync_;
+  a.bar = reinterpret_cast<unsigned int*>(mk_sync_ + 2);
+  a.eps = c.rms_norm_eps;
+  a.trace = mk_trace_;
+  ORX_CHECK(launch_decode_mk(a, model->num_sms, s));
 }
 
 void Decoder::decode_step_device(const int* d_token, int pos, cudaStream_t s) {
   if (pos < 0 || pos >= model->cfg.max_seq_len) throw std::invalid_argument("position out of range");
+  cache_len_ = pos + 1;
+  if (use_mk_) {
+    launch_mk(d_token, 1, pos, 0, false, false, 0, -1, -1, s);
+    return;
+  }
   ORX_CHECK(cudaMemcpyAsync(&st_->pos, &pos, 4, cudaMemcpyHostToDevice, s));
   ORX_CHECK(cudaStreamSynchronize(s));  // `pos` is a stack value
-  cache_len_ = pos + 1;
   record_body(s, d_token, false, false);
   ORX_CHECK(cudaGetLastError());
 }
@@ -341,7 +412,7 @@ std::vector<int> Decoder::decode_greedy(int start_pos, int max_new, int eos0, in
     ORX_CHECK(cudaMallocHost(&h_out_, sizeof(int) * max_new));
     out_cap_ = max_new;
   }
-  ensure_graphs(s);
+  if (!use_mk_) ensure_graphs(s);
   ORX_CHECK(cudaStreamSynchronize(s));
   StepState init = {};
   init.pos = start_pos;
@@ -375,7 +446,10 @@ std::vector<int> Decoder::decode_greedy(int start_pos, int max_new, int eos0, in
   while (emitted < max_new) {
     const bool next_ban = (emitted + 1) < ban_steps;
     const int this_batch = next_ban ? 1 : std::min(batch, max_new - emitted);
-    int left = this_batch;
+    int left = use_mk_ ? 0 : this_batch;
+    if (use_mk_)
+      launch_mk(&st_->tok, this_batch, start_pos + emitted, emitted, true, true, ban_steps, eos0,
+                eos1, s);
     while (left >= graph_steps) {
       ORX_CHECK(cudaGraphLaunch(gk_, s));
       left -= graph_steps;
@@ -414,6 +488,56 @@ void Decoder::profile_kernels(int iters, float* ms, cudaStream_t s) {
   }
   ORX_CHECK(cudaEventDestroy(e0));
   ORX_CHECK(cudaEventDestroy(e1));
+}
+
+// Debug timeline of `steps` eager decode bodies from the current cache end:
+// per launch {first CTA start, last CTA past griddepcontrol.wait, last CTA end}
+// in global-timer ns, written to host_out[steps * launches_per_step * 3].
+int Decoder::trace_decode(int steps, unsigned long long* host_out, cudaStream_t s) {
+  const int per = 5 * model->cfg.num_layers + 1;
+  if (use_mk_) {
+    // persistent kernel: CTA 0's barrier arrive / depart times, 2 per barrier
+    const size_t n = 2 * ((size_t)steps * per + 1);
+    unsigned long long* buf = dalloc<unsigned long long>(n);
+    ORX_CHECK(cudaMemset(buf, 0, n * 8));
+    mk_trace_ = buf;
+    launch_mk(&st_->tok, steps, cache_len_, 0, false, true, 0, -1, -1, s);
+    mk_trace_ = nullptr;
+    ORX_CHECK(cudaStreamSynchronize(s));
+    std::vector<unsigned long long> h(n);
+    ORX_CHECK(cudaMemcpy(h.data(), buf, n * 8, cudaMemcpyDeviceToHost));
+    cudaFree(buf);
+    for (size_t i = 0; i < (size_t)steps * per * 3; ++i) host_out[i] = 0;
+    for (size_t k = 1; k <= (size_t)steps * per; ++k) {  // launch slot k-1: {prev depart, arrive, depart}
+      host_out[(k - 1) * 3] = h[2 * (k - 1) + 1];
+      host_out[(k - 1) * 3 + 1] = h[2 * k];
+      host_out[(k - 1) * 3 + 2] = h[2 * k + 1];
+    }
+    cache_len_ += steps;
+    return per;
+  }
+  const size_t n = (size_t)steps * per * 4;
+  std::vector<unsigned long long> init(n, 0ull);
+  for (size_t i = 0; i < n; i += 4) init[i] = ~0ull;
+  unsigned long long* buf = dalloc<unsigned long long>(n);
+  ORX_CHECK(cudaMemcpy(buf, init.data(), n * 8, cudaMemcpyHostToDevice));
+  int pos = cache_len_;
+  ORX_CHECK(cudaMemcpy(&st_->pos, &pos, 4, cudaMemcpyHostToDevice));
+  for (int i = 0; i < steps; ++i) {
+    trace_ = buf + (size_t)i * per * 4;
+    record_body(s, &st_->tok, false, true);
+  }
+  trace_ = nullptr;
+  ORX_CHECK(cudaStreamSynchronize(s));
+  ORX_CHECK(cudaMemcpy(init.data(), buf, n * 8, cudaMemcpyDeviceToHost));
+  cudaFree(buf);
+  for (size_t i = 0, j = 0; i < n; i += 4, j += 3) {
+    host_out[j] = init[i];
+    host_out[j + 1] = init[i + 1];
+    host_out[j + 2] = init[i + 2];
+  }
+  cache_len_ = pos + steps;
+  return per;
 }
 
 }  // namespace orx

@@ -102,6 +102,15 @@ class Decoder {
   void record_body(cudaStream_t s, const int* tok_ptr, bool record, bool finalize,
                    int only = -1);
   void profile_kernels(int iters, float* ms, cudaStream_t s);
+  int trace_decode(int steps, unsigned long long* host_out, cudaStream_t s);
+  void launch_mk(const int* tok_ptr, int steps, int pos0, int count0, bool record, bool finalize,
+                 int ban_steps, int ban0, int ban1, cudaStream_t s);
+  bool use_mk_ = false;
+  MkLayerW* mk_layers_ = nullptr;
+  float* mk_part_ = nullptr;
+  unsigned long long* mk_sync_ = nullptr;  // [best0, best1, barrier counter]
+  unsigned long long* mk_trace_ = nullptr;
+  unsigned long long* trace_ = nullptr;
 
   Model* model;
   int graph_steps = 8;

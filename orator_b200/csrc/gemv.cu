@@ -20,6 +20,7 @@
 //  * fused epilogues: fp32 store, residual add, SwiGLU + bf16 cast, or logits
 //    with a fused banned argmax (per-CTA best -> 64-bit atomicMax -> last CTA
 //    publishes the token and advances the position).
+#include <cstdlib>
 #include <utility>
 
 #include "common.cuh"
@@ -31,13 +32,13 @@ namespace {
 constexpr int kChunk = 2048;             // bf16 elements per ring slot
 constexpr int kChunkBytes = kChunk * 2;  // 4 KiB
 constexpr int kConsumerWarps = 8;
-constexpr int kDepth = 3;  // chunks in flight per warp
-constexpr int kSlots = kConsumerWarps * kDepth;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreadsGemv = kConsumers;
 constexpr int kMaxK = kInter;  // 6144
 
+template <int kDepth>
 struct GemvSmem {
+  static constexpr int kSlots = kConsumerWarps * kDepth;
   alignas(128) uint8_t ring[kSlots][kChunkBytes];
   alignas(16) uint16_t xs[kMaxK];
   uint64_t full[kSlots];
@@ -57,13 +58,15 @@ __device__ __forceinline__ long long unit_row(int epi, int u, int r) {
   return u;
 }
 
+template <int kDepth>
 __global__ void __launch_bounds__(kThreadsGemv, 2) gemv_kernel(GemvArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  GemvSmem& sm = *reinterpret_cast<GemvSmem*>(
+  GemvSmem<kDepth>& sm = *reinterpret_cast<GemvSmem<kDepth>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
+  trace_mark(a.trace, 0);
   const long long u0 = (long long)blockIdx.x * a.units / G;
   const long long u1 = (long long)(blockIdx.x + 1) * a.units / G;
   const int my_units = static_cast<int>(u1 - u0);
@@ -95,6 +98,7 @@ __global__ void __launch_bounds__(kThreadsGemv, 2) gemv_kernel(GemvArgs a) {
   pdl_trigger();
 
   pdl_wait();
+  trace_mark(a.trace, 1);
   if (a.act_mode == kActBf16) {
     const uint4* src = reinterpret_cast<const uint4*>(a.act);
     uint4* dst = reinterpret_cast<uint4*>(sm.xs);
@@ -216,6 +220,10 @@ __global__ void __launch_bounds__(kThreadsGemv, 2) gemv_kernel(GemvArgs a) {
     }
   }
 
+  if (a.trace) {
+    __syncthreads();
+    trace_mark(a.trace, 2);
+  }
   if (a.epi == kEpiLogits && a.st) {
     if (lane == 0) sm.best[warp] = best;
     consumer_sync();
@@ -239,18 +247,45 @@ __global__ void __launch_bounds__(kThreadsGemv, 2) gemv_kernel(GemvArgs a) {
   }
 }
 
-}  // namespace
 
-void launch_gemv(const GemvArgs& a, int num_sms, cudaStream_t s) {
+template <int D>
+void launch_depth(const GemvArgs& a, int grid, cudaStream_t s) {
   static bool configured = false;
-  const size_t smem = sizeof(GemvSmem) + 128;
+  const size_t smem = sizeof(GemvSmem<D>) + 128;
   if (!configured) {
-    cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(gemv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
     configured = true;
   }
+  launch_pdl(gemv_kernel<D>, dim3(grid), dim3(kThreadsGemv), smem, s, a);
+}
+
+// Ring depth per warp: deeper rings keep more bytes in flight per SM (better
+// for long streams) but stop two GEMV CTAs from sharing an SM (less
+// prologue overlap under programmatic dependent launch).
+int depth_for(const GemvArgs& a) {
+  static const int layer_depth = [] {
+    const char* v = std::getenv("ORX_GEMV_DEPTH");
+    return v ? std::atoi(v) : 3;
+  }();
+  static const int head_depth = [] {
+    const char* v = std::getenv("ORX_GEMV_HEAD_DEPTH");
+    return v ? std::atoi(v) : 6;
+  }();
+  return a.epi == kEpiLogits ? head_depth : layer_depth;
+}
+
+}  // namespace
+
+void launch_gemv(const GemvArgs& a, int num_sms, cudaStream_t s) {
   const int grid = a.units < num_sms ? a.units : num_sms;
-  launch_pdl(gemv_kernel, dim3(grid), dim3(kThreadsGemv), smem, s, a);
+  switch (depth_for(a)) {
+    case 2: launch_depth<2>(a, grid, s); break;
+    case 4: launch_depth<4>(a, grid, s); break;
+    case 5: launch_depth<5>(a, grid, s); break;
+    case 6: launch_depth<6>(a, grid, s); break;
+    default: launch_depth<3>(a, grid, s); break;
+  }
 }
 
 }  // namespace orx

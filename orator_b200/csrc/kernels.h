@@ -45,6 +45,7 @@ struct GemvArgs {
   uint16_t* out_bf16;     // kEpiSwiglu target
   int finalize;           // kEpiLogits: write st->tok and advance st->pos
   StepState* st;
+  unsigned long long* trace;  // optional debug timeline slot (3 words)
 };
 
 // Weight-streaming GEMV for one activation row (decode at batch 1).
@@ -75,6 +76,7 @@ struct AttnArgs {
   int* counters;           // [rows * 8] split tickets (self-resetting)
   uint16_t* out;           // [rows, 2048] bf16
   int* err;
+  unsigned long long* trace;  // optional debug timeline slot (3 words)
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
 
@@ -113,6 +115,44 @@ void launch_f32_to_bf16(const float* in, uint16_t* out, long long n, cudaStream_
 void launch_bf16_to_f32(const uint16_t* in, float* out, long long n, cudaStream_t s);
 void launch_embed_rows(const uint16_t* table, const int* ids, float* out, int rows,
                        cudaStream_t s);
+
+// Persistent cooperative decode kernel (decode_mk.cu).
+constexpr int kMkMaxSplit = 32;  // attention splits per kv head: 32 x 8 pages = 4096 positions
+constexpr int kMkPart = 2 * 132;
+struct MkLayerW {
+  const uint16_t *qkv, *o, *gu, *down;
+  const float *in_ln, *post_ln, *qn, *kn;
+};
+struct MkArgs {
+  const MkLayerW* layers;
+  int L;
+  const uint16_t* embed;
+  const float* final_norm;
+  int vocab;
+  const float* rope_cos;
+  const float* rope_sin;
+  uint16_t* kv;                // pool base; layer l at kv + l * kv_layer_stride
+  long long kv_layer_stride;   // elements
+  const int* page_table;       // identity or session table [max_pages]
+  int max_pages;
+  StepState* st;
+  const int* tok_ptr;          // token of step 0
+  int steps, record, finalize;
+  int pos0, count0, ban_steps, ban0, ban1;
+  float* x;                    // [2048] residual
+  float* qkv;                  // [4096]
+  float* part;                 // [8 * kMaxSplit * kPart]
+  uint16_t* act_g;             // [6144]
+  float* logits;               // [vocab]
+  unsigned long long* best2;   // [2] packed argmax, double-buffered per token
+  unsigned int* bar;           // arrival counter, zero at launch
+  float eps;
+  unsigned long long* trace;   // optional: CTA 0 barrier arrive/depart times
+};
+cudaError_t launch_decode_mk(const MkArgs& a, int grid, cudaStream_t s);
+int decode_mk_max_grid();
+size_t decode_mk_smem();
+void launch_decode_mk_config();
 
 // Programmatic dependent launch is on unless ORX_NO_PDL=1 is set.
 bool pdl_enabled();

@@ -185,6 +185,14 @@ class AsrTextDecoder:
              ms.ctypes.data_as(C.c_void_p))
         return dict(zip(["qkv", "attention", "o", "gateup", "down", "lm_head"], ms.tolist()))
 
+    def trace_decode(self, steps: int = 2, stream=None) -> np.ndarray:
+        per = 5 * self.config.num_layers + 1
+        out = np.zeros(steps * per * 3, np.uint64)
+        n = C.c_int()
+        call("orx_decoder_trace_decode", self._h, steps, _stream(stream),
+             out.ctypes.data_as(C.c_void_p), C.byref(n))
+        return out.reshape(steps, per, 3)
+
     def device_error(self) -> int:
         v = C.c_int()
         call("orx_decoder_device_error", self._h, C.byref(v))
