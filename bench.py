@@ -239,7 +239,106 @@ def run_ours(args):
     mean_s = PROMPT_ROWS + (NEW_TOKENS + 1) / 2
     step_bytes = WEIGHT_BYTES + KV_BYTES_PER_POS * mean_s
     tok_ms = ms / (NEW_TOKENS * args.steps)
-    launches_per_token = 5 * LAYERS + 1
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, seeded N(0,1) audio rows)",
+        "config": {"workload": "config2: 28-layer Qwen3-ASR-1.7B decoder, 400-row prefill, "
+                               "greedy decode of 128 tokens at B=1 (KV 401..528)",
+                   "global_batch": world, "parallelism": f"replicas x{world} (independent sessions)",
+                   "l2": "inputs larger than L2 (3.44 GB of weights streamed per token)"},
+        "per_token_ms": tok_ms,
+        "step_hbm": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes / (tok_ms * 1e-3) / 1e9,
+                     "frac": step_bytes / (tok_ms * 1e-3) / 1e9 / hbm},
+        "roofline": {"bound": "hbm",
+                     "kernel": "decode_mk_kernel (one cooperative launch = 128 tokens x 28 layers + lm_head)",
+                     "achieved": step_bytes * NEW_TOKENS / (ms / args.steps * 1e-3) / 1e9,
+                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": step_bytes * NEW_TOKENS / (ms / args.steps * 1e-3) / 1e9 / hbm,
+                     "traffic": None,
+                     "algorithmic_bytes_per_launch": step_bytes * NEW_TOKENS,
+                     "gemv_kernel_lm_head": {"achieved_gbs": lm_gbs, "frac": lm_gbs / hbm,
+                                             "note": "per-kernel path, 622 MB launch, CUDA events"},
+                     "per_class_ms_per_kernel_path": prof},
+        "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    from orator_b200 import AsrTextConfig, AsrTextDecoder
+
+    dec = AsrTextDecoder(AsrTextConfig(max_seq_len=2048))
+    dec.init_synthetic(SEED)
+    prompt = build_prompt_gpu(dec, torch)
+    dec.ResetCache()
+    dec.Prefill(prompt)
+
+    def step():
+        dec.TruncateCache(PROMPT_ROWS)
+        # ban_steps 0 and no EOS ids: every step decodes exactly 128 tokens
+        return dec.DecodeGreedy(PROMPT_ROWS, NEW_TOKENS, -1, -1, ban_steps=0, batch=NEW_TOKENS)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    barrier()
+    with sampler:
+        e0.record(s)
+        for _ in range(args.steps):
+            toks = step()
+        e1.record(s)
+        barrier()
+    ms = e0.elapsed_time(e1)
+    clocks = sampler.summary()
+
+    # end to end through the public API: host prompt in (H2D), host tokens out (D2H)
+    for _ in range(1):
+        dec.ResetCache(); dec.Prefill(prompt); dec.DecodeGreedy(PROMPT_ROWS, NEW_TOKENS, -1, -1, 0, 32)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(s)
+    for _ in range(args.steps):
+        dec.ResetCache()
+        dec.Prefill(prompt)
+        dec.DecodeGreedy(PROMPT_ROWS, NEW_TOKENS, -1, -1, ban_steps=0, batch=32)
+    f1.record(s)
+    barrier()
+    e2e_ms = f0.elapsed_time(f1)
+
+    prof = dec.profile_kernels(iters=20)
+    if dist:
+        t = torch.tensor([ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return
+    tokens = NEW_TOKENS * args.steps * world
+    value = tokens / (ms / 1e3)
+    hbm, peak_kind = peaks()
+    lm_bytes = VOCAB * HIDDEN * 2 + HIDDEN * 4
+    lm_gbs = lm_bytes / (prof["lm_head"] * 1e-3) / 1e9
+    mean_s = PROMPT_ROWS + (NEW_TOKENS + 1) / 2
+    step_bytes = WEIGHT_BYTES + KV_BYTES_PER_POS * mean_s
+    tok_ms = ms / (NEW_TOKENS * args.steps)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -260,7 +359,7 @@ def run_ours(args):
                 "h2d_bytes_per_step": PROMPT_ROWS * HIDDEN * 4,
                 "d2h_bytes_per_step": NEW_TOKENS * 4,
                 "note": "per step: Prefill(host 400x2048 fp32) + DecodeGreedy(128, batch 32) through the C ABI"},
-        "gpu_launches": args.steps * (NEW_TOKENS * launches_per_token + 1),
+        "gpu_launches": args.steps * 2,  # seed argmax + one persistent decode launch per step
         "clocks": clocks,
     }
     if world == 1 and not args.no_cpu_baseline:

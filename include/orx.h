@@ -99,6 +99,13 @@ int orx_decoder_logits_device(const orx_decoder* d, const float** out);
 /* Device error word written by bounded waits (0 = none). */
 int orx_decoder_device_error(const orx_decoder* d, int* out);
 
+/* asr_gemm::LinearPre (include/model/asr_gemm.h:36-38): out[M,N] = in[M,K] @ W[N,K]^T
+ * with bf16 operands and fp32 accumulation, on the tcgen05 tensor cores.
+ * Device pointers; asynchronous on `stream`. Supported here: bias == NULL,
+ * act == 0, N % 128 == 0, K % 64 == 0 (every Qwen3-ASR decoder projection). */
+int orx_linear_pre(const uint16_t* in_bf16, const uint16_t* W_bf16, const float* bias,
+                   float* out_f32, int M, int K, int N, int act, void* stream);
+
 /* Diagnostic (no reference counterpart): average device ms per launch of each
  * decode kernel class, ms[6] = {qkv GEMV, attention, o GEMV, gate/up GEMV,
  * down GEMV, lm_head GEMV}, each timed over `iters` back-to-back launches with

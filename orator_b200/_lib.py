@@ -71,6 +71,8 @@ _SIGS = {
                                             C.c_void_p]),
     "orx_decoder_trace_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                            C.POINTER(C.c_int)]),
+    "orx_linear_pre": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                 C.c_int, C.c_int, C.c_void_p]),
     "orx_synth_f32": (C.c_int, [C.c_void_p, C.c_longlong, C.c_int, C.c_int, C.c_double,
                                 C.c_float, C.c_int, C.c_void_p]),
 }

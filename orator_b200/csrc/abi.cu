@@ -297,6 +297,27 @@ int orx_decoder_trace_decode(orx_decoder* d, int steps, void* stream,
   });
 }
 
+int orx_linear_pre(const uint16_t* in_bf16, const uint16_t* W_bf16, const float* bias,
+                   float* out_f32, int M, int K, int N, int act, void* stream) {
+  return guard([&] {
+    if (M <= 0 || K <= 0 || N <= 0) return;  // empty input is a no-op, as in the reference
+    need(in_bf16, "in");
+    need(W_bf16, "W");
+    need(out_f32, "out");
+    if (bias || act != 0) throw std::invalid_argument("bias / activation epilogues are not supported");
+    if (N % 128 != 0 || K % 64 != 0) throw std::invalid_argument("N must be a multiple of 128 and K of 64");
+    orx::TcArgs g = {N, K, M, orx::kEpiStore, out_f32, nullptr, N, nullptr};
+    static int* d_err = nullptr;
+    if (!d_err) {
+      orx::check(cudaMalloc(&d_err, sizeof(int)), "cudaMalloc");
+      orx::check(cudaMemset(d_err, 0, sizeof(int)), "cudaMemset");
+    }
+    g.err = d_err;
+    orx::launch_gemm_tc(in_bf16, W_bf16, g, 1, S(stream));
+    orx::check(cudaGetLastError(), "tcgen05 gemm");
+  });
+}
+
 int orx_synth_f32(float* d_out, long long n, int seed, int tid, double std, float mean,
                   int round_bf16, void* stream) {
   return guard([&] {

@@ -1,0 +1,283 @@
+// tcgen05 / TMEM projection GEMM for prefill and batched decode (sm_100a).
+//
+//   out[t, n] (op)= sum_k X[t, k] * W[n, k]       X: [T, K] bf16, W: [N, K] bf16
+//
+// "Weight-stationary" orientation: the MMA's M side is 128 weight rows and its
+// N side is a tile of BN tokens (16..256), so a batch of 64 decode tokens or
+// a 400-row prefill both map onto full 128-row tcgen05 tiles. Each CTA owns
+// one 128-row weight tile, one token tile and one K range (split-K for the
+// short projections):
+//   * warp 0 / one lane: TMA producer — 128x64 weight box and BNx64
+//     activation box per stage (128-byte swizzle), mbarrier complete_tx;
+//   * warp 1 / one lane: MMA issuer — 4 x tcgen05.mma (K = 16 each) per stage
+//     into a TMEM accumulator of BN fp32 columns, tcgen05.commit releases the
+//     stage;
+//   * all 4 warps: epilogue — tcgen05.ld of their 32 TMEM lanes (= 32 weight
+//     rows), then fp32 store, residual add (atomic when split over K) or
+//     SwiGLU on [64 gate | 64 up] tiles with the bf16 cast of the reference.
+// Replaces Bf16WmmaKernel2 (include/model/gemm.cuh:394-459) and the
+// F32ToBf16 / AddResidual / SwiGLU launches around it.
+// No TMA multicast anywhere: every CTA loads its own tiles.
+#include <cuda.h>
+
+#include <cstdio>
+#include <mutex>
+#include <utility>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace orx {
+namespace {
+
+constexpr int kTcThreads = 128;
+constexpr int kBK = 64;                  // K per stage (128 bytes of bf16)
+constexpr int kATileB = 128 * kBK * 2;   // 16 KiB
+
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>(1) << 16;            // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;    // SBO: 8 rows x 128 B
+  d |= static_cast<uint64_t>(1) << 46;            // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;            // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN, int STAGES>
+struct TcSmem {
+  alignas(1024) uint8_t a[STAGES][kATileB];
+  alignas(1024) uint8_t b[STAGES][BN * kBK * 2];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t done;
+  uint32_t tmem_base;
+  float swap[64][33];  // SwiGLU: up rows handed from warps 2-3 to warps 0-1
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                   TcArgs g) {
+  extern __shared__ uint8_t tc_raw[];
+  TcSmem<BN, STAGES>& sm = *reinterpret_cast<TcSmem<BN, STAGES>*>(
+      (reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * 128, n0 = blockIdx.y * BN;
+  const int kper = g.K / gridDim.z;
+  const int kbeg = blockIdx.z * kper;
+  const int KT = kper / kBK;
+  constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  int* err = g.err;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int s = 0; s < STAGES; ++s) {
+        mbar_init(&sm.full[s], 1);
+        mbar_init(&sm.empty[s], 1);
+      }
+      mbar_init(&sm.done, 1);
+      fence_mbar_init();
+    }
+    __syncwarp();
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sm.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = sm.tmem_base;
+  pdl_trigger();
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer (weights do not depend on the previous kernel) ----
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES && !mbar_wait(&sm.empty[s], ((kt / STAGES) - 1) & 1, err, 31)) break;
+      mbar_arrive_expect_tx(&sm.full[s], kATileB + BN * kBK * 2);
+      tma_load_2d(sm.a[s], &tmW, kbeg + kt * kBK, m0, &sm.full[s]);
+      if (kt == 0) pdl_wait();  // activations come from the previous kernel
+      tma_load_2d(sm.b[s], &tmX, kbeg + kt * kBK, n0, &sm.full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                               (static_cast<uint32_t>(BN >> 3) << 17) | (8u << 24);
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (!mbar_wait(&sm.full[s], (kt / STAGES) & 1, err, 32)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint64_t ad = umma_desc_sw128(smem_u32(sm.a[s]));
+      const uint64_t bd = umma_desc_sw128(smem_u32(sm.b[s]));
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes per K=16 step inside the atom
+        umma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kt | kk) != 0);
+      umma_commit(&sm.empty[s]);
+    }
+    umma_commit(&sm.done);
+  }
+  __syncwarp();
+
+  // ---- epilogue: all warps; warp w owns TMEM lanes (weight rows) 32w..32w+31 ----
+  pdl_wait();
+  mbar_wait(&sm.done, 0, err, 33);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const int row = m0 + warp * 32 + lane;
+  const uint32_t tbase = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    float v[32];
+    tmem_ld32(tbase + c0, v);
+    if (g.epi == kEpiSwiglu) {
+      __syncthreads();
+      if (warp >= 2) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sm.swap[(warp - 2) * 32 + lane][i] = v[i];
+      }
+      __syncthreads();
+      if (warp < 2) {
+        const int r = warp * 32 + lane;  // gate row within the tile
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int t = n0 + c0 + i;
+          if (c0 + i < BN && t < g.T) {
+            const float gt = v[i], up = sm.swap[r][i];
+            g.out_bf16[(long long)t * g.ldo + (m0 >> 1) + r] = f2bf((gt / (1.0f + expf(-gt))) * up);
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int t = n0 + c0 + i;
+        if (c0 + i < BN && t < g.T) {
+          float* o = g.out_f32 + (long long)t * g.ldo + row;
+          if (gridDim.z > 1)
+            atomicAdd(o, v[i]);
+          else if (g.epi == kEpiResid)
+            *o += v[i];
+          else
+            *o = v[i];
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                              CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                              CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeFn>(nullptr);
+    return reinterpret_cast<EncodeFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D bf16 map over a row-major [rows, K] matrix; box = 64 elements x box_rows,
+// 128-byte swizzle (the canonical K-major layout of tcgen05 operands).
+bool make_map(CUtensorMap* m, const void* base, long long rows, int K, int box_rows) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES>
+void launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& g, int splits,
+               cudaStream_t s) {
+  static bool configured = false;
+  const size_t smem = sizeof(TcSmem<BN, STAGES>) + 1024;
+  if (!configured) {
+    cudaFuncSetAttribute(tc_gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    configured = true;
+  }
+  launch_pdl(tc_gemm_kernel<BN, STAGES>, dim3(g.N / 128, (g.T + BN - 1) / BN, splits),
+             dim3(kTcThreads), smem, s, mw, mx, g);
+}
+
+}  // namespace
+
+bool tc_available() { return encode_fn() != nullptr; }
+
+void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
+                    cudaStream_t s) {
+  if (g.T <= 0) return;
+  const int bn = g.T <= 16 ? 16 : g.T <= 32 ? 32 : g.T <= 64 ? 64 : g.T <= 128 ? 128 : 256;
+  CUtensorMap mw, mx;
+  if (!make_map(&mw, W, g.N, g.K, 128) || !make_map(&mx, X, g.T, g.K, bn)) {
+    fprintf(stderr, "orx: tensor map encoding failed\n");
+    return;
+  }
+  switch (bn) {
+    case 16: launch_bn<16, 8>(mw, mx, g, splits, s); break;
+    case 32: launch_bn<32, 8>(mw, mx, g, splits, s); break;
+    case 64: launch_bn<64, 6>(mw, mx, g, splits, s); break;
+    case 128: launch_bn<128, 6>(mw, mx, g, splits, s); break;
+    default: launch_bn<256, 4>(mw, mx, g, splits, s); break;
+  }
+}
+
+}  // namespace orx

@@ -102,6 +102,20 @@ struct GemmArgs {
 };
 void launch_gemm(const GemmArgs& a, cudaStream_t s);
 
+// tcgen05 GEMM (gemm_tc.cu): out[t, n] (op)= sum_k X[t, k] W[n, k].
+struct TcArgs {
+  int N, K, T;         // weight rows (multiple of 128), depth (multiple of 64 * splits), tokens
+  int epi;             // kEpiStore / kEpiResid / kEpiSwiglu
+  float* out_f32;      // [T, ldo]; split-K accumulates atomically (zero it for kEpiStore)
+  uint16_t* out_bf16;  // SwiGLU output [T, ldo]
+  int ldo;
+  int* err;
+};
+// X: [T, K] bf16 row-major (device), W: [N, K] bf16. splits divides K / 64.
+void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
+                    cudaStream_t s);
+bool tc_available();
+
 // Argmax over fp32 logits with up to two banned ids into st (finalize sets st->tok).
 void launch_argmax(const float* logits, int n, int ban0, int ban1, StepState* st, int* out_dev,
                    cudaStream_t s);
