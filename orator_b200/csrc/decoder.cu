@@ -10,6 +10,23 @@
 
 namespace orx {
 
+// Projection on the tcgen05 GEMM with split-K chosen so that about one wave
+// of CTAs covers the SMs (the short projections o / down / qkv at small T).
+void run_proj(const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi, float* out_f32,
+              uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s) {
+  if (T <= 0) return;
+  const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+  const int tiles = (N / 128) * ((T + bn - 1) / bn);
+  int splits = 1;
+  if (epi != kEpiSwiglu)
+    while (tiles * splits * 2 <= num_sms && (K % (64 * splits * 2)) == 0 && K / (splits * 2) >= 256)
+      splits *= 2;
+  if (epi == kEpiStore && splits > 1)
+    ORX_CHECK(cudaMemsetAsync(out_f32, 0, sizeof(float) * (size_t)T * ldo, s));
+  TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err};
+  launch_gemm_tc(X, W, g, splits, s);
+}
+
 namespace {
 constexpr int kDecodePagesPerSplit = 8;  // flash-decoding split size at batch 1
 constexpr int kPartStride = 2 * 132;
@@ -64,7 +81,7 @@ Decoder::~Decoder() {
   for (void* p : {(void*)page_table_, (void*)dx_, (void*)dqkv_, (void*)dattn_, (void*)dact_,
                   (void*)logits_, (void*)part_, (void*)counters_, (void*)st_, (void*)d_out_,
                   (void*)d_tmp_tok_, (void*)px_, (void*)pqkv_, (void*)pxn_, (void*)pattn_,
-                  (void*)pact_, (void*)pcounters_, (void*)mk_layers_, (void*)mk_part_,
+                  (void*)pact_, (void*)pcounters_, (void*)ppart_, (void*)mk_layers_, (void*)mk_part_,
                   (void*)mk_sync_})
     if (p) cudaFree(p);
   if (h_out_) cudaFreeHost(h_out_);
@@ -99,9 +116,11 @@ void Decoder::ensure_prefill(int T) {
   if (T <= tcap_) return;
   int cap = std::max(T, 64);
   for (void* p : {(void*)px_, (void*)pqkv_, (void*)pxn_, (void*)pattn_, (void*)pact_,
-                  (void*)pcounters_})
+                  (void*)pcounters_, (void*)ppart_})
     if (p) cudaFree(p);
   px_ = dalloc<float>((size_t)cap * kHidden);
+  ppart_ = dalloc<float>((size_t)cap * kKvHeads *
+                         ((max_pages_ + kDecodePagesPerSplit - 1) / kDecodePagesPerSplit) * kPartStride);
   pqkv_ = dalloc<float>((size_t)cap * kQkvDim);
   pxn_ = dalloc<uint16_t>((size_t)cap * kHidden);
   pattn_ = dalloc<uint16_t>((size_t)cap * kQDim);
@@ -118,7 +137,7 @@ void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
     const Model::Layer& L = model->layers[l];
     uint16_t* kvl = kv_->layer(l);
     launch_rmsnorm_bf16(px_, L.in_ln, pxn_, T, c.rms_norm_eps, s);
-    launch_gemm({pxn_, L.qkv, T, kQkvDim, kHidden, kEpiStore, pqkv_, nullptr, kQkvDim}, s);
+    run_proj(pxn_, L.qkv, kQkvDim, kHidden, T, kEpiStore, pqkv_, nullptr, kQkvDim, &st_->err, model->num_sms, s);
     launch_qk_norm_rope_store(pqkv_, T, L.q_norm, L.k_norm, model->rope_cos, model->rope_sin,
                               kvl, page_table_, max_pages_, nullptr, nullptr, pos0, s);
     AttnArgs a = {};
@@ -132,16 +151,18 @@ void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
     a.pos_base = pos0;
     a.rows = T;
     a.fused_kv = 0;
-    a.nsplit_max = 1;
-    a.pages_per_split = max_pages_;
+    // splits needed by the longest row (position pos0 + T - 1)
+    a.nsplit_max = ((pos0 + T + kPage - 1) / kPage + kDecodePagesPerSplit - 1) / kDecodePagesPerSplit;
+    a.pages_per_split = kDecodePagesPerSplit;
+    a.part = ppart_;
     a.counters = pcounters_;
     a.out = pattn_;
     a.err = &st_->err;
     launch_attention(a, s);
-    launch_gemm({pattn_, L.o, T, kHidden, kQDim, kEpiResid, px_, nullptr, kHidden}, s);
+    run_proj(pattn_, L.o, kHidden, kQDim, T, kEpiResid, px_, nullptr, kHidden, &st_->err, model->num_sms, s);
     launch_rmsnorm_bf16(px_, L.post_ln, pxn_, T, c.rms_norm_eps, s);
-    launch_gemm({pxn_, L.gateup, T, 2 * kInter, kHidden, kEpiSwiglu, nullptr, pact_, kInter}, s);
-    launch_gemm({pact_, L.down, T, kHidden, kInter, kEpiResid, px_, nullptr, kHidden}, s);
+    run_proj(pxn_, L.gateup, 2 * kInter, kHidden, T, kEpiSwiglu, nullptr, pact_, kInter, &st_->err, model->num_sms, s);
+    run_proj(pact_, L.down, kHidden, kInter, T, kEpiResid, px_, nullptr, kHidden, &st_->err, model->num_sms, s);
   }
   // Final norm of the last row + tied lm_head (+ argmax into the step state).
   GemvArgs g = {};

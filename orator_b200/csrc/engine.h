@@ -37,6 +37,9 @@ struct ModelConfig {
 // Device-resident weights of the 28-layer decoder (layout chosen for the
 // streaming GEMV and the GEMM epilogues; see set_tensor for the mapping from
 // the reference's thinker.model.* tensors).
+void run_proj(const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi, float* out_f32,
+              uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s);
+
 class Model {
  public:
   struct Layer {
@@ -144,6 +147,7 @@ class Decoder {
   float *px_ = nullptr, *pqkv_ = nullptr;
   uint16_t *pxn_ = nullptr, *pattn_ = nullptr, *pact_ = nullptr;
   int* pcounters_ = nullptr;
+  float* ppart_ = nullptr;
   float* h_stage_ = nullptr;
   size_t h_stage_cap_ = 0;
   cudaGraphExec_t g1_ = nullptr, gk_ = nullptr;

@@ -85,5 +85,6 @@ def test_loader_matches_synthetic_init(trio, cuda):
     ours.ResetCache()
     ours.Prefill(x)
     other.Prefill(x)
-    assert np.array_equal(ours.CopyLogits(), other.CopyLogits())
+    # split-K accumulation is atomic, so the summation order may differ run to run
+    assert np.abs(ours.CopyLogits() - other.CopyLogits()).max() < 1e-2
     other.close()
