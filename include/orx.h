@@ -99,6 +99,35 @@ int orx_decoder_logits_device(const orx_decoder* d, const float** out);
 /* Device error word written by bounded waits (0 = none). */
 int orx_decoder_device_error(const orx_decoder* d, int* out);
 
+/* ---- Continuous batching (no single reference counterpart: replaces one
+ * AsrTextDecoder per session, src/model/asr_text_decoder.cu:309-318, and the
+ * per-session worker threads of src/pipeline/asr_worker.cc:270-416). Many
+ * sessions share one paged KV pool (16-token pages) and the weights of an
+ * existing decoder (`weights`, which must outlive the batch). */
+typedef struct orx_batch orx_batch;
+int orx_batch_create(orx_decoder* weights, int max_sessions, int max_batch, int pool_pages,
+                     int max_pages_per_session, orx_batch** out);
+void orx_batch_destroy(orx_batch* b);
+/* New empty session (ORX_EINVAL when every slot is in use). */
+int orx_batch_session_create(orx_batch* b, int* sid);
+/* Ends a session and returns its pages to the pool. */
+int orx_batch_session_free(orx_batch* b, int sid);
+/* cache_len / TruncateCache per session (asr_text_decoder.h:73-76); truncation
+ * returns whole pages beyond the new length to the pool. */
+int orx_batch_cache_len(const orx_batch* b, int sid, int* out);
+int orx_batch_truncate(orx_batch* b, int sid, int len);
+int orx_batch_free_pages(const orx_batch* b, int* out);
+/* PrefillAt for n sessions at once: lens[i] host embedding rows (concatenated
+ * [sum lens, 2048] fp32) appended at each session's cache end; leaves each
+ * session's next greedy token on the device. ORX_EINVAL and nothing changed
+ * when the page pool cannot hold the rows (the join is rejected). */
+int orx_batch_prefill(orx_batch* b, const int* sids, const int* lens, int n,
+                      const float* embeds, void* stream);
+/* One greedy decode token for each of the n sessions (ragged lengths) in one
+ * batched step; tokens_out (host, n ints, may be NULL) receives them. */
+int orx_batch_step(orx_batch* b, const int* sids, int n, int* tokens_out, void* stream);
+int orx_batch_device_error(const orx_batch* b, int* out);
+
 /* asr_gemm::LinearPre (include/model/asr_gemm.h:36-38): out[M,N] = in[M,K] @ W[N,K]^T
  * with bf16 operands and fp32 accumulation, on the tcgen05 tensor cores.
  * Device pointers; asynchronous on `stream`. Supported here: bias == NULL,

@@ -71,6 +71,18 @@ _SIGS = {
                                             C.c_void_p]),
     "orx_decoder_trace_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                            C.POINTER(C.c_int)]),
+    "orx_batch_create": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                   C.POINTER(C.c_void_p)]),
+    "orx_batch_destroy": (None, [C.c_void_p]),
+    "orx_batch_session_create": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "orx_batch_session_free": (C.c_int, [C.c_void_p, C.c_int]),
+    "orx_batch_cache_len": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
+    "orx_batch_truncate": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "orx_batch_free_pages": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "orx_batch_prefill": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                    C.c_void_p]),
+    "orx_batch_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "orx_batch_device_error": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     "orx_linear_pre": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                  C.c_int, C.c_int, C.c_void_p]),
     "orx_synth_f32": (C.c_int, [C.c_void_p, C.c_longlong, C.c_int, C.c_int, C.c_double,

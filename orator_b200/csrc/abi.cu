@@ -14,6 +14,11 @@ struct orx_decoder {
   int device = 0;
 };
 
+struct orx_batch {
+  orx::BatchDecoder* b = nullptr;
+  int device = 0;
+};
+
 namespace {
 thread_local std::string g_err;
 
@@ -294,6 +299,86 @@ int orx_decoder_trace_decode(orx_decoder* d, int steps, void* stream,
     DeviceScope ds(d->device);
     const int per = d->dec->trace_decode(steps, out, S(stream));
     if (launches_per_step) *launches_per_step = per;
+  });
+}
+
+int orx_batch_create(orx_decoder* weights, int max_sessions, int max_batch, int pool_pages,
+                     int max_pages_per_session, orx_batch** out) {
+  return guard([&] {
+    need(weights, "weights decoder");
+    need(out, "out");
+    *out = nullptr;
+    DeviceScope ds(weights->device);
+    auto* h = new orx_batch;
+    h->device = weights->device;
+    try {
+      h->b = new orx::BatchDecoder(weights->dec->model, max_sessions, max_batch, pool_pages,
+                                   max_pages_per_session);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+void orx_batch_destroy(orx_batch* b) {
+  if (!b) return;
+  DeviceScope ds(b->device);
+  delete b->b;
+  delete b;
+}
+
+int orx_batch_session_create(orx_batch* b, int* sid) {
+  return guard([&] {
+    need(b, "batch");
+    need(sid, "sid");
+    *sid = b->b->create_session();
+    if (*sid < 0) throw std::invalid_argument("no free session slot");
+  });
+}
+
+int orx_batch_session_free(orx_batch* b, int sid) {
+  return guard([&] { need(b, "batch"); b->b->free_session(sid); });
+}
+
+int orx_batch_cache_len(const orx_batch* b, int sid, int* out) {
+  return guard([&] { need(b, "batch"); need(out, "out"); *out = b->b->cache_len(sid); });
+}
+
+int orx_batch_truncate(orx_batch* b, int sid, int len) {
+  return guard([&] { need(b, "batch"); b->b->truncate(sid, len); });
+}
+
+int orx_batch_free_pages(const orx_batch* b, int* out) {
+  return guard([&] { need(b, "batch"); need(out, "out"); *out = b->b->free_pages(); });
+}
+
+int orx_batch_prefill(orx_batch* b, const int* sids, const int* lens, int n,
+                      const float* embeds, void* stream) {
+  return guard([&] {
+    need(b, "batch");
+    if (n > 0) { need(sids, "sids"); need(lens, "lens"); need(embeds, "embeds"); }
+    DeviceScope ds(b->device);
+    b->b->prefill(sids, lens, n, embeds, S(stream));
+  });
+}
+
+int orx_batch_step(orx_batch* b, const int* sids, int n, int* tokens_out, void* stream) {
+  return guard([&] {
+    need(b, "batch");
+    if (n > 0) need(sids, "sids");
+    DeviceScope ds(b->device);
+    b->b->step(sids, n, tokens_out, S(stream));
+  });
+}
+
+int orx_batch_device_error(const orx_batch* b, int* out) {
+  return guard([&] {
+    need(b, "batch");
+    need(out, "out");
+    DeviceScope ds(b->device);
+    *out = b->b->device_error();
   });
 }
 

@@ -1,0 +1,343 @@
+// Continuous-batching decoder: many independent sessions share one paged KV
+// pool and one set of weights; every decode step packs the active sessions'
+// next tokens into one batch (ragged KV lengths, per-session page tables).
+//
+// The reference decodes one session per AsrTextDecoder with a contiguous
+// [max_seq, 8, 128] cache (src/model/asr_text_decoder.cu:309-318) and one
+// pipeline thread per session (src/pipeline/asr_worker.cc:270-416); this is
+// the batched replacement: projections run on the tcgen05 GEMM with M = 128
+// weight rows x N = batch tokens, attention is flash-decoding over each row's
+// own page table, and joins / leaves only edit host-side page lists and the
+// device page table.
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+#include "engine.h"
+
+namespace orx {
+
+namespace {
+constexpr int kSplitPages = 8;
+constexpr int kPartFloats = 2 * 132;
+
+// tokens[r] = next_tok[row_table[r]]; x[r] = embed[tokens[r]] (fp32).
+__global__ void gather_tokens_embed(const int* next_tok, const int* row_table, const uint16_t* embed,
+                                    int* tokens, float* x) {
+  pdl_wait();
+  const int r = blockIdx.x;
+  const int tok = next_tok[row_table[r]];
+  if (threadIdx.x == 0) tokens[r] = tok;
+  const uint16_t* src = embed + (long long)tok * kHidden;
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) x[(long long)r * kHidden + i] = bf2f(src[i]);
+}
+
+// Row-wise banned-free argmax of logits [rows, n]; writes next_tok[row_table[r]]
+// and out[r]. Exact ties resolve to the lowest index.
+__global__ void __launch_bounds__(1024) rows_argmax(const float* logits, int n, const int* row_table,
+                                                    int* next_tok, int* out) {
+  pdl_wait();
+  __shared__ unsigned long long sb[32];
+  const int r = blockIdx.x;
+  const float* x = logits + (long long)r * n;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = x[i];
+    if (v != v) continue;
+    const unsigned long long k = argmax_key(v, i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, o);
+    best = ob > best ? ob : best;
+  }
+  if ((threadIdx.x & 31) == 0) sb[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long b = 0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) b = sb[w] > b ? sb[w] : b;
+    const int tok = b ? argmax_key_index(b) : 0;
+    if (row_table) next_tok[row_table[r]] = tok;
+    if (out) out[r] = tok;
+  }
+}
+
+// x_last[i] = x[last_row[i]]
+__global__ void gather_rows(const float* x, const int* rows, float* out) {
+  pdl_wait();
+  const int i = blockIdx.x;
+  const float* src = x + (long long)rows[i] * kHidden;
+  for (int j = threadIdx.x; j < kHidden; j += blockDim.x) out[(long long)i * kHidden + j] = src[j];
+}
+}  // namespace
+
+BatchDecoder::BatchDecoder(Model* m, int max_sessions, int max_batch, int pool_pages,
+                           int max_pages_per_session)
+    : model(m), max_sessions_(max_sessions), max_batch_(max_batch), mps_(max_pages_per_session) {
+  if (max_sessions <= 0 || max_batch <= 0 || pool_pages <= 0 || max_pages_per_session <= 0)
+    throw std::invalid_argument("invalid batch decoder sizes");
+  if ((long long)max_pages_per_session * kPage > m->rope_positions)
+    throw std::invalid_argument("max_pages_per_session exceeds the model's max_seq_len");
+  kv_ = new KvPool(m->cfg.num_layers, pool_pages);
+  free_pages_.resize(pool_pages);
+  for (int i = 0; i < pool_pages; ++i) free_pages_[i] = pool_pages - 1 - i;
+  sessions_.resize(max_sessions);
+  h_table_.assign((size_t)max_sessions * mps_, 0);
+  d_table_ = dalloc<int>((size_t)max_sessions * mps_);
+  ORX_CHECK(cudaMemset(d_table_, 0, sizeof(int) * (size_t)max_sessions * mps_));
+  d_next_tok_ = dalloc<int>(max_sessions);
+  ORX_CHECK(cudaMemset(d_next_tok_, 0, sizeof(int) * max_sessions));
+  st_ = dalloc<StepState>(1);
+  StepState init = {};
+  ORX_CHECK(cudaMemcpy(st_, &init, sizeof(init), cudaMemcpyHostToDevice));
+  ORX_CHECK(cudaMallocHost(&h_rows_, sizeof(int) * 2 * 65536));
+  ensure_rows(max_batch);
+}
+
+BatchDecoder::~BatchDecoder() {
+  delete kv_;
+  for (void* p : {(void*)d_table_, (void*)d_next_tok_, (void*)st_, (void*)x_, (void*)xn_, (void*)qkv_,
+                  (void*)attn_, (void*)act_, (void*)logits_, (void*)part_, (void*)counters_,
+                  (void*)d_rows_, (void*)d_tokens_, (void*)d_out_})
+    if (p) cudaFree(p);
+  if (h_rows_) cudaFreeHost(h_rows_);
+}
+
+void BatchDecoder::ensure_rows(int rows) {
+  if (rows <= rows_cap_) return;
+  const int cap = std::max(rows, 64);
+  for (void* p : {(void*)x_, (void*)xn_, (void*)qkv_, (void*)attn_, (void*)act_, (void*)part_,
+                  (void*)counters_, (void*)d_rows_, (void*)d_tokens_, (void*)d_out_})
+    if (p) cudaFree(p);
+  x_ = dalloc<float>((size_t)cap * kHidden);
+  xn_ = dalloc<uint16_t>((size_t)cap * kHidden);
+  qkv_ = dalloc<float>((size_t)cap * kQkvDim);
+  attn_ = dalloc<uint16_t>((size_t)cap * kQDim);
+  act_ = dalloc<uint16_t>((size_t)cap * kInter);
+  const int nsplit_cap = (mps_ + kSplitPages - 1) / kSplitPages;
+  part_ = dalloc<float>((size_t)cap * kKvHeads * nsplit_cap * kPartFloats);
+  counters_ = dalloc<int>((size_t)cap * kKvHeads);
+  ORX_CHECK(cudaMemset(counters_, 0, sizeof(int) * (size_t)cap * kKvHeads));
+  d_rows_ = dalloc<int>((size_t)cap * 2);
+  d_tokens_ = dalloc<int>(cap);
+  d_out_ = dalloc<int>(cap);
+  rows_cap_ = cap;
+}
+
+void BatchDecoder::ensure_logits(int rows) {
+  if (rows <= logits_cap_) return;
+  if (logits_) cudaFree(logits_);
+  logits_ = dalloc<float>((size_t)rows * model->cfg.vocab_size);
+  logits_cap_ = rows;
+}
+
+int BatchDecoder::create_session() {
+  for (int i = 0; i < max_sessions_; ++i)
+    if (!sessions_[i].live) {
+      sessions_[i] = Session{};
+      sessions_[i].live = true;
+      return i;
+    }
+  return -1;
+}
+
+void BatchDecoder::check_sid(int sid) const {
+  if (sid < 0 || sid >= max_sessions_ || !sessions_[sid].live)
+    throw std::invalid_argument("unknown session id");
+}
+
+void BatchDecoder::free_session(int sid) {
+  check_sid(sid);
+  for (int p : sessions_[sid].pages) free_pages_.push_back(p);
+  sessions_[sid] = Session{};
+}
+
+int BatchDecoder::cache_len(int sid) const {
+  check_sid(sid);
+  return sessions_[sid].len;
+}
+
+void BatchDecoder::truncate(int sid, int len) {
+  check_sid(sid);
+  Session& s = sessions_[sid];
+  if (len < 0 || len > s.len) throw std::invalid_argument("bad truncate length");
+  s.len = len;
+  const int keep = (len + kPage - 1) / kPage;
+  while ((int)s.pages.size() > keep) {
+    free_pages_.push_back(s.pages.back());
+    s.pages.pop_back();
+  }
+}
+
+// Makes session `sid` own pages for positions [0, new_len); false when the
+// pool or the session's page table is exhausted (nothing is allocated then).
+bool BatchDecoder::reserve(int sid, int new_len) {
+  Session& s = sessions_[sid];
+  const int need = (new_len + kPage - 1) / kPage;
+  if (need > mps_) return false;
+  const int extra = need - static_cast<int>(s.pages.size());
+  if (extra <= 0) return true;
+  if (extra > static_cast<int>(free_pages_.size())) return false;
+  for (int i = 0; i < extra; ++i) {
+    const int p = free_pages_.back();
+    free_pages_.pop_back();
+    h_table_[(size_t)sid * mps_ + s.pages.size()] = p;
+    s.pages.push_back(p);
+  }
+  dirty_ = true;
+  return true;
+}
+
+void BatchDecoder::upload_table(cudaStream_t st) {
+  if (!dirty_) return;
+  ORX_CHECK(cudaMemcpyAsync(d_table_, h_table_.data(), sizeof(int) * h_table_.size(),
+                            cudaMemcpyHostToDevice, st));
+  ORX_CHECK(cudaStreamSynchronize(st));  // h_table_ is pageable and may change next call
+  dirty_ = false;
+}
+
+// Shared per-layer body over `rows` rows of x_ whose (session, position) are in
+// d_rows_ = [row_table | row_pos]. fused: decode mode (q/k norm, RoPE and the
+// K/V store inside attention); otherwise the prefill store kernel runs first.
+void BatchDecoder::layers(int rows, int max_len, bool fused, cudaStream_t s) {
+  const auto& c = model->cfg;
+  const int* row_table = d_rows_;
+  const int* row_pos = d_rows_ + rows_cap_;
+  const int sms = model->num_sms;
+  const int nsplit = ((max_len + kPage - 1) / kPage + kSplitPages - 1) / kSplitPages;
+  int* err = &st_->err;
+  for (int l = 0; l < c.num_layers; ++l) {
+    const Model::Layer& L = model->layers[l];
+    uint16_t* kvl = kv_->layer(l);
+    launch_rmsnorm_bf16(x_, L.in_ln, xn_, rows, c.rms_norm_eps, s);
+    run_proj(xn_, L.qkv, kQkvDim, kHidden, rows, kEpiStore, qkv_, nullptr, kQkvDim, err, sms, s);
+    if (!fused)
+      launch_qk_norm_rope_store(qkv_, rows, L.q_norm, L.k_norm, model->rope_cos, model->rope_sin,
+                                kvl, d_table_, mps_, row_table, row_pos, 0, s);
+    AttnArgs a = {};
+    a.qkv = qkv_;
+    a.qkv_stride = kQkvDim;
+    a.q_norm_w = L.q_norm;
+    a.k_norm_w = L.k_norm;
+    a.rope_cos = model->rope_cos;
+    a.rope_sin = model->rope_sin;
+    a.kv_layer = kvl;
+    a.page_table = d_table_;
+    a.max_pages = mps_;
+    a.row_table = row_table;
+    a.row_pos = row_pos;
+    a.rows = rows;
+    a.fused_kv = fused ? 1 : 0;
+    a.nsplit_max = nsplit;
+    a.pages_per_split = kSplitPages;
+    a.part = part_;
+    a.counters = counters_;
+    a.out = attn_;
+    a.err = err;
+    launch_attention(a, s);
+    run_proj(attn_, L.o, kHidden, kQDim, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s);
+    launch_rmsnorm_bf16(x_, L.post_ln, xn_, rows, c.rms_norm_eps, s);
+    run_proj(xn_, L.gateup, 2 * kInter, kHidden, rows, kEpiSwiglu, nullptr, act_, kInter, err, sms, s);
+    run_proj(act_, L.down, kHidden, kInter, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s);
+  }
+}
+
+void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float* host_embeds,
+                           cudaStream_t s) {
+  if (n <= 0) return;
+  int total = 0, max_len = 0;
+  for (int i = 0; i < n; ++i) {
+    check_sid(sids[i]);
+    if (lens[i] <= 0) throw std::invalid_argument("empty prefill");
+    for (int j = 0; j < i; ++j)
+      if (sids[j] == sids[i]) throw std::invalid_argument("session listed twice");
+    total += lens[i];
+  }
+  if (total > 65536 / 2) throw std::invalid_argument("too many prefill rows in one call");
+  for (int i = 0; i < n; ++i)
+    if (!reserve(sids[i], sessions_[sids[i]].len + lens[i]))
+      throw std::invalid_argument("KV page pool exhausted");
+  ensure_rows(std::max(total, n));
+  ensure_logits(n);
+  // rows: [row_table (rows_cap_) | row_pos (rows_cap_)], then the last-row list
+  int r = 0;
+  std::vector<int> last(n);
+  for (int i = 0; i < n; ++i) {
+    const Session& ss = sessions_[sids[i]];
+    for (int t = 0; t < lens[i]; ++t, ++r) {
+      h_rows_[r] = sids[i];
+      h_rows_[rows_cap_ + r] = ss.len + t;
+    }
+    last[i] = r - 1;
+    max_len = std::max(max_len, ss.len + lens[i]);
+  }
+  upload_table(s);
+  ORX_CHECK(cudaMemcpyAsync(d_rows_, h_rows_, sizeof(int) * 2 * rows_cap_, cudaMemcpyHostToDevice, s));
+  ORX_CHECK(cudaMemcpyAsync(x_, host_embeds, sizeof(float) * (size_t)total * kHidden,
+                            cudaMemcpyHostToDevice, s));
+  layers(total, max_len, false, s);
+  // final norm + lm_head on each session's last row -> first decoded token
+  std::memcpy(h_rows_ + 2 * rows_cap_, last.data(), sizeof(int) * n);
+  for (int i = 0; i < n; ++i) h_rows_[2 * rows_cap_ + n + i] = sids[i];
+  ORX_CHECK(cudaMemcpyAsync(d_tokens_, h_rows_ + 2 * rows_cap_, sizeof(int) * n,
+                            cudaMemcpyHostToDevice, s));
+  ORX_CHECK(cudaMemcpyAsync(d_out_, h_rows_ + 2 * rows_cap_ + n, sizeof(int) * n,
+                            cudaMemcpyHostToDevice, s));
+  launch_pdl(gather_rows, dim3(n), dim3(256), 0, s, (const float*)x_, (const int*)d_tokens_,
+             (float*)qkv_);
+  const auto& c = model->cfg;
+  launch_rmsnorm_bf16(qkv_, model->final_norm, xn_, n, c.rms_norm_eps, s);
+  run_proj(xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr, c.vocab_size,
+           &st_->err, model->num_sms, s);
+  launch_pdl(rows_argmax, dim3(n), dim3(1024), 0, s, (const float*)logits_, c.vocab_size,
+             (const int*)d_out_, d_next_tok_, (int*)nullptr);
+  ORX_CHECK(cudaGetLastError());
+  ORX_CHECK(cudaStreamSynchronize(s));  // h_rows_ is reused by the next call
+  for (int i = 0; i < n; ++i) sessions_[sids[i]].len += lens[i];
+}
+
+void BatchDecoder::step(const int* sids, int n, int* host_tokens_out, cudaStream_t s) {
+  if (n <= 0) return;
+  if (n > max_batch_) throw std::invalid_argument("batch larger than max_batch");
+  int max_len = 0;
+  for (int i = 0; i < n; ++i) {
+    check_sid(sids[i]);
+    if (sessions_[sids[i]].len <= 0) throw std::invalid_argument("session has no prefix");
+    if (!reserve(sids[i], sessions_[sids[i]].len + 1))
+      throw std::invalid_argument("KV page pool exhausted");
+  }
+  for (int i = 0; i < n; ++i) {
+    h_rows_[i] = sids[i];
+    h_rows_[rows_cap_ + i] = sessions_[sids[i]].len;
+    max_len = std::max(max_len, sessions_[sids[i]].len + 1);
+  }
+  upload_table(s);
+  ORX_CHECK(cudaMemcpyAsync(d_rows_, h_rows_, sizeof(int) * 2 * rows_cap_, cudaMemcpyHostToDevice, s));
+  ensure_logits(n);
+  launch_pdl(gather_tokens_embed, dim3(n), dim3(256), 0, s, (const int*)d_next_tok_,
+             (const int*)d_rows_, (const uint16_t*)model->embed, d_tokens_, x_);
+  layers(n, max_len, true, s);
+  const auto& c = model->cfg;
+  launch_rmsnorm_bf16(x_, model->final_norm, xn_, n, c.rms_norm_eps, s);
+  run_proj(xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr, c.vocab_size,
+           &st_->err, model->num_sms, s);
+  launch_pdl(rows_argmax, dim3(n), dim3(1024), 0, s, (const float*)logits_, c.vocab_size,
+             (const int*)d_rows_, d_next_tok_, d_out_);
+  ORX_CHECK(cudaGetLastError());
+  if (host_tokens_out) {
+    ORX_CHECK(cudaMemcpyAsync(h_rows_ + 2 * rows_cap_, d_out_, sizeof(int) * n,
+                              cudaMemcpyDeviceToHost, s));
+  }
+  ORX_CHECK(cudaStreamSynchronize(s));
+  if (host_tokens_out) std::memcpy(host_tokens_out, h_rows_ + 2 * rows_cap_, sizeof(int) * n);
+  for (int i = 0; i < n; ++i) sessions_[sids[i]].len += 1;
+}
+
+int BatchDecoder::device_error() const {
+  int e = 0;
+  ORX_CHECK(cudaMemcpy(&e, &st_->err, 4, cudaMemcpyDeviceToHost));
+  return e;
+}
+
+}  // namespace orx

@@ -155,4 +155,52 @@ class Decoder {
   bool embed_host_ready_ = false;
 };
 
+// Continuous-batching decoder over a shared paged KV pool (batch.cu).
+class BatchDecoder {
+ public:
+  BatchDecoder(Model* model, int max_sessions, int max_batch, int pool_pages,
+               int max_pages_per_session);
+  ~BatchDecoder();
+  int create_session();   // -1 when every slot is live
+  void free_session(int sid);
+  int cache_len(int sid) const;
+  void truncate(int sid, int len);
+  // Appends lens[i] rows of host embeddings (concatenated, [sum lens, 2048])
+  // to each session and leaves its next greedy token on the device.
+  void prefill(const int* sids, const int* lens, int n, const float* host_embeds, cudaStream_t s);
+  // One greedy token for each listed session (ragged lengths), batched.
+  void step(const int* sids, int n, int* host_tokens_out, cudaStream_t s);
+  int free_pages() const { return static_cast<int>(free_pages_.size()); }
+  int device_error() const;
+  Model* model;
+
+ private:
+  struct Session {
+    bool live = false;
+    int len = 0;
+    std::vector<int> pages;
+  };
+  void check_sid(int sid) const;
+  bool reserve(int sid, int new_len);
+  void upload_table(cudaStream_t s);
+  void ensure_rows(int rows);
+  void ensure_logits(int rows);
+  void layers(int rows, int max_len, bool fused, cudaStream_t s);
+
+  int max_sessions_, max_batch_, mps_;
+  KvPool* kv_ = nullptr;
+  std::vector<int> free_pages_;
+  std::vector<Session> sessions_;
+  std::vector<int> h_table_;
+  bool dirty_ = true;
+  int* d_table_ = nullptr;
+  int* d_next_tok_ = nullptr;
+  StepState* st_ = nullptr;
+  int* h_rows_ = nullptr;  // pinned staging
+  int rows_cap_ = 0, logits_cap_ = 0;
+  float *x_ = nullptr, *qkv_ = nullptr, *part_ = nullptr, *logits_ = nullptr;
+  uint16_t *xn_ = nullptr, *attn_ = nullptr, *act_ = nullptr;
+  int *counters_ = nullptr, *d_rows_ = nullptr, *d_tokens_ = nullptr, *d_out_ = nullptr;
+};
+
 }  // namespace orx
