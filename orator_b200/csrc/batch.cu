@@ -189,6 +189,18 @@ bool BatchDecoder::reserve(int sid, int new_len) {
   return true;
 }
 
+// Whether every session can grow by lens[i] rows (no allocation happens).
+bool BatchDecoder::fits(const int* sids, const int* lens, int n) const {
+  long long extra = 0;
+  for (int i = 0; i < n; ++i) {
+    const Session& s = sessions_[sids[i]];
+    const int need = (s.len + lens[i] + kPage - 1) / kPage;
+    if (need > mps_) return false;
+    extra += std::max(0, need - static_cast<int>(s.pages.size()));
+  }
+  return extra <= static_cast<long long>(free_pages_.size());
+}
+
 void BatchDecoder::upload_table(cudaStream_t st) {
   if (!dirty_) return;
   ORX_CHECK(cudaMemcpyAsync(d_table_, h_table_.data(), sizeof(int) * h_table_.size(),
@@ -211,7 +223,7 @@ void BatchDecoder::layers(int rows, int max_len, bool fused, cudaStream_t s) {
     const Model::Layer& L = model->layers[l];
     uint16_t* kvl = kv_->layer(l);
     launch_rmsnorm_bf16(x_, L.in_ln, xn_, rows, c.rms_norm_eps, s);
-    run_proj(xn_, L.qkv, kQkvDim, kHidden, rows, kEpiStore, qkv_, nullptr, kQkvDim, err, sms, s);
+    run_proj(gws_, xn_, L.qkv, kQkvDim, kHidden, rows, kEpiStore, qkv_, nullptr, kQkvDim, err, sms, s);
     if (!fused)
       launch_qk_norm_rope_store(qkv_, rows, L.q_norm, L.k_norm, model->rope_cos, model->rope_sin,
                                 kvl, d_table_, mps_, row_table, row_pos, 0, s);
@@ -236,10 +248,10 @@ void BatchDecoder::layers(int rows, int max_len, bool fused, cudaStream_t s) {
     a.out = attn_;
     a.err = err;
     launch_attention(a, s);
-    run_proj(attn_, L.o, kHidden, kQDim, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s);
+    run_proj(gws_, attn_, L.o, kHidden, kQDim, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s);
     launch_rmsnorm_bf16(x_, L.post_ln, xn_, rows, c.rms_norm_eps, s);
-    run_proj(xn_, L.gateup, 2 * kInter, kHidden, rows, kEpiSwiglu, nullptr, act_, kInter, err, sms, s);
-    run_proj(act_, L.down, kHidden, kInter, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s);
+    run_proj(gws_, xn_, L.gateup, 2 * kInter, kHidden, rows, kEpiSwiglu, nullptr, act_, kInter, err, sms, s);
+    run_proj(gws_, act_, L.down, kHidden, kInter, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s);
   }
 }
 
@@ -255,9 +267,8 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
     total += lens[i];
   }
   if (total > 65536 / 2) throw std::invalid_argument("too many prefill rows in one call");
-  for (int i = 0; i < n; ++i)
-    if (!reserve(sids[i], sessions_[sids[i]].len + lens[i]))
-      throw std::invalid_argument("KV page pool exhausted");
+  if (!fits(sids, lens, n)) throw std::invalid_argument("KV page pool exhausted");
+  for (int i = 0; i < n; ++i) reserve(sids[i], sessions_[sids[i]].len + lens[i]);
   ensure_rows(std::max(total, n));
   ensure_logits(n);
   // rows: [row_table (rows_cap_) | row_pos (rows_cap_)], then the last-row list
@@ -288,7 +299,7 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
              (float*)qkv_);
   const auto& c = model->cfg;
   launch_rmsnorm_bf16(qkv_, model->final_norm, xn_, n, c.rms_norm_eps, s);
-  run_proj(xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr, c.vocab_size,
+  run_proj(gws_, xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr, c.vocab_size,
            &st_->err, model->num_sms, s);
   launch_pdl(rows_argmax, dim3(n), dim3(1024), 0, s, (const float*)logits_, c.vocab_size,
              (const int*)d_out_, d_next_tok_, (int*)nullptr);
@@ -304,9 +315,12 @@ void BatchDecoder::step(const int* sids, int n, int* host_tokens_out, cudaStream
   for (int i = 0; i < n; ++i) {
     check_sid(sids[i]);
     if (sessions_[sids[i]].len <= 0) throw std::invalid_argument("session has no prefix");
-    if (!reserve(sids[i], sessions_[sids[i]].len + 1))
-      throw std::invalid_argument("KV page pool exhausted");
   }
+  {
+    std::vector<int> ones(n, 1);
+    if (!fits(sids, ones.data(), n)) throw std::invalid_argument("KV page pool exhausted");
+  }
+  for (int i = 0; i < n; ++i) reserve(sids[i], sessions_[sids[i]].len + 1);
   for (int i = 0; i < n; ++i) {
     h_rows_[i] = sids[i];
     h_rows_[rows_cap_ + i] = sessions_[sids[i]].len;
@@ -320,7 +334,7 @@ void BatchDecoder::step(const int* sids, int n, int* host_tokens_out, cudaStream
   layers(n, max_len, true, s);
   const auto& c = model->cfg;
   launch_rmsnorm_bf16(x_, model->final_norm, xn_, n, c.rms_norm_eps, s);
-  run_proj(xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr, c.vocab_size,
+  run_proj(gws_, xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr, c.vocab_size,
            &st_->err, model->num_sms, s);
   launch_pdl(rows_argmax, dim3(n), dim3(1024), 0, s, (const float*)logits_, c.vocab_size,
              (const int*)d_rows_, d_next_tok_, d_out_);

@@ -12,18 +12,30 @@ namespace orx {
 
 // Projection on the tcgen05 GEMM with split-K chosen so that about one wave
 // of CTAs covers the SMs (the short projections o / down / qkv at small T).
-void run_proj(const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi, float* out_f32,
-              uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s) {
+GemmWs::~GemmWs() {
+  if (ws) cudaFree(ws);
+  if (cnt) cudaFree(cnt);
+}
+
+void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi,
+              float* out_f32, uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s) {
   if (T <= 0) return;
   const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   const int tiles = (N / 128) * ((T + bn - 1) / bn);
   int splits = 1;
-  if (epi != kEpiSwiglu)
-    while (tiles * splits * 2 <= num_sms && (K % (64 * splits * 2)) == 0 && K / (splits * 2) >= 256)
-      splits *= 2;
-  if (epi == kEpiStore && splits > 1)
-    ORX_CHECK(cudaMemsetAsync(out_f32, 0, sizeof(float) * (size_t)T * ldo, s));
-  TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err};
+  while (epi != kEpiSwiglu && tiles * splits * 2 <= num_sms && (K % (64 * splits * 2)) == 0 && K / (splits * 2) >= 256)
+    splits *= 2;
+  TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err, nullptr, nullptr};
+  if (splits > 1) {
+    const size_t need = (size_t)splits * T * N;
+    if (need > w.cap) {
+      ORX_CHECK(cudaStreamSynchronize(s));
+      if (w.ws) cudaFree(w.ws);
+      w.ws = dalloc<float>(need);
+      w.cap = need;
+    }
+    g.ws = w.ws;
+  }
   launch_gemm_tc(X, W, g, splits, s);
 }
 
@@ -137,7 +149,7 @@ void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
     const Model::Layer& L = model->layers[l];
     uint16_t* kvl = kv_->layer(l);
     launch_rmsnorm_bf16(px_, L.in_ln, pxn_, T, c.rms_norm_eps, s);
-    run_proj(pxn_, L.qkv, kQkvDim, kHidden, T, kEpiStore, pqkv_, nullptr, kQkvDim, &st_->err, model->num_sms, s);
+    run_proj(gws_, pxn_, L.qkv, kQkvDim, kHidden, T, kEpiStore, pqkv_, nullptr, kQkvDim, &st_->err, model->num_sms, s);
     launch_qk_norm_rope_store(pqkv_, T, L.q_norm, L.k_norm, model->rope_cos, model->rope_sin,
                               kvl, page_table_, max_pages_, nullptr, nullptr, pos0, s);
     AttnArgs a = {};
@@ -159,10 +171,10 @@ void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
     a.out = pattn_;
     a.err = &st_->err;
     launch_attention(a, s);
-    run_proj(pattn_, L.o, kHidden, kQDim, T, kEpiResid, px_, nullptr, kHidden, &st_->err, model->num_sms, s);
+    run_proj(gws_, pattn_, L.o, kHidden, kQDim, T, kEpiResid, px_, nullptr, kHidden, &st_->err, model->num_sms, s);
     launch_rmsnorm_bf16(px_, L.post_ln, pxn_, T, c.rms_norm_eps, s);
-    run_proj(pxn_, L.gateup, 2 * kInter, kHidden, T, kEpiSwiglu, nullptr, pact_, kInter, &st_->err, model->num_sms, s);
-    run_proj(pact_, L.down, kHidden, kInter, T, kEpiResid, px_, nullptr, kHidden, &st_->err, model->num_sms, s);
+    run_proj(gws_, pxn_, L.gateup, 2 * kInter, kHidden, T, kEpiSwiglu, nullptr, pact_, kInter, &st_->err, model->num_sms, s);
+    run_proj(gws_, pact_, L.down, kHidden, kInter, T, kEpiResid, px_, nullptr, kHidden, &st_->err, model->num_sms, s);
   }
   // Final norm of the last row + tied lm_head (+ argmax into the step state).
   GemvArgs g = {};

@@ -37,8 +37,16 @@ struct ModelConfig {
 // Device-resident weights of the 28-layer decoder (layout chosen for the
 // streaming GEMV and the GEMM epilogues; see set_tensor for the mapping from
 // the reference's thinker.model.* tensors).
-void run_proj(const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi, float* out_f32,
-              uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s);
+// Split-K workspace of one stream's projections (grown on demand).
+struct GemmWs {
+  float* ws = nullptr;
+  size_t cap = 0;
+  int* cnt = nullptr;
+  int cnt_cap = 0;
+  ~GemmWs();
+};
+void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi,
+              float* out_f32, uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s);
 
 class Model {
  public:
@@ -151,6 +159,7 @@ class Decoder {
   float* h_stage_ = nullptr;
   size_t h_stage_cap_ = 0;
   cudaGraphExec_t g1_ = nullptr, gk_ = nullptr;
+  GemmWs gws_;
   std::vector<uint16_t> embed_host_;
   bool embed_host_ready_ = false;
 };
@@ -182,6 +191,7 @@ class BatchDecoder {
   };
   void check_sid(int sid) const;
   bool reserve(int sid, int new_len);
+  bool fits(const int* sids, const int* lens, int n) const;
   void upload_table(cudaStream_t s);
   void ensure_rows(int rows);
   void ensure_logits(int rows);
@@ -201,6 +211,7 @@ class BatchDecoder {
   float *x_ = nullptr, *qkv_ = nullptr, *part_ = nullptr, *logits_ = nullptr;
   uint16_t *xn_ = nullptr, *attn_ = nullptr, *act_ = nullptr;
   int *counters_ = nullptr, *d_rows_ = nullptr, *d_tokens_ = nullptr, *d_out_ = nullptr;
+  GemmWs gws_;
 };
 
 }  // namespace orx

@@ -20,6 +20,7 @@
 // No TMA multicast anywhere: every CTA loads its own tiles.
 #include <cuda.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 #include <utility>
@@ -168,9 +169,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const int row = m0 + warp * 32 + lane;
   const uint32_t tbase = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  for (int c0 = 0; c0 < BN; c0 += 32) {
-    float v[32];
-    tmem_ld32(tbase + c0, v);
+  // Epilogue on 32 columns (tokens n0 + c0 .. +31) of this thread's weight row.
+  auto epilogue = [&](const float* v, int c0) {
     if (g.epi == kEpiSwiglu) {
       __syncthreads();
       if (warp >= 2) {
@@ -195,13 +195,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int t = n0 + c0 + i;
         if (c0 + i < BN && t < g.T) {
           float* o = g.out_f32 + (long long)t * g.ldo + row;
-          if (gridDim.z > 1)
-            atomicAdd(o, v[i]);
-          else if (g.epi == kEpiResid)
+          if (g.epi == kEpiResid)
             *o += v[i];
           else
             *o = v[i];
         }
+      }
+    }
+  };
+  if (gridDim.z == 1) {
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      float v[32];
+      tmem_ld32(tbase + c0, v);
+      epilogue(v, c0);
+    }
+  } else {
+    // Split over K: each split stores its partial tile to the workspace;
+    // splitk_reduce_kernel sums them in split order (deterministic) and runs
+    // the epilogue.
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      float v[32];
+      tmem_ld32(tbase + c0, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int t = n0 + c0 + i;
+        if (c0 + i < BN && t < g.T) g.ws[((long long)blockIdx.z * g.T + t) * g.N + row] = v[i];
       }
     }
   }
@@ -244,6 +262,20 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, int K, int box_r
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+__global__ void splitk_reduce_kernel(TcArgs g, int splits) {
+  pdl_trigger();
+  pdl_wait();
+  const long long n = (long long)g.T * g.N;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int z = 0; z < splits; ++z) acc += g.ws[z * n + i];
+    const long long t = i / g.N, row = i % g.N;
+    float* o = g.out_f32 + t * g.ldo + row;
+    if (g.epi == kEpiResid) *o += acc; else *o = acc;
+  }
+}
+
 template <int BN, int STAGES>
 void launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& g, int splits,
                cudaStream_t s) {
@@ -277,6 +309,11 @@ void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int s
     case 64: launch_bn<64, 6>(mw, mx, g, splits, s); break;
     case 128: launch_bn<128, 6>(mw, mx, g, splits, s); break;
     default: launch_bn<256, 4>(mw, mx, g, splits, s); break;
+  }
+  if (splits > 1) {
+    const long long n = (long long)g.T * g.N;
+    const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, 148 * 16));
+    launch_pdl(splitk_reduce_kernel, dim3(grid), dim3(256), 0, s, g, splits);
   }
 }
 

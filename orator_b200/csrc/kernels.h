@@ -106,10 +106,12 @@ void launch_gemm(const GemmArgs& a, cudaStream_t s);
 struct TcArgs {
   int N, K, T;         // weight rows (multiple of 128), depth (multiple of 64 * splits), tokens
   int epi;             // kEpiStore / kEpiResid / kEpiSwiglu
-  float* out_f32;      // [T, ldo]; split-K accumulates atomically (zero it for kEpiStore)
+  float* out_f32;      // [T, ldo]
   uint16_t* out_bf16;  // SwiGLU output [T, ldo]
   int ldo;
   int* err;
+  float* ws;           // split-K partials [splits, T, N]
+  int* unused;
 };
 // X: [T, K] bf16 row-major (device), W: [N, K] bf16. splits divides K / 64.
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
