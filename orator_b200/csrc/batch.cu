@@ -11,6 +11,8 @@
 // device page table.
 #include <algorithm>
 #include <cstring>
+#include <map>
+#include <set>
 
 #include "common.cuh"
 #include "engine.h"
@@ -92,6 +94,13 @@ BatchDecoder::BatchDecoder(Model* m, int max_sessions, int max_batch, int pool_p
   StepState init = {};
   ORX_CHECK(cudaMemcpy(st_, &init, sizeof(init), cudaMemcpyHostToDevice));
   ORX_CHECK(cudaMallocHost(&h_rows_, sizeof(int) * 2 * 65536));
+  for (int b = 0; b < 2; ++b) {
+    ORX_CHECK(cudaMallocHost(&h_step_[b], sizeof(int) * 2 * max_batch));
+    ORX_CHECK(cudaMallocHost(&h_tbl_[b], sizeof(int) * h_table_.size()));
+    ORX_CHECK(cudaEventCreateWithFlags(&ev_rows_[b], cudaEventDisableTiming));
+    ORX_CHECK(cudaEventCreateWithFlags(&ev_table_[b], cudaEventDisableTiming));
+  }
+  ORX_CHECK(cudaMallocHost(&h_out_, sizeof(int) * max_batch));
   ensure_rows(max_batch);
 }
 
@@ -102,10 +111,19 @@ BatchDecoder::~BatchDecoder() {
                   (void*)d_rows_, (void*)d_tokens_, (void*)d_out_})
     if (p) cudaFree(p);
   if (h_rows_) cudaFreeHost(h_rows_);
+  for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+  for (int b = 0; b < 2; ++b) {
+    if (h_step_[b]) cudaFreeHost(h_step_[b]);
+    if (h_tbl_[b]) cudaFreeHost(h_tbl_[b]);
+    if (ev_rows_[b]) cudaEventDestroy(ev_rows_[b]);
+    if (ev_table_[b]) cudaEventDestroy(ev_table_[b]);
+  }
+  if (h_out_) cudaFreeHost(h_out_);
 }
 
 void BatchDecoder::ensure_rows(int rows) {
   if (rows <= rows_cap_) return;
+  cudaDeviceSynchronize();
   const int cap = std::max(rows, 64);
   for (void* p : {(void*)x_, (void*)xn_, (void*)qkv_, (void*)attn_, (void*)act_, (void*)part_,
                   (void*)counters_, (void*)d_rows_, (void*)d_tokens_, (void*)d_out_})
@@ -123,13 +141,16 @@ void BatchDecoder::ensure_rows(int rows) {
   d_tokens_ = dalloc<int>(cap);
   d_out_ = dalloc<int>(cap);
   rows_cap_ = cap;
+  ++buf_gen_;
 }
 
 void BatchDecoder::ensure_logits(int rows) {
   if (rows <= logits_cap_) return;
+  cudaDeviceSynchronize();
   if (logits_) cudaFree(logits_);
   logits_ = dalloc<float>((size_t)rows * model->cfg.vocab_size);
   logits_cap_ = rows;
+  ++buf_gen_;
 }
 
 int BatchDecoder::create_session() {
@@ -203,9 +224,12 @@ bool BatchDecoder::fits(const int* sids, const int* lens, int n) const {
 
 void BatchDecoder::upload_table(cudaStream_t st) {
   if (!dirty_) return;
-  ORX_CHECK(cudaMemcpyAsync(d_table_, h_table_.data(), sizeof(int) * h_table_.size(),
+  const int b = table_count_++ & 1;
+  ORX_CHECK(cudaEventSynchronize(ev_table_[b]));  // that staging copy has been consumed
+  std::memcpy(h_tbl_[b], h_table_.data(), sizeof(int) * h_table_.size());
+  ORX_CHECK(cudaMemcpyAsync(d_table_, h_tbl_[b], sizeof(int) * h_table_.size(),
                             cudaMemcpyHostToDevice, st));
-  ORX_CHECK(cudaStreamSynchronize(st));  // h_table_ is pageable and may change next call
+  ORX_CHECK(cudaEventRecord(ev_table_[b], st));
   dirty_ = false;
 }
 
@@ -308,44 +332,87 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
   for (int i = 0; i < n; ++i) sessions_[sids[i]].len += lens[i];
 }
 
+// Kernels of one decode step for n rows whose (session, position) are in
+// d_rows_; every varying input lives in device memory, so the sequence is
+// captured once per batch size and replayed as a CUDA graph.
+void BatchDecoder::record_step(int n, cudaStream_t s) {
+  launch_pdl(gather_tokens_embed, dim3(n), dim3(256), 0, s, (const int*)d_next_tok_,
+             (const int*)d_rows_, (const uint16_t*)model->embed, d_tokens_, x_);
+  layers(n, mps_ * kPage, true, s);
+  const auto& c = model->cfg;
+  launch_rmsnorm_bf16(x_, model->final_norm, xn_, n, c.rms_norm_eps, s);
+  run_proj(gws_, xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr,
+           c.vocab_size, &st_->err, model->num_sms, s);
+  launch_pdl(rows_argmax, dim3(n), dim3(1024), 0, s, (const float*)logits_, c.vocab_size,
+             (const int*)d_rows_, d_next_tok_, d_out_);
+}
+
 void BatchDecoder::step(const int* sids, int n, int* host_tokens_out, cudaStream_t s) {
   if (n <= 0) return;
   if (n > max_batch_) throw std::invalid_argument("batch larger than max_batch");
-  int max_len = 0;
   for (int i = 0; i < n; ++i) {
     check_sid(sids[i]);
     if (sessions_[sids[i]].len <= 0) throw std::invalid_argument("session has no prefix");
+    for (int j = 0; j < i; ++j)
+      if (sids[j] == sids[i]) throw std::invalid_argument("session listed twice");
   }
   {
     std::vector<int> ones(n, 1);
     if (!fits(sids, ones.data(), n)) throw std::invalid_argument("KV page pool exhausted");
   }
   for (int i = 0; i < n; ++i) reserve(sids[i], sessions_[sids[i]].len + 1);
-  for (int i = 0; i < n; ++i) {
-    h_rows_[i] = sids[i];
-    h_rows_[rows_cap_ + i] = sessions_[sids[i]].len;
-    max_len = std::max(max_len, sessions_[sids[i]].len + 1);
-  }
+  ensure_logits(max_batch_);
   upload_table(s);
-  ORX_CHECK(cudaMemcpyAsync(d_rows_, h_rows_, sizeof(int) * 2 * rows_cap_, cudaMemcpyHostToDevice, s));
-  ensure_logits(n);
-  launch_pdl(gather_tokens_embed, dim3(n), dim3(256), 0, s, (const int*)d_next_tok_,
-             (const int*)d_rows_, (const uint16_t*)model->embed, d_tokens_, x_);
-  layers(n, max_len, true, s);
-  const auto& c = model->cfg;
-  launch_rmsnorm_bf16(x_, model->final_norm, xn_, n, c.rms_norm_eps, s);
-  run_proj(gws_, xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr, c.vocab_size,
-           &st_->err, model->num_sms, s);
-  launch_pdl(rows_argmax, dim3(n), dim3(1024), 0, s, (const float*)logits_, c.vocab_size,
-             (const int*)d_rows_, d_next_tok_, d_out_);
-  ORX_CHECK(cudaGetLastError());
-  if (host_tokens_out) {
-    ORX_CHECK(cudaMemcpyAsync(h_rows_ + 2 * rows_cap_, d_out_, sizeof(int) * n,
-                              cudaMemcpyDeviceToHost, s));
+  // double-buffered pinned staging: wait only for the copy issued two steps ago
+  const int b = step_count_ & 1;
+  ORX_CHECK(cudaEventSynchronize(ev_rows_[b]));
+  int* stage = h_step_[b];
+  for (int i = 0; i < n; ++i) {
+    stage[i] = sids[i];
+    stage[max_batch_ + i] = sessions_[sids[i]].len;
   }
-  ORX_CHECK(cudaStreamSynchronize(s));
-  if (host_tokens_out) std::memcpy(host_tokens_out, h_rows_ + 2 * rows_cap_, sizeof(int) * n);
+  ORX_CHECK(cudaMemcpyAsync(d_rows_, stage, sizeof(int) * n, cudaMemcpyHostToDevice, s));
+  ORX_CHECK(cudaMemcpyAsync(d_rows_ + rows_cap_, stage + max_batch_, sizeof(int) * n,
+                            cudaMemcpyHostToDevice, s));
+  ORX_CHECK(cudaEventRecord(ev_rows_[b], s));
+  ++step_count_;
+
+  auto it = graphs_.find(n);
+  const bool stale = it != graphs_.end() && (graph_ws_ != gws_.ws || graph_gen_ != buf_gen_);
+  if (stale) {
+    for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+    graphs_.clear();
+    it = graphs_.end();
+  }
+  if (it == graphs_.end() && warmed_.count(n) == 0) {
+    record_step(n, s);  // eager first run sizes every buffer
+    warmed_.insert(n);
+  } else {
+    if (it == graphs_.end()) {
+      ORX_CHECK(cudaStreamSynchronize(s));
+      cudaStream_t cs;
+      ORX_CHECK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+      ORX_CHECK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+      record_step(n, cs);
+      cudaGraph_t g;
+      ORX_CHECK(cudaStreamEndCapture(cs, &g));
+      cudaGraphExec_t e;
+      ORX_CHECK(cudaGraphInstantiate(&e, g, 0));
+      ORX_CHECK(cudaGraphDestroy(g));
+      ORX_CHECK(cudaStreamDestroy(cs));
+      it = graphs_.emplace(n, e).first;
+      graph_ws_ = gws_.ws;
+      graph_gen_ = buf_gen_;
+    }
+    ORX_CHECK(cudaGraphLaunch(it->second, s));
+  }
+  ORX_CHECK(cudaGetLastError());
   for (int i = 0; i < n; ++i) sessions_[sids[i]].len += 1;
+  if (host_tokens_out) {
+    ORX_CHECK(cudaMemcpyAsync(h_out_, d_out_, sizeof(int) * n, cudaMemcpyDeviceToHost, s));
+    ORX_CHECK(cudaStreamSynchronize(s));
+    std::memcpy(host_tokens_out, h_out_, sizeof(int) * n);
+  }
 }
 
 int BatchDecoder::device_error() const {

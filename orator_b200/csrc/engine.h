@@ -5,6 +5,8 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <map>
+#include <set>
 #include <vector>
 
 #include <cuda_runtime.h>
@@ -196,6 +198,7 @@ class BatchDecoder {
   void ensure_rows(int rows);
   void ensure_logits(int rows);
   void layers(int rows, int max_len, bool fused, cudaStream_t s);
+  void record_step(int n, cudaStream_t s);
 
   int max_sessions_, max_batch_, mps_;
   KvPool* kv_ = nullptr;
@@ -212,6 +215,16 @@ class BatchDecoder {
   uint16_t *xn_ = nullptr, *attn_ = nullptr, *act_ = nullptr;
   int *counters_ = nullptr, *d_rows_ = nullptr, *d_tokens_ = nullptr, *d_out_ = nullptr;
   GemmWs gws_;
+  int* h_step_[2] = {nullptr, nullptr};
+  int* h_tbl_[2] = {nullptr, nullptr};
+  int* h_out_ = nullptr;
+  cudaEvent_t ev_rows_[2] = {nullptr, nullptr};
+  cudaEvent_t ev_table_[2] = {nullptr, nullptr};
+  long long step_count_ = 0, table_count_ = 0;
+  std::map<int, cudaGraphExec_t> graphs_;
+  std::set<int> warmed_;
+  float* graph_ws_ = nullptr;
+  long long graph_gen_ = -1, buf_gen_ = 0;
 };
 
 }  // namespace orx
