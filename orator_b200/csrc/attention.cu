@@ -25,7 +25,7 @@ constexpr int kKRow = kHeadDim * 2 + 16;  // padded K row in shared memory (byte
 constexpr int kKTile = kPage * kKRow;     // 4352
 constexpr int kVTile = kPage * kHeadDim * 2;  // 4096
 constexpr int kGroupBytes = kAttnWarps * (kKTile + kVTile);
-constexpr int kAttnSmem = kGroupBytes + 128;
+constexpr int kAttnSmem = 2 * kGroupBytes + 128;  // double-buffered page groups
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
@@ -145,18 +145,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   const int r = lane & 15, hh = lane >> 4;
+  // Page groups of kAttnWarps pages, double-buffered: group i+1 is in flight
+  // while group i is consumed.
+  if (staged_end < (pb + kAttnWarps < pe ? pb + kAttnWarps : pe)) {
+    const int g1 = pb + kAttnWarps < pe ? pb + kAttnWarps : pe;
+    stage_pages(sm + (staged_end - pb) * (kKTile + kVTile), a.kv_layer, pt, h, staged_end, g1, t);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
   for (int g0 = pb; g0 < pe; g0 += kAttnWarps) {
     const int g1 = g0 + kAttnWarps < pe ? g0 + kAttnWarps : pe;
-    if (g0 != pb) __syncthreads();  // previous group fully consumed
-    if (g0 != pb || staged_end < g1) {
-      const int from = (g0 == pb) ? staged_end : g0;
-      stage_pages(sm + (from - g0) * (kKTile + kVTile), a.kv_layer, pt, h, from, g1, t);
+    uint8_t* buf = sm + (((g0 - pb) / kAttnWarps) & 1) * kGroupBytes;
+    const bool more = g1 < pe;
+    if (more) {
+      const int n0 = g1, n1 = g1 + kAttnWarps < pe ? g1 + kAttnWarps : pe;
+      stage_pages(sm + ((((g0 - pb) / kAttnWarps) + 1) & 1) * kGroupBytes, a.kv_layer, pt, h, n0,
+                  n1, t);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
-    cp_async_wait_all();
     __syncthreads();  // every thread's copies of this group have landed
     if (owner && warp == 2 && g1 == pe) {
       // the staged copy of the newest slot may predate this step: patch it
-      uint8_t* base = sm + (pos / kPage - g0) * (kKTile + kVTile);
+      uint8_t* base = buf + (pos / kPage - g0) * (kKTile + kVTile);
       uint16_t* kd = reinterpret_cast<uint16_t*>(base + (pos % kPage) * kKRow);
       uint16_t* vd = reinterpret_cast<uint16_t*>(base + kKTile + (pos % kPage) * kHeadDim * 2);
 #pragma unroll
@@ -168,7 +180,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
     __syncthreads();
     const int p = g0 + warp;
     if (p < g1) {
-      const uint8_t* base = sm + warp * (kKTile + kVTile);
+      const uint8_t* base = buf + warp * (kKTile + kVTile);
       const uint4* krow = reinterpret_cast<const uint4*>(base + r * kKRow);
       const uint16_t* V = reinterpret_cast<const uint16_t*>(base + kKTile);
       float d4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -223,6 +235,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
         }
       }
     }
+    __syncthreads();  // this buffer is restaged two groups later
   }
   if (lane == 0) {
     sm_m[warp][0] = m[0]; sm_m[warp][1] = m[1];

@@ -20,7 +20,7 @@
 namespace orx {
 
 namespace {
-constexpr int kSplitPages = 8;
+constexpr int kSplitPages = 32;  // pages per attention split (4 double-buffered groups)
 constexpr int kPartFloats = 2 * 132;
 
 // tokens[r] = next_tok[row_table[r]]; x[r] = embed[tokens[r]] (fp32).

@@ -22,8 +22,10 @@ void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int
   if (T <= 0) return;
   const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   const int tiles = (N / 128) * ((T + bn - 1) / bn);
+  // about two CTAs per SM, at least 256 of K per split
   int splits = 1;
-  while (epi != kEpiSwiglu && tiles * splits * 2 <= num_sms && (K % (64 * splits * 2)) == 0 && K / (splits * 2) >= 256)
+  while (tiles * splits * 2 <= 2 * num_sms && (K % (64 * splits * 2)) == 0 &&
+         K / (splits * 2) >= 256)
     splits *= 2;
   TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err, nullptr, nullptr};
   if (splits > 1) {
@@ -164,8 +166,8 @@ void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
     a.rows = T;
     a.fused_kv = 0;
     // splits needed by the longest row (position pos0 + T - 1)
-    a.nsplit_max = ((pos0 + T + kPage - 1) / kPage + kDecodePagesPerSplit - 1) / kDecodePagesPerSplit;
-    a.pages_per_split = kDecodePagesPerSplit;
+    a.nsplit_max = ((pos0 + T + kPage - 1) / kPage + 31) / 32;
+    a.pages_per_split = 32;
     a.part = ppart_;
     a.counters = pcounters_;
     a.out = pattn_;

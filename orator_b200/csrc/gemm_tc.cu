@@ -276,6 +276,26 @@ __global__ void splitk_reduce_kernel(TcArgs g, int splits) {
   }
 }
 
+// SwiGLU after split-K: output j of token t pairs gate row (j/64)*128 + j%64
+// with the up row 64 further in the same 128-row tile.
+__global__ void splitk_swiglu_kernel(TcArgs g, int splits) {
+  pdl_trigger();
+  pdl_wait();
+  const long long n = (long long)g.T * g.N, half = (long long)g.T * (g.N / 2);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < half;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long t = i / (g.N / 2);
+    const int j = static_cast<int>(i % (g.N / 2));
+    const long long gr = t * g.N + (j >> 6) * 128 + (j & 63);
+    float gt = 0.f, up = 0.f;
+    for (int z = 0; z < splits; ++z) {
+      gt += g.ws[z * n + gr];
+      up += g.ws[z * n + gr + 64];
+    }
+    g.out_bf16[t * g.ldo + j] = f2bf((gt / (1.0f + expf(-gt))) * up);
+  }
+}
+
 template <int BN, int STAGES>
 void launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& g, int splits,
                cudaStream_t s) {
@@ -306,14 +326,17 @@ void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int s
   switch (bn) {
     case 16: launch_bn<16, 8>(mw, mx, g, splits, s); break;
     case 32: launch_bn<32, 8>(mw, mx, g, splits, s); break;
-    case 64: launch_bn<64, 6>(mw, mx, g, splits, s); break;
+    case 64: launch_bn<64, 4>(mw, mx, g, splits, s); break;
     case 128: launch_bn<128, 6>(mw, mx, g, splits, s); break;
     default: launch_bn<256, 4>(mw, mx, g, splits, s); break;
   }
   if (splits > 1) {
     const long long n = (long long)g.T * g.N;
     const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, 148 * 16));
-    launch_pdl(splitk_reduce_kernel, dim3(grid), dim3(256), 0, s, g, splits);
+    if (g.epi == kEpiSwiglu)
+      launch_pdl(splitk_swiglu_kernel, dim3(grid), dim3(256), 0, s, g, splits);
+    else
+      launch_pdl(splitk_reduce_kernel, dim3(grid), dim3(256), 0, s, g, splits);
   }
 }
 
