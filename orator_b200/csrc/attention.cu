@@ -17,21 +17,32 @@
 namespace orx {
 namespace {
 
-constexpr int kAttnWarps = 8;          // one page per warp per group
+constexpr int kAttnWarps = 4;          // one page per warp per group
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kPartStride = 2 * 132;   // per split: 2 heads x (128 acc, m, l, pad)
 constexpr int kMaxSplits = 128;        // 2 * kMaxSplits <= threads
-constexpr int kKRow = kHeadDim * 2 + 16;  // padded K row in shared memory (bytes)
-constexpr int kKTile = kPage * kKRow;     // 4352
-constexpr int kVTile = kPage * kHeadDim * 2;  // 4096
+constexpr int kKRow = kHeadDim * 2;       // K / V row in shared memory (bytes)
+constexpr int kKTile = kPage * kKRow;     // 4 KiB: one (page, kv head) K tile, as in HBM
+constexpr int kVTile = kPage * kKRow;
 constexpr int kGroupBytes = kAttnWarps * (kKTile + kVTile);
 constexpr int kAttnSmem = 2 * kGroupBytes + 128;  // double-buffered page groups
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n cp.async.wait_all;" ::: "memory");
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  return static_cast<uint32_t>(f2bf(lo)) | (static_cast<uint32_t>(f2bf(hi)) << 16);
+}
+// bf16 part of x for rows 0-1 (hi) or its remainder for rows 2-3 (lo):
+// hi + lo represents x to about 2^-16 relative, so bf16 MMAs give fp32-grade dots.
+__device__ __forceinline__ float split_part(float x, bool lo) {
+  const float h = bf2f(f2bf(x));
+  return lo ? x - h : h;
 }
 
 // RMSNorm (eps 1e-6) + rotate-half RoPE of one 128-wide head held by a warp:
@@ -52,19 +63,17 @@ __device__ __forceinline__ void head_norm_rope(float v[4], const float* w, const
   }
 }
 
-// Stage pages [g0, g1) (at most kAttnWarps) of kv head h into shared memory.
+// Stage pages [g0, g1) (at most kAttnWarps) of kv head h: one 1-D bulk copy
+// (TMA engine) per 4 KiB K or V tile, completion counted on `bar`. Called by
+// one thread; arrives on `bar` with the byte count.
 __device__ __forceinline__ void stage_pages(uint8_t* sm, const uint16_t* kv, const int* pt,
-                                            int h, int g0, int g1, int t) {
-  const int n = (g1 - g0) * 2 * kPage * 16;  // 16-byte pieces (K and V)
-  for (int i = t; i < n; i += kAttnThreads) {
-    const int pg = i / (2 * kPage * 16), rem = i % (2 * kPage * 16);
-    const int isv = rem / (kPage * 16), r = (rem / 16) % kPage, c = rem % 16;
-    const uint16_t* src = kv + (long long)pt[g0 + pg] * kPageElems + (isv ? kHalfPageElems : 0) +
-                          (h * kPage + r) * kHeadDim + c * 8;
-    uint8_t* base = sm + pg * (kKTile + kVTile);
-    const uint32_t dst = smem_u32(isv ? base + kKTile + r * kHeadDim * 2 + c * 16
-                                      : base + r * kKRow + c * 16);
-    cp_async16(dst, src);
+                                            int h, int g0, int g1, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, static_cast<uint32_t>((g1 - g0) * (kKTile + kVTile)));
+  for (int p = g0; p < g1; ++p) {
+    const uint16_t* src = kv + (long long)pt[p] * kPageElems + h * kPage * kHeadDim;
+    uint8_t* base = sm + (p - g0) * (kKTile + kVTile);
+    bulk_g2s(base, src, kKTile, bar);
+    bulk_g2s(base + kKTile, src + kHalfPageElems, kVTile, bar);
   }
 }
 
@@ -74,7 +83,7 @@ __device__ __forceinline__ void stage_pages(uint8_t* sm, const uint16_t* kv, con
 // griddepcontrol.wait using a speculative read of the position: cache entries
 // older than the current position never change, and the one page that may be
 // missing (when the position just crossed a page) is fetched after the wait.
-__global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   extern __shared__ uint8_t attn_smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(attn_smem_raw) + 127) & ~uintptr_t(127));
@@ -86,16 +95,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
   const int* pt = a.page_table + (long long)tab * a.max_pages;
   const int* pos_ptr = a.pos_scalar ? a.pos_scalar : (a.row_pos ? a.row_pos + row : nullptr);
   const int pb = split * P;
-  int staged_end = pb;  // pages [pb, staged_end) already requested
-  if (a.fused_kv && pos_ptr) {
-    const int pos_g = *reinterpret_cast<const volatile int*>(pos_ptr);
-    int e = (pos_g + kPage) / kPage;
-    e = e < pb + P ? e : pb + P;
-    e = e < pb + kAttnWarps ? e : pb + kAttnWarps;
-    if (e > pb && e <= a.max_pages) {
-      stage_pages(sm, a.kv_layer, pt, h, pb, e, t);
-      staged_end = e;
+  // bar[0]: first group (2 arrivals: speculative + completion), bar[1], bar[2]:
+  // later groups in buffers 0 / 1 (1 arrival each).
+  __shared__ uint64_t bar[3];
+  __shared__ int staged_end_s;
+  if (t == 0) {
+    mbar_init(&bar[0], 2);
+    mbar_init(&bar[1], 1);
+    mbar_init(&bar[2], 1);
+    fence_mbar_init();
+    int e = pb;
+    if (a.fused_kv && pos_ptr) {
+      const int pos_g = *reinterpret_cast<const volatile int*>(pos_ptr);
+      e = (pos_g + kPage) / kPage;
+      e = e < pb + P ? e : pb + P;
+      e = e < pb + kAttnWarps ? e : pb + kAttnWarps;
+      if (e < pb || e > a.max_pages) e = pb;
     }
+    stage_pages(sm, a.kv_layer, pt, h, pb, e, &bar[0]);  // e == pb: arrival only
+    staged_end_s = e;
   }
   pdl_trigger();
   pdl_wait();
@@ -103,8 +121,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
   const int pos = pos_ptr ? *pos_ptr : a.pos_base + row;
   const int npages = (pos + kPage) / kPage;  // pages holding positions [0, pos]
   const int nsplit = (npages + P - 1) / P;
+  __syncthreads();
+  const int staged_end = staged_end_s;
   if (split >= nsplit) {
-    cp_async_wait_all();
+    if (t == 0) {  // do not leave with copies in flight
+      mbar_arrive_expect_tx(&bar[0], 0);
+      mbar_wait(&bar[0], 0, a.err, 41);
+    }
     return;
   }
   const int pe = pb + P < npages ? pb + P : npages;
@@ -142,35 +165,59 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
   }
 
   const float scale = 0.08838834764831845f;  // 1/sqrt(128) as float
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  const int r = lane & 15, hh = lane >> 4;
+  // Lane roles in the m16n8k16 fragments: row g = lane / 4. Rows 0-1 carry the
+  // bf16 "hi" parts of query heads 0-1, rows 2-3 their "lo" remainders.
+  const int g = lane >> 2;
+  const bool qrow_ok = g < 4;
+  float m_r = -INFINITY, l_r = 0.f;  // softmax state of head (g & 1)
+  float acc16[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc16[i][0] = acc16[i][1] = acc16[i][2] = acc16[i][3] = 0.f;
+  __syncthreads();  // qs written by warps 0-1
+  uint32_t qa[8][2];  // A fragments (a0, a2) of the 8 K-steps; a1 = a3 = 0 (rows 8-15)
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const int dim = ks * 16 + (lane & 3) * 2;
+    if (qrow_ok) {
+      const float* qv = qs[g & 1];
+      const bool lo = g >= 2;
+      qa[ks][0] = pack_bf16(split_part(qv[dim], lo), split_part(qv[dim + 1], lo));
+      qa[ks][1] = pack_bf16(split_part(qv[dim + 8], lo), split_part(qv[dim + 9], lo));
+    } else {
+      qa[ks][0] = qa[ks][1] = 0u;
+    }
+  }
   // Page groups of kAttnWarps pages, double-buffered: group i+1 is in flight
   // while group i is consumed.
-  if (staged_end < (pb + kAttnWarps < pe ? pb + kAttnWarps : pe)) {
+  if (t == 0) {
     const int g1 = pb + kAttnWarps < pe ? pb + kAttnWarps : pe;
-    stage_pages(sm + (staged_end - pb) * (kKTile + kVTile), a.kv_layer, pt, h, staged_end, g1, t);
+    if (staged_end < g1)
+      stage_pages(sm + (staged_end - pb) * (kKTile + kVTile), a.kv_layer, pt, h, staged_end, g1,
+                  &bar[0]);
+    else
+      mbar_arrive_expect_tx(&bar[0], 0);
   }
-  asm volatile("cp.async.commit_group;" ::: "memory");
   for (int g0 = pb; g0 < pe; g0 += kAttnWarps) {
+    const int gi = (g0 - pb) / kAttnWarps;
     const int g1 = g0 + kAttnWarps < pe ? g0 + kAttnWarps : pe;
-    uint8_t* buf = sm + (((g0 - pb) / kAttnWarps) & 1) * kGroupBytes;
-    const bool more = g1 < pe;
-    if (more) {
-      const int n0 = g1, n1 = g1 + kAttnWarps < pe ? g1 + kAttnWarps : pe;
-      stage_pages(sm + ((((g0 - pb) / kAttnWarps) + 1) & 1) * kGroupBytes, a.kv_layer, pt, h, n0,
-                  n1, t);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    uint8_t* buf = sm + (gi & 1) * kGroupBytes;
+    if (g1 < pe && t == 0) {
+      const int n1 = g1 + kAttnWarps < pe ? g1 + kAttnWarps : pe;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      stage_pages(sm + ((gi + 1) & 1) * kGroupBytes, a.kv_layer, pt, h, g1, n1,
+                  &bar[1 + ((gi + 1) & 1)]);
     }
+    // group gi >= 1 lives in buffer gi & 1 with barrier 1 + (gi & 1), phase (gi - 1) / 2
+    if (gi == 0)
+      mbar_wait(&bar[0], 0, a.err, 42);
+    else
+      mbar_wait(&bar[1 + (gi & 1)], ((gi - 1) >> 1) & 1, a.err, 43);
     __syncthreads();  // every thread's copies of this group have landed
     if (owner && warp == 2 && g1 == pe) {
       // the staged copy of the newest slot may predate this step: patch it
       uint8_t* base = buf + (pos / kPage - g0) * (kKTile + kVTile);
       uint16_t* kd = reinterpret_cast<uint16_t*>(base + (pos % kPage) * kKRow);
-      uint16_t* vd = reinterpret_cast<uint16_t*>(base + kKTile + (pos % kPage) * kHeadDim * 2);
+      uint16_t* vd = reinterpret_cast<uint16_t*>(base + kKTile + (pos % kPage) * kKRow);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         kd[lane + 32 * i] = f2bf(knew[i]);
@@ -180,94 +227,119 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
     __syncthreads();
     const int p = g0 + warp;
     if (p < g1) {
+      // Tensor-core page: scores[16 rows x 16 positions] = Q~ K^T with Q~ rows
+      // {q0 hi, q1 hi, q0 lo, q1 lo, 0...}; out += P~ V likewise.
       const uint8_t* base = buf + warp * (kKTile + kVTile);
-      const uint4* krow = reinterpret_cast<const uint4*>(base + r * kKRow);
-      const uint16_t* V = reinterpret_cast<const uint16_t*>(base + kKTile);
-      float d4[4] = {0.f, 0.f, 0.f, 0.f};
+      float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint4 w = krow[i];
-        const float* q = &qs[hh][i * 8];
-        float& dot = d4[i & 3];
-        dot = fmaf(q[0], bf_lo(w.x), dot);
-        dot = fmaf(q[1], bf_hi(w.x), dot);
-        dot = fmaf(q[2], bf_lo(w.y), dot);
-        dot = fmaf(q[3], bf_hi(w.y), dot);
-        dot = fmaf(q[4], bf_lo(w.z), dot);
-        dot = fmaf(q[5], bf_hi(w.z), dot);
-        dot = fmaf(q[6], bf_lo(w.w), dot);
-        dot = fmaf(q[7], bf_hi(w.w), dot);
-      }
-      const float dot = (d4[0] + d4[1]) + (d4[2] + d4[3]);
-      const bool valid = p * kPage + r <= pos;
-      const float s = valid ? dot * scale : -INFINITY;
-      float mx = s;
+      for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float mx_other = __shfl_xor_sync(0xffffffffu, mx, 16);
-      const float mx0 = hh ? mx_other : mx, mx1 = hh ? mx : mx_other;
-      const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
-      const float c0 = expf(m[0] - mn0), c1 = expf(m[1] - mn1);
-      const float pl = valid ? expf(s - (hh ? mn1 : mn0)) : 0.f;
-      float ps = pl;
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      const float ps_other = __shfl_xor_sync(0xffffffffu, ps, 16);
-      l[0] = l[0] * c0 + (hh ? ps_other : ps);
-      l[1] = l[1] * c1 + (hh ? ps : ps_other);
-      m[0] = mn0;
-      m[1] = mn1;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        acc[0][i] *= c0;
-        acc[1][i] *= c1;
-      }
-#pragma unroll
-      for (int r2 = 0; r2 < kPage; ++r2) {
-        const uint2 vv = reinterpret_cast<const uint2*>(V + r2 * kHeadDim)[lane];
-        const float p0 = __shfl_sync(0xffffffffu, pl, r2);
-        const float p1 = __shfl_sync(0xffffffffu, pl, 16 + r2);
-        const float v4[4] = {bf_lo(vv.x), bf_hi(vv.x), bf_lo(vv.y), bf_hi(vv.y)};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          acc[0][i] = fmaf(p0, v4[i], acc[0][i]);
-          acc[1][i] = fmaf(p1, v4[i], acc[1][i]);
+        for (int nt = 0; nt < 2; ++nt) {
+          const uint8_t* kr = base + (nt * 8 + (lane >> 2)) * kKRow + (ks * 16 + (lane & 3) * 2) * 2;
+          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr);
+          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 16);
+          mma_bf16(d[nt], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
         }
+      }
+      // combine hi + lo rows (lane ^ 8 holds the partner row g ^ 2)
+      float sc[4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float v = d[nt][j] + __shfl_xor_sync(0xffffffffu, d[nt][j], 8);
+          const int ppos = p * kPage + nt * 8 + (lane & 3) * 2 + j;
+          sc[nt * 2 + j] = (ppos <= pos) ? v * scale : -INFINITY;
+        }
+      float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      // rows 4-15 (lanes 16-31) are zero rows: their state is computed but unused
+      const float mn = fmaxf(m_r, mx);
+      const float corr = expf(m_r - mn);
+      float pr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pr[i] = sc[i] == -INFINITY ? 0.f : expf(sc[i] - mn);
+      float ps = (pr[0] + pr[1]) + (pr[2] + pr[3]);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+      l_r = l_r * corr + ps;
+      m_r = mn;
+      const bool lo = (lane >> 2) >= 2;
+      uint32_t pa0 = 0u, pa2 = 0u;
+      if (qrow_ok) {
+        pa0 = pack_bf16(split_part(pr[0], lo), split_part(pr[1], lo));
+        pa2 = pack_bf16(split_part(pr[2], lo), split_part(pr[3], lo));
+      }
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt) {
+        acc16[nt][0] *= corr;
+        acc16[nt][1] *= corr;
+      }
+      const uint8_t* vb = base + kKTile;
+#pragma unroll
+      for (int nt = 0; nt < 16; nt += 2) {
+        // matrices: (pos 0-7, dims 8nt..), (pos 8-15, dims 8nt..), (pos 0-7, dims 8nt+8..), (pos 8-15, ...)
+        const int vrow = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int vcol = nt * 8 + (lane >> 4) * 8;
+        const uint32_t addr = smem_u32(vb + vrow * kKRow + vcol * 2);
+        uint32_t b0, b1, b2, b3;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3)
+                     : "r"(addr));
+        mma_bf16(acc16[nt], pa0, 0u, pa2, 0u, b0, b1);
+        mma_bf16(acc16[nt + 1], pa0, 0u, pa2, 0u, b2, b3);
       }
     }
     __syncthreads();  // this buffer is restaged two groups later
   }
-  if (lane == 0) {
-    sm_m[warp][0] = m[0]; sm_m[warp][1] = m[1];
-    sm_l[warp][0] = l[0]; sm_l[warp][1] = l[1];
+  // out rows: head (g&1) = row g + row g^2 (hi + lo)
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    acc16[nt][0] += __shfl_xor_sync(0xffffffffu, acc16[nt][0], 8);
+    acc16[nt][1] += __shfl_xor_sync(0xffffffffu, acc16[nt][1], 8);
   }
+  if (g < 2) {
 #pragma unroll
-  for (int k = 0; k < 2; ++k)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sm_acc[warp][k][lane * 4 + i] = acc[k][i];
+    for (int nt = 0; nt < 16; ++nt) {
+      sm_acc[warp][g][nt * 8 + (lane & 3) * 2] = acc16[nt][0];
+      sm_acc[warp][g][nt * 8 + (lane & 3) * 2 + 1] = acc16[nt][1];
+    }
+    if ((lane & 3) == 0) {
+      sm_m[warp][g] = m_r;
+      sm_l[warp][g] = l_r;
+    }
+  }
   __syncthreads();
-  const bool own = t < 2 * kHeadDim;  // threads 0..255 own (head kk, dim d)
-  const int kk = (t >> 7) & 1, d = t & 127;
-  float mm = -INFINITY, ll = 0.f, aa = 0.f;
-  if (own) {
+  // Outputs (head kk, dim d), o = kk * 128 + d, strided over the threads.
+  constexpr int kOut = 2 * kHeadDim / kAttnThreads;
+  float mmv[kOut], llv[kOut], aav[kOut];
+#pragma unroll
+  for (int q = 0; q < kOut; ++q) {
+    const int o = t + q * kAttnThreads, kk = o >> 7, d = o & 127;
+    float mm = -INFINITY, ll = 0.f, aa = 0.f;
     for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, sm_m[w][kk]);
     for (int w = 0; w < kAttnWarps; ++w) {
       const float e = sm_l[w][kk] > 0.f ? expf(sm_m[w][kk] - mm) : 0.f;
       ll += sm_l[w][kk] * e;
       aa += sm_acc[w][kk][d] * e;
     }
+    mmv[q] = mm; llv[q] = ll; aav[q] = aa;
   }
-  uint16_t* orow = a.out + (long long)row * kQDim + (2 * h + kk) * kHeadDim + d;
+  uint16_t* orow = a.out + (long long)row * kQDim + (2 * h) * kHeadDim;
   if (nsplit == 1) {
-    if (own) *orow = f2bf(aa * (1.0f / ll));
+#pragma unroll
+    for (int q = 0; q < kOut; ++q) orow[t + q * kAttnThreads] = f2bf(aav[q] * (1.0f / llv[q]));
     trace_mark(a.trace, 2);
     return;
   }
   const long long slot = ((long long)row * kKvHeads + h) * a.nsplit_max;
-  if (own) {
+#pragma unroll
+  for (int q = 0; q < kOut; ++q) {
+    const int o = t + q * kAttnThreads, kk = o >> 7, d = o & 127;
     float* part = a.part + (slot + split) * kPartStride + kk * 132;
-    part[d] = aa;
-    if (d == 0) { part[128] = mm; part[129] = ll; }
+    part[d] = aav[q];
+    if (d == 0) { part[128] = mmv[q]; part[129] = llv[q]; }
   }
   __threadfence();
   __syncthreads();
@@ -282,11 +354,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
   }
   __threadfence();
   // Combine the splits: per-split (m, l) staged in shared memory, then every
-  // owning thread sums its output dimension over the splits.
+  // thread sums its output dimensions over the splits.
   __shared__ float sw[2][kMaxSplits];
   __shared__ float sl[2];
-  if (t < 2 * nsplit) {
-    const int k = t / nsplit, s2 = t % nsplit;
+  for (int i2 = t; i2 < 2 * nsplit; i2 += kAttnThreads) {
+    const int k = i2 / nsplit, s2 = i2 % nsplit;
     sw[k][s2] = __ldcg(a.part + (slot + s2) * kPartStride + k * 132 + 128);
   }
   __syncthreads();
@@ -302,11 +374,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(AttnArgs a) {
     sl[t] = l2;
   }
   __syncthreads();
-  if (own) {
+#pragma unroll
+  for (int q = 0; q < kOut; ++q) {
+    const int o = t + q * kAttnThreads, kk = o >> 7, d = o & 127;
     float a2 = 0.f;
     for (int s2 = 0; s2 < nsplit; ++s2)
       a2 += __ldcg(a.part + (slot + s2) * kPartStride + kk * 132 + d) * sw[kk][s2];
-    *orow = f2bf(a2 * (1.0f / sl[kk]));
+    orow[o] = f2bf(a2 * (1.0f / sl[kk]));
   }
   if (t == 0) a.counters[row * kKvHeads + h] = 0;
   trace_mark(a.trace, 2);
