@@ -9,6 +9,8 @@
 // so each K/V page is read once per group.  Math is the reference's: fp32 q,
 // bf16 K/V, scores scaled by 1/sqrt(128), exp-normalised in fp32, output
 // rounded to bf16 (the cast the reference does before o_proj).
+#include <cuda.h>
+
 #include <utility>
 
 #include "common.cuh"
@@ -25,7 +27,7 @@ constexpr int kKRow = kHeadDim * 2;       // K / V row in shared memory (bytes)
 constexpr int kKTile = kPage * kKRow;     // 4 KiB: one (page, kv head) K tile, as in HBM
 constexpr int kVTile = kPage * kKRow;
 constexpr int kGroupBytes = kAttnWarps * (kKTile + kVTile);
-constexpr int kAttnSmem = 2 * kGroupBytes + 128;  // double-buffered page groups
+constexpr int kAttnSmem = kAttnWarps * 2 * (kKTile + kVTile) + 1024;  // 2-slot ring per warp
 
 __device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -83,10 +85,26 @@ __device__ __forceinline__ void stage_pages(uint8_t* sm, const uint16_t* kv, con
 // griddepcontrol.wait using a speculative read of the position: cache entries
 // older than the current position never change, and the one page that may be
 // missing (when the position just crossed a page) is fetched after the wait.
-__global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                       uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Byte offset of element (r, c) of a staged 16 x 128 bf16 tile: two 16 x 64
+// halves, each in the 128-byte TMA swizzle (16-byte chunk ^ row % 8).
+__device__ __forceinline__ int sw_off(int r, int c) {
+  return (c >> 6) * 2048 + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2;
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 3)
+    attn_kernel(const __grid_constant__ CUtensorMap kvmap, AttnArgs a) {
   extern __shared__ uint8_t attn_smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(attn_smem_raw) + 127) & ~uintptr_t(127));
+      (reinterpret_cast<uintptr_t>(attn_smem_raw) + 1023) & ~uintptr_t(1023));
   const int split = blockIdx.x, h = blockIdx.y, row = blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int P = a.pages_per_split;
@@ -95,25 +113,35 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   const int* pt = a.page_table + (long long)tab * a.max_pages;
   const int* pos_ptr = a.pos_scalar ? a.pos_scalar : (a.row_pos ? a.row_pos + row : nullptr);
   const int pb = split * P;
-  // bar[0]: first group (2 arrivals: speculative + completion), bar[1], bar[2]:
-  // later groups in buffers 0 / 1 (1 arrival each).
-  __shared__ uint64_t bar[3];
-  __shared__ int staged_end_s;
-  if (t == 0) {
-    mbar_init(&bar[0], 2);
-    mbar_init(&bar[1], 1);
-    mbar_init(&bar[2], 1);
+  // Each warp streams its own pages (pb + warp, pb + warp + kAttnWarps, ...)
+  // through a private 2-slot ring: K and V tiles by 2-D TMA with 128-byte
+  // swizzle (conflict-free fragment loads), one mbarrier per slot.
+  __shared__ uint64_t bar[kAttnWarps][2];
+  uint8_t* ring = sm + warp * 2 * (kKTile + kVTile);
+  auto issue = [&](int page_idx, int slot) {  // lane 0
+    uint8_t* dst = ring + slot * (kKTile + kVTile);
+    const int r0 = a.kv_row0 + (pt[page_idx] * 2 * kKvHeads + h) * kPage;   // K rows
+    const int r1 = r0 + kKvHeads * kPage;                                     // V rows
+    mbar_arrive_expect_tx(&bar[warp][slot], kKTile + kVTile);
+    tma_2d(dst, &kvmap, 0, r0, &bar[warp][slot]);
+    tma_2d(dst + 2048, &kvmap, 64, r0, &bar[warp][slot]);
+    tma_2d(dst + kKTile, &kvmap, 0, r1, &bar[warp][slot]);
+    tma_2d(dst + kKTile + 2048, &kvmap, 64, r1, &bar[warp][slot]);
+  };
+  int issued = 0;  // pages of this warp already requested (lane 0's view)
+  if (lane == 0) {
+    mbar_init(&bar[warp][0], 1);
+    mbar_init(&bar[warp][1], 1);
     fence_mbar_init();
-    int e = pb;
     if (a.fused_kv && pos_ptr) {
+      // speculative: entries older than the current position never change
       const int pos_g = *reinterpret_cast<const volatile int*>(pos_ptr);
-      e = (pos_g + kPage) / kPage;
+      int e = (pos_g + kPage) / kPage;
       e = e < pb + P ? e : pb + P;
-      e = e < pb + kAttnWarps ? e : pb + kAttnWarps;
-      if (e < pb || e > a.max_pages) e = pb;
+      if (e <= a.max_pages)
+        for (; issued < 2 && pb + warp + issued * kAttnWarps < e; ++issued)
+          issue(pb + warp + issued * kAttnWarps, issued);
     }
-    stage_pages(sm, a.kv_layer, pt, h, pb, e, &bar[0]);  // e == pb: arrival only
-    staged_end_s = e;
   }
   pdl_trigger();
   pdl_wait();
@@ -121,25 +149,25 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   const int pos = pos_ptr ? *pos_ptr : a.pos_base + row;
   const int npages = (pos + kPage) / kPage;  // pages holding positions [0, pos]
   const int nsplit = (npages + P - 1) / P;
-  __syncthreads();
-  const int staged_end = staged_end_s;
+  const int pe = pb + P < npages ? pb + P : npages;
+  const int nw = pe > pb + warp ? (pe - pb - warp + kAttnWarps - 1) / kAttnWarps : 0;
+  if (lane == 0)
+    for (; issued < 2 && issued < nw; ++issued) issue(pb + warp + issued * kAttnWarps, issued);
+  issued = __shfl_sync(0xffffffffu, issued, 0);
   if (split >= nsplit) {
-    if (t == 0) {  // do not leave with copies in flight
-      mbar_arrive_expect_tx(&bar[0], 0);
-      mbar_wait(&bar[0], 0, a.err, 41);
-    }
+    // drain speculative copies before leaving
+    for (int j = 0; j < issued; ++j) mbar_wait(&bar[warp][j], 0, a.err, 41);
     return;
   }
-  const int pe = pb + P < npages ? pb + P : npages;
 
   __shared__ float qs[2][kHeadDim];
+  __shared__ uint16_t knew_s[kHeadDim], vnew_s[kHeadDim];
   __shared__ float sm_m[kAttnWarps][2], sm_l[kAttnWarps][2];
   __shared__ float sm_acc[kAttnWarps][2][kHeadDim];
   __shared__ int sm_last;
 
   const float* qrow = a.qkv + (long long)row * a.qkv_stride;
   const bool owner = a.fused_kv && pe == npages;  // this split holds position `pos`
-  float knew[4], vnew[4];
   if (warp < 2) {
     float v[4];
 #pragma unroll
@@ -149,6 +177,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
     for (int i = 0; i < 4; ++i) qs[warp][lane + 32 * i] = v[i];
   } else if (warp == 2 && owner) {
     // normalise, rotate and store K; store V (bf16, as the reference cache)
+    float knew[4], vnew[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       knew[i] = qrow[kQDim + h * kHeadDim + lane + 32 * i];
@@ -159,8 +188,11 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
                     (h * kPage + pos % kPage) * kHeadDim;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      dst[lane + 32 * i] = f2bf(knew[i]);
-      dst[kHalfPageElems + lane + 32 * i] = f2bf(vnew[i]);
+      const uint16_t kb = f2bf(knew[i]), vb = f2bf(vnew[i]);
+      dst[lane + 32 * i] = kb;
+      dst[kHalfPageElems + lane + 32 * i] = vb;
+      knew_s[lane + 32 * i] = kb;
+      vnew_s[lane + 32 * i] = vb;
     }
   }
 
@@ -173,7 +205,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   float acc16[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) acc16[i][0] = acc16[i][1] = acc16[i][2] = acc16[i][3] = 0.f;
-  __syncthreads();  // qs written by warps 0-1
+  __syncthreads();  // qs / knew_s / vnew_s written
   uint32_t qa[8][2];  // A fragments (a0, a2) of the 8 K-steps; a1 = a3 = 0 (rows 8-15)
 #pragma unroll
   for (int ks = 0; ks < 8; ++ks) {
@@ -187,57 +219,34 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
       qa[ks][0] = qa[ks][1] = 0u;
     }
   }
-  // Page groups of kAttnWarps pages, double-buffered: group i+1 is in flight
-  // while group i is consumed.
-  if (t == 0) {
-    const int g1 = pb + kAttnWarps < pe ? pb + kAttnWarps : pe;
-    if (staged_end < g1)
-      stage_pages(sm + (staged_end - pb) * (kKTile + kVTile), a.kv_layer, pt, h, staged_end, g1,
-                  &bar[0]);
-    else
-      mbar_arrive_expect_tx(&bar[0], 0);
-  }
-  for (int g0 = pb; g0 < pe; g0 += kAttnWarps) {
-    const int gi = (g0 - pb) / kAttnWarps;
-    const int g1 = g0 + kAttnWarps < pe ? g0 + kAttnWarps : pe;
-    uint8_t* buf = sm + (gi & 1) * kGroupBytes;
-    if (g1 < pe && t == 0) {
-      const int n1 = g1 + kAttnWarps < pe ? g1 + kAttnWarps : pe;
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      stage_pages(sm + ((gi + 1) & 1) * kGroupBytes, a.kv_layer, pt, h, g1, n1,
-                  &bar[1 + ((gi + 1) & 1)]);
-    }
-    // group gi >= 1 lives in buffer gi & 1 with barrier 1 + (gi & 1), phase (gi - 1) / 2
-    if (gi == 0)
-      mbar_wait(&bar[0], 0, a.err, 42);
-    else
-      mbar_wait(&bar[1 + (gi & 1)], ((gi - 1) >> 1) & 1, a.err, 43);
-    __syncthreads();  // every thread's copies of this group have landed
-    if (owner && warp == 2 && g1 == pe) {
+
+  for (int j = 0; j < nw; ++j) {
+    const int p = pb + warp + j * kAttnWarps;
+    const int slot = j & 1;
+    mbar_wait(&bar[warp][slot], (j >> 1) & 1, a.err, 42);
+    uint8_t* base = ring + slot * (kKTile + kVTile);
+    if (owner && p == pos / kPage) {
       // the staged copy of the newest slot may predate this step: patch it
-      uint8_t* base = buf + (pos / kPage - g0) * (kKTile + kVTile);
-      uint16_t* kd = reinterpret_cast<uint16_t*>(base + (pos % kPage) * kKRow);
-      uint16_t* vd = reinterpret_cast<uint16_t*>(base + kKTile + (pos % kPage) * kKRow);
+      const int r = pos % kPage;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        kd[lane + 32 * i] = f2bf(knew[i]);
-        vd[lane + 32 * i] = f2bf(vnew[i]);
+        const int c = lane + 32 * i;
+        *reinterpret_cast<uint16_t*>(base + sw_off(r, c)) = knew_s[c];
+        *reinterpret_cast<uint16_t*>(base + kKTile + sw_off(r, c)) = vnew_s[c];
       }
+      __syncwarp();
     }
-    __syncthreads();
-    const int p = g0 + warp;
-    if (p < g1) {
+    {
       // Tensor-core page: scores[16 rows x 16 positions] = Q~ K^T with Q~ rows
       // {q0 hi, q1 hi, q0 lo, q1 lo, 0...}; out += P~ V likewise.
-      const uint8_t* base = buf + warp * (kKTile + kVTile);
       float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
-          const uint8_t* kr = base + (nt * 8 + (lane >> 2)) * kKRow + (ks * 16 + (lane & 3) * 2) * 2;
-          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr);
-          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 16);
+          const int r = nt * 8 + (lane >> 2), c = ks * 16 + (lane & 3) * 2;
+          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(base + sw_off(r, c));
+          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(base + sw_off(r, c + 8));
           mma_bf16(d[nt], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
         }
       }
@@ -246,10 +255,10 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const float v = d[nt][j] + __shfl_xor_sync(0xffffffffu, d[nt][j], 8);
-          const int ppos = p * kPage + nt * 8 + (lane & 3) * 2 + j;
-          sc[nt * 2 + j] = (ppos <= pos) ? v * scale : -INFINITY;
+        for (int jj = 0; jj < 2; ++jj) {
+          const float v = d[nt][jj] + __shfl_xor_sync(0xffffffffu, d[nt][jj], 8);
+          const int ppos = p * kPage + nt * 8 + (lane & 3) * 2 + jj;
+          sc[nt * 2 + jj] = (ppos <= pos) ? v * scale : -INFINITY;
         }
       float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -265,7 +274,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
       ps += __shfl_xor_sync(0xffffffffu, ps, 2);
       l_r = l_r * corr + ps;
       m_r = mn;
-      const bool lo = (lane >> 2) >= 2;
+      const bool lo = g >= 2;
       uint32_t pa0 = 0u, pa2 = 0u;
       if (qrow_ok) {
         pa0 = pack_bf16(split_part(pr[0], lo), split_part(pr[1], lo));
@@ -282,7 +291,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
         // matrices: (pos 0-7, dims 8nt..), (pos 8-15, dims 8nt..), (pos 0-7, dims 8nt+8..), (pos 8-15, ...)
         const int vrow = (lane & 7) + ((lane >> 3) & 1) * 8;
         const int vcol = nt * 8 + (lane >> 4) * 8;
-        const uint32_t addr = smem_u32(vb + vrow * kKRow + vcol * 2);
+        const uint32_t addr = smem_u32(vb + sw_off(vrow, vcol));
         uint32_t b0, b1, b2, b3;
         asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                      : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3)
@@ -291,7 +300,11 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
         mma_bf16(acc16[nt + 1], pa0, 0u, pa2, 0u, b2, b3);
       }
     }
-    __syncthreads();  // this buffer is restaged two groups later
+    __syncwarp();
+    if (lane == 0 && j + 2 < nw) {  // the slot is free again: next page of this warp
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(pb + warp + (j + 2) * kAttnWarps, slot);
+    }
   }
   // out rows: head (g&1) = row g + row g^2 (hi + lo)
 #pragma unroll
@@ -439,14 +452,18 @@ __global__ void __launch_bounds__(256) qk_norm_rope_store_kernel(
 
 }  // namespace
 
-void launch_attention(const AttnArgs& a, cudaStream_t s) {
+void launch_attention(const AttnArgs& a, const uint16_t* kv_pool, long long pool_rows,
+                      cudaStream_t s) {
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
     configured = true;
   }
+  // one map per pool; encoding is a host-side operation of about a microsecond
+  CUtensorMap map;
+  if (!make_tmap_2d(&map, kv_pool, pool_rows, kHeadDim, 64, kPage)) return;
   launch_pdl(attn_kernel, dim3(a.nsplit_max < kMaxSplits ? a.nsplit_max : kMaxSplits, kKvHeads, a.rows),
-             dim3(kAttnThreads), kAttnSmem, s, a);
+             dim3(kAttnThreads), kAttnSmem, s, map, a);
 }
 
 void launch_qk_norm_rope_store(float* qkv, int rows, const float* qn, const float* kn,

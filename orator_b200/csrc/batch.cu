@@ -271,7 +271,8 @@ void BatchDecoder::layers(int rows, int max_len, bool fused, cudaStream_t s) {
     a.counters = counters_;
     a.out = attn_;
     a.err = err;
-    launch_attention(a, s);
+    a.kv_row0 = l * kv_->pages * 2 * kKvHeads * kPage;
+    launch_attention(a, kv_->base, (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
     run_proj(gws_, attn_, L.o, kHidden, kQDim, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s);
     launch_rmsnorm_bf16(x_, L.post_ln, xn_, rows, c.rms_norm_eps, s);
     run_proj(gws_, xn_, L.gateup, 2 * kInter, kHidden, rows, kEpiSwiglu, nullptr, act_, kInter, err, sms, s);

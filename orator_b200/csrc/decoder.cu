@@ -172,7 +172,8 @@ void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
     a.counters = pcounters_;
     a.out = pattn_;
     a.err = &st_->err;
-    launch_attention(a, s);
+    a.kv_row0 = l * kv_->pages * 2 * kKvHeads * kPage;
+    launch_attention(a, kv_->base, (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
     run_proj(gws_, pattn_, L.o, kHidden, kQDim, T, kEpiResid, px_, nullptr, kHidden, &st_->err, model->num_sms, s);
     launch_rmsnorm_bf16(px_, L.post_ln, pxn_, T, c.rms_norm_eps, s);
     run_proj(gws_, pxn_, L.gateup, 2 * kInter, kHidden, T, kEpiSwiglu, nullptr, pact_, kInter, &st_->err, model->num_sms, s);
@@ -269,7 +270,8 @@ void Decoder::record_body(cudaStream_t s, const int* tok_ptr, bool record, bool 
     a.out = dattn_;
     a.err = &st_->err;
     a.trace = tr();
-    if (on(1)) launch_attention(a, s);
+    a.kv_row0 = l * kv_->pages * 2 * kKvHeads * kPage;
+    if (on(1)) launch_attention(a, kv_->base, (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
 
     GemvArgs o = {};
     o.W = L.o;

@@ -61,6 +61,7 @@ struct AttnArgs {
   const float* rope_cos;   // [max_pos, 64]
   const float* rope_sin;
   uint16_t* kv_layer;      // this layer's page pool base
+  int kv_row0;             // first 128-wide row of this layer in the pool's tensor map
   long long layer_stride;  // elements between layers (for reference only)
   const int* page_table;   // [n_tables, max_pages]
   int max_pages;
@@ -78,7 +79,13 @@ struct AttnArgs {
   int* err;
   unsigned long long* trace;  // optional debug timeline slot (3 words)
 };
-void launch_attention(const AttnArgs& a, cudaStream_t s);
+// kv_pool: pool base ([layers * pages * 2 * 8 * 16, 128] bf16 rows).
+void launch_attention(const AttnArgs& a, const uint16_t* kv_pool, long long pool_rows,
+                      cudaStream_t s);
+// 2-D bf16 TMA map over a row-major [rows, cols] matrix, box box_cols x box_rows,
+// 128-byte swizzle.
+bool make_tmap_2d(void* map, const void* base, long long rows, int cols, int box_cols,
+                  int box_rows);
 
 // q/k RMSNorm + RoPE + K/V store for T prefill rows (q normalised in place).
 void launch_qk_norm_rope_store(float* qkv, int rows, const float* qn, const float* kn,
