@@ -190,16 +190,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
     } else {
+      // residual: issue all 32 loads before any store (independent, pipelined)
+      float r[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int t = n0 + c0 + i;
-        if (c0 + i < BN && t < g.T) {
-          float* o = g.out_f32 + (long long)t * g.ldo + row;
-          if (g.epi == kEpiResid)
-            *o += v[i];
-          else
-            *o = v[i];
-        }
+        r[i] = (g.epi == kEpiResid && c0 + i < BN && t < g.T)
+                   ? g.out_f32[(long long)t * g.ldo + row] : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int t = n0 + c0 + i;
+        if (c0 + i < BN && t < g.T) g.out_f32[(long long)t * g.ldo + row] = r[i] + v[i];
       }
     }
   };
