@@ -29,24 +29,6 @@ constexpr int kVTile = kPage * kKRow;
 constexpr int kGroupBytes = kAttnWarps * (kKTile + kVTile);
 constexpr int kAttnSmem = kAttnWarps * 2 * (kKTile + kVTile) + 1024;  // 2-slot ring per warp
 
-__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  return static_cast<uint32_t>(f2bf(lo)) | (static_cast<uint32_t>(f2bf(hi)) << 16);
-}
-// bf16 part of x for rows 0-1 (hi) or its remainder for rows 2-3 (lo):
-// hi + lo represents x to about 2^-16 relative, so bf16 MMAs give fp32-grade dots.
-__device__ __forceinline__ float split_part(float x, bool lo) {
-  const float h = bf2f(f2bf(x));
-  return lo ? x - h : h;
-}
-
 // RMSNorm (eps 1e-6) + rotate-half RoPE of one 128-wide head held by a warp:
 // lane holds d = lane + 32*i, so the RoPE partner d +/- 64 is in the same lane.
 __device__ __forceinline__ void head_norm_rope(float v[4], const float* w, const float* cosT,
@@ -85,21 +67,6 @@ __device__ __forceinline__ void stage_pages(uint8_t* sm, const uint16_t* kv, con
 // griddepcontrol.wait using a speculative read of the position: cache entries
 // older than the current position never change, and the one page that may be
 // missing (when the position just crossed a page) is fetched after the wait.
-__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y,
-                                       uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Byte offset of element (r, c) of a staged 16 x 128 bf16 tile: two 16 x 64
-// halves, each in the 128-byte TMA swizzle (16-byte chunk ^ row % 8).
-__device__ __forceinline__ int sw_off(int r, int c) {
-  return (c >> 6) * 2048 + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2;
-}
-
 __global__ void __launch_bounds__(kAttnThreads, 3)
     attn_kernel(const __grid_constant__ CUtensorMap kvmap, AttnArgs a) {
   extern __shared__ uint8_t attn_smem_raw[];

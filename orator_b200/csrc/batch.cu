@@ -108,9 +108,10 @@ BatchDecoder::~BatchDecoder() {
   delete kv_;
   for (void* p : {(void*)d_table_, (void*)d_next_tok_, (void*)st_, (void*)x_, (void*)xn_, (void*)qkv_,
                   (void*)attn_, (void*)act_, (void*)logits_, (void*)part_, (void*)counters_,
-                  (void*)d_rows_, (void*)d_tokens_, (void*)d_out_})
+                  (void*)d_rows_, (void*)d_tokens_, (void*)d_out_, (void*)d_tiles_})
     if (p) cudaFree(p);
   if (h_rows_) cudaFreeHost(h_rows_);
+  if (h_tiles_) cudaFreeHost(h_tiles_);
   for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
   for (int b = 0; b < 2; ++b) {
     if (h_step_[b]) cudaFreeHost(h_step_[b]);
@@ -251,28 +252,42 @@ void BatchDecoder::layers(int rows, int max_len, bool fused, cudaStream_t s) {
     if (!fused)
       launch_qk_norm_rope_store(qkv_, rows, L.q_norm, L.k_norm, model->rope_cos, model->rope_sin,
                                 kvl, d_table_, mps_, row_table, row_pos, 0, s);
-    AttnArgs a = {};
-    a.qkv = qkv_;
-    a.qkv_stride = kQkvDim;
-    a.q_norm_w = L.q_norm;
-    a.k_norm_w = L.k_norm;
-    a.rope_cos = model->rope_cos;
-    a.rope_sin = model->rope_sin;
-    a.kv_layer = kvl;
-    a.page_table = d_table_;
-    a.max_pages = mps_;
-    a.row_table = row_table;
-    a.row_pos = row_pos;
-    a.rows = rows;
-    a.fused_kv = fused ? 1 : 0;
-    a.nsplit_max = nsplit;
-    a.pages_per_split = kSplitPages;
-    a.part = part_;
-    a.counters = counters_;
-    a.out = attn_;
-    a.err = err;
-    a.kv_row0 = l * kv_->pages * 2 * kKvHeads * kPage;
-    launch_attention(a, kv_->base, (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
+    if (fused) {
+      AttnArgs a = {};
+      a.qkv = qkv_;
+      a.qkv_stride = kQkvDim;
+      a.q_norm_w = L.q_norm;
+      a.k_norm_w = L.k_norm;
+      a.rope_cos = model->rope_cos;
+      a.rope_sin = model->rope_sin;
+      a.kv_layer = kvl;
+      a.page_table = d_table_;
+      a.max_pages = mps_;
+      a.row_table = row_table;
+      a.row_pos = row_pos;
+      a.rows = rows;
+      a.fused_kv = fused ? 1 : 0;
+      a.nsplit_max = nsplit;
+      a.pages_per_split = kSplitPages;
+      a.part = part_;
+      a.counters = counters_;
+      a.out = attn_;
+      a.err = err;
+      a.kv_row0 = l * kv_->pages * 2 * kKvHeads * kPage;
+      launch_attention(a, kv_->base, (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
+    } else {
+      PrefillAttnArgs pa = {};
+      pa.qkv = qkv_;
+      pa.qkv_stride = kQkvDim;
+      pa.tiles = d_tiles_;
+      pa.page_table = d_table_;
+      pa.max_pages = mps_;
+      pa.kv_row0 = l * kv_->pages * 2 * kKvHeads * kPage;
+      pa.out = attn_;
+      pa.err = err;
+      launch_attn_prefill(pa, ntiles_, kv_->base,
+                          (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
+    }
     run_proj(gws_, attn_, L.o, kHidden, kQDim, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s);
     launch_rmsnorm_bf16(x_, L.post_ln, xn_, rows, c.rms_norm_eps, s);
     run_proj(gws_, xn_, L.gateup, 2 * kInter, kHidden, rows, kEpiSwiglu, nullptr, act_, kInter, err, sms, s);
@@ -307,6 +322,29 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
     }
     last[i] = r - 1;
     max_len = std::max(max_len, ss.len + lens[i]);
+  }
+  // attention tiles: runs of consecutive rows of one session
+  {
+    const int tr = prefill_tile_rows();
+    std::vector<PrefillTile> tiles;
+    int row = 0;
+    for (int i = 0; i < n; ++i) {
+      const int base = sessions_[sids[i]].len;
+      for (int t0 = 0; t0 < lens[i]; t0 += tr)
+        tiles.push_back({sids[i], base + t0, std::min(tr, lens[i] - t0), row + t0});
+      row += lens[i];
+    }
+    ntiles_ = static_cast<int>(tiles.size());
+    if (ntiles_ > tiles_cap_) {
+      if (d_tiles_) cudaFree(d_tiles_);
+      if (h_tiles_) cudaFreeHost(h_tiles_);
+      d_tiles_ = dalloc<PrefillTile>(ntiles_);
+      ORX_CHECK(cudaMallocHost(&h_tiles_, sizeof(PrefillTile) * ntiles_));
+      tiles_cap_ = ntiles_;
+    }
+    std::memcpy(h_tiles_, tiles.data(), sizeof(PrefillTile) * ntiles_);
+    ORX_CHECK(cudaMemcpyAsync(d_tiles_, h_tiles_, sizeof(PrefillTile) * ntiles_,
+                              cudaMemcpyHostToDevice, s));
   }
   upload_table(s);
   ORX_CHECK(cudaMemcpyAsync(d_rows_, h_rows_, sizeof(int) * 2 * rows_cap_, cudaMemcpyHostToDevice, s));

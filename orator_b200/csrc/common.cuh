@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -158,6 +159,40 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int m = 16; m > 0; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
   return v;
+}
+
+// ---- tensor-core and TMA helpers shared by the attention kernels ----------
+__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  return static_cast<uint32_t>(f2bf(lo)) | (static_cast<uint32_t>(f2bf(hi)) << 16);
+}
+// bf16 part of x for rows 0-1 (hi) or its remainder for rows 2-3 (lo):
+// hi + lo represents x to about 2^-16 relative, so bf16 MMAs give fp32-grade dots.
+__device__ __forceinline__ float split_part(float x, bool lo) {
+  const float h = bf2f(f2bf(x));
+  return lo ? x - h : h;
+}
+
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                       uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Byte offset of element (r, c) of a staged 16 x 128 bf16 tile: two 16 x 64
+// halves, each in the 128-byte TMA swizzle (16-byte chunk ^ row % 8).
+__device__ __forceinline__ int sw_off(int r, int c) {
+  return (c >> 6) * 2048 + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2;
 }
 
 }  // namespace orx

@@ -95,12 +95,13 @@ Decoder::~Decoder() {
   for (void* p : {(void*)page_table_, (void*)dx_, (void*)dqkv_, (void*)dattn_, (void*)dact_,
                   (void*)logits_, (void*)part_, (void*)counters_, (void*)st_, (void*)d_out_,
                   (void*)d_tmp_tok_, (void*)px_, (void*)pqkv_, (void*)pxn_, (void*)pattn_,
-                  (void*)pact_, (void*)pcounters_, (void*)ppart_, (void*)mk_layers_, (void*)mk_part_,
+                  (void*)pact_, (void*)pcounters_, (void*)ppart_, (void*)d_tiles_, (void*)mk_layers_, (void*)mk_part_,
                   (void*)mk_sync_})
     if (p) cudaFree(p);
   if (h_out_) cudaFreeHost(h_out_);
   if (h_tok_) cudaFreeHost(h_tok_);
   if (h_stage_) cudaFreeHost(h_stage_);
+  if (h_tiles_) cudaFreeHost(h_tiles_);
   if (own_model_) delete model;
 }
 
@@ -147,6 +148,22 @@ void Decoder::ensure_prefill(int T) {
 // Prefill forward (Forward, asr_text_decoder.cu:457-583) over T rows of px_.
 void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
   const auto& c = model->cfg;
+  // attention tiles: consecutive rows of the single session
+  const int tr = prefill_tile_rows();
+  const int ntiles = (T + tr - 1) / tr;
+  if (ntiles > tiles_cap_) {
+    ORX_CHECK(cudaStreamSynchronize(s));
+    if (d_tiles_) cudaFree(d_tiles_);
+    if (h_tiles_) cudaFreeHost(h_tiles_);
+    d_tiles_ = dalloc<PrefillTile>(ntiles);
+    ORX_CHECK(cudaMallocHost(&h_tiles_, sizeof(PrefillTile) * ntiles));
+    tiles_cap_ = ntiles;
+  }
+  ORX_CHECK(cudaStreamSynchronize(s));  // h_tiles_ may still feed an earlier copy
+  for (int i = 0; i < ntiles; ++i)
+    h_tiles_[i] = {0, pos0 + i * tr, std::min(tr, T - i * tr), i * tr};
+  ORX_CHECK(cudaMemcpyAsync(d_tiles_, h_tiles_, sizeof(PrefillTile) * ntiles,
+                            cudaMemcpyHostToDevice, s));
   for (int l = 0; l < c.num_layers; ++l) {
     const Model::Layer& L = model->layers[l];
     uint16_t* kvl = kv_->layer(l);
@@ -154,26 +171,17 @@ void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
     run_proj(gws_, pxn_, L.qkv, kQkvDim, kHidden, T, kEpiStore, pqkv_, nullptr, kQkvDim, &st_->err, model->num_sms, s);
     launch_qk_norm_rope_store(pqkv_, T, L.q_norm, L.k_norm, model->rope_cos, model->rope_sin,
                               kvl, page_table_, max_pages_, nullptr, nullptr, pos0, s);
-    AttnArgs a = {};
-    a.qkv = pqkv_;
-    a.qkv_stride = kQkvDim;
-    a.rope_cos = model->rope_cos;
-    a.rope_sin = model->rope_sin;
-    a.kv_layer = kvl;
-    a.page_table = page_table_;
-    a.max_pages = max_pages_;
-    a.pos_base = pos0;
-    a.rows = T;
-    a.fused_kv = 0;
-    // splits needed by the longest row (position pos0 + T - 1)
-    a.nsplit_max = ((pos0 + T + kPage - 1) / kPage + 31) / 32;
-    a.pages_per_split = 32;
-    a.part = ppart_;
-    a.counters = pcounters_;
-    a.out = pattn_;
-    a.err = &st_->err;
-    a.kv_row0 = l * kv_->pages * 2 * kKvHeads * kPage;
-    launch_attention(a, kv_->base, (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
+    PrefillAttnArgs pa = {};
+    pa.qkv = pqkv_;
+    pa.qkv_stride = kQkvDim;
+    pa.tiles = d_tiles_;
+    pa.page_table = page_table_;
+    pa.max_pages = max_pages_;
+    pa.kv_row0 = l * kv_->pages * 2 * kKvHeads * kPage;
+    pa.out = pattn_;
+    pa.err = &st_->err;
+    launch_attn_prefill(pa, ntiles, kv_->base,
+                        (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
     run_proj(gws_, pattn_, L.o, kHidden, kQDim, T, kEpiResid, px_, nullptr, kHidden, &st_->err, model->num_sms, s);
     launch_rmsnorm_bf16(px_, L.post_ln, pxn_, T, c.rms_norm_eps, s);
     run_proj(gws_, pxn_, L.gateup, 2 * kInter, kHidden, T, kEpiSwiglu, nullptr, pact_, kInter, &st_->err, model->num_sms, s);

@@ -158,6 +158,9 @@ class Decoder {
   uint16_t *pxn_ = nullptr, *pattn_ = nullptr, *pact_ = nullptr;
   int* pcounters_ = nullptr;
   float* ppart_ = nullptr;
+  PrefillTile* d_tiles_ = nullptr;
+  PrefillTile* h_tiles_ = nullptr;
+  int tiles_cap_ = 0;
   float* h_stage_ = nullptr;
   size_t h_stage_cap_ = 0;
   cudaGraphExec_t g1_ = nullptr, gk_ = nullptr;
@@ -215,6 +218,9 @@ class BatchDecoder {
   uint16_t *xn_ = nullptr, *attn_ = nullptr, *act_ = nullptr;
   int *counters_ = nullptr, *d_rows_ = nullptr, *d_tokens_ = nullptr, *d_out_ = nullptr;
   GemmWs gws_;
+  PrefillTile* d_tiles_ = nullptr;
+  PrefillTile* h_tiles_ = nullptr;
+  int tiles_cap_ = 0, ntiles_ = 0;
   int* h_step_[2] = {nullptr, nullptr};
   int* h_tbl_[2] = {nullptr, nullptr};
   int* h_out_ = nullptr;

@@ -87,6 +87,28 @@ void launch_attention(const AttnArgs& a, const uint16_t* kv_pool, long long pool
 bool make_tmap_2d(void* map, const void* base, long long rows, int cols, int box_cols,
                   int box_rows);
 
+// Causal prefill attention (attn_prefill.cu): tiles of up to prefill_tile_rows()
+// consecutive query positions of one session.
+struct PrefillTile {
+  int tab;    // page-table row of the session
+  int pos0;   // position of the tile's first row
+  int nrows;  // rows in the tile
+  int row0;   // first row in qkv / out
+};
+struct PrefillAttnArgs {
+  const float* qkv;  // normalised + roped q in cols [0, 2048)
+  int qkv_stride;
+  const PrefillTile* tiles;
+  const int* page_table;
+  int max_pages;
+  int kv_row0;       // first 128-wide row of this layer in the pool's tensor map
+  uint16_t* out;     // [rows, 2048] bf16
+  int* err;
+};
+void launch_attn_prefill(const PrefillAttnArgs& a, int ntiles, const uint16_t* kv_pool,
+                         long long pool_rows, cudaStream_t s);
+int prefill_tile_rows();
+
 // q/k RMSNorm + RoPE + K/V store for T prefill rows (q normalised in place).
 void launch_qk_norm_rope_store(float* qkv, int rows, const float* qn, const float* kn,
                                const float* cos, const float* sin, uint16_t* kv_layer,
