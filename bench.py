@@ -349,197 +349,6 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
-def run_ragged(dec, torch, world, dist):
-    """BASELINE config 3 on this GPU: 64 concurrent sessions, initial KV lengths
-    U[128, 2048] (seed 2), 16-token pages; every 16 steps 8 sessions (drawn
-    with the same generator) leave and 8 join with a 400-row prefill; 256 steps.
-    Returns decode tokens / wall time including the joins' prefills."""
-    from orator_b200 import BatchDecoder, synth_f32
-    rng = np.random.default_rng(2)
-    B, STEPS, PAGE = 64, 256, 16
-    init = rng.integers(128, 2049, B)
-    max_pages = (2048 + STEPS + 400 + PAGE) // PAGE + 1
-    bd = BatchDecoder(dec, max_sessions=B + 8, max_batch=B, pool_pages=(B + 8) * max_pages,
-                      max_pages_per_session=max_pages)
-    rows_buf = torch.empty(2048 * HIDDEN, dtype=torch.float32, device="cuda")
-
-    def embeds(n, tid):
-        synth_f32(rows_buf.data_ptr(), n * HIDDEN, SEED, tid, 1.0)
-        torch.cuda.synchronize()
-        return rows_buf[: n * HIDDEN].cpu().numpy().reshape(n, HIDDEN)
-
-    sids = []
-    for i in range(B):  # initial histories (untimed)
-        sid = bd.create_session()
-        bd.prefill([sid], [embeds(int(init[i]), 61000 + i)])
-        sids.append(sid)
-    joins = [embeds(PROMPT_ROWS, 62000 + j) for j in range(8)]
-    for _ in range(3):  # warm-up: eager step, graph capture, replay (state is advanced)
-        bd.step(sids)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    lens = {s: bd.cache_len(s) for s in sids}
-    sum_s = []
-    s0 = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    pre_ms = 0.0
-    e0.record(s0)
-    for step in range(STEPS):
-        if step and step % 16 == 0:
-            leave = rng.choice(len(sids), 8, replace=False)
-            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            p0.record(s0)
-            for k in sorted(leave, reverse=True):
-                bd.free_session(sids[k])
-                lens.pop(sids[k])
-                sids.pop(k)
-            new = [bd.create_session() for _ in range(8)]
-            bd.prefill(new, joins)
-            p1.record(s0)
-            p1.synchronize()
-            pre_ms += p0.elapsed_time(p1)
-            for n_ in new:
-                lens[n_] = PROMPT_ROWS
-            sids += new
-        sum_s.append(sum(lens[s] + 1 for s in sids))
-        bd.step(sids)
-        for s in sids:
-            lens[s] += 1
-    e1.record(s0)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    err = bd.device_error()
-    bd.close()
-    if dist:
-        t = torch.tensor([ms, pre_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, pre_ms = t.tolist()
-    tokens = B * STEPS * world
-    step_bytes = [WEIGHT_BYTES + KV_BYTES_PER_POS * x for x in sum_s]
-    dec_ms = ms - pre_ms
-    hbm, kind = peaks()
-    return {"workload": "config3: 64 ragged sessions per GPU, KV U[128,2048] (seed 2), "
-                        "8 leave + 8 join (400-row prefill) every 16 steps, 256 steps",
-            "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
-            "scaling": "weak", "ms_total": ms, "ms_prefill_joins": pre_ms,
-            "decode_only_tokens_per_s": tokens / (dec_ms / 1e3),
-            "mean_sum_kv": float(np.mean(sum_s)),
-            "step_hbm": {"bytes_per_step_mean": float(np.mean(step_bytes)),
-                         "achieved_gbs": float(np.sum(step_bytes)) / (dec_ms * 1e-3) / 1e9,
-                         "frac": float(np.sum(step_bytes)) / (dec_ms * 1e-3) / 1e9 / hbm},
-            "device_error": err}
-
-
-def run_ours(args):
-    import torch
-    rank, local, world = dist_env()
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    from orator_b200 import AsrTextConfig, AsrTextDecoder
-
-    dec = AsrTextDecoder(AsrTextConfig(max_seq_len=2816))  # room for config 3's longest session
-    dec.init_synthetic(SEED)
-    prompt = build_prompt_gpu(dec, torch)
-    dec.ResetCache()
-    dec.Prefill(prompt)
-
-    def step():
-        dec.TruncateCache(PROMPT_ROWS)
-        # ban_steps 0 and no EOS ids: every step decodes exactly 128 tokens
-        return dec.DecodeGreedy(PROMPT_ROWS, NEW_TOKENS, -1, -1, ban_steps=0, batch=NEW_TOKENS)
-
-    def barrier():
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    for _ in range(args.warmup):
-        step()
-    s = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local)
-    barrier()
-    with sampler:
-        e0.record(s)
-        for _ in range(args.steps):
-            toks = step()
-        e1.record(s)
-        barrier()
-    ms = e0.elapsed_time(e1)
-    clocks = sampler.summary()
-
-    # end to end through the public API: host prompt in (H2D), host tokens out (D2H)
-    for _ in range(1):
-        dec.ResetCache(); dec.Prefill(prompt); dec.DecodeGreedy(PROMPT_ROWS, NEW_TOKENS, -1, -1, 0, 32)
-    barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(s)
-    for _ in range(args.steps):
-        dec.ResetCache()
-        dec.Prefill(prompt)
-        dec.DecodeGreedy(PROMPT_ROWS, NEW_TOKENS, -1, -1, ban_steps=0, batch=32)
-    f1.record(s)
-    barrier()
-    e2e_ms = f0.elapsed_time(f1)
-
-    prof = dec.profile_kernels(iters=20)
-    ragged = None if args.no_ragged else run_ragged(dec, torch, world, dist)
-    if dist:
-        t = torch.tensor([ms, e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = t.tolist()
-    if rank != 0:
-        if dist:
-            dist.destroy_process_group()
-        return
-    tokens = NEW_TOKENS * args.steps * world
-    value = tokens / (ms / 1e3)
-    hbm, peak_kind = peaks()
-    lm_bytes = VOCAB * HIDDEN * 2 + HIDDEN * 4
-    lm_gbs = lm_bytes / (prof["lm_head"] * 1e-3) / 1e9
-    mean_s = PROMPT_ROWS + (NEW_TOKENS + 1) / 2
-    step_bytes = WEIGHT_BYTES + KV_BYTES_PER_POS * mean_s
-    tok_ms = ms / (NEW_TOKENS * args.steps)
-    line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded random-init weights, seeded N(0,1) audio rows)",
-        "config": {"workload": "config2: 28-layer Qwen3-ASR-1.7B decoder, 400-row prefill, "
-                               "greedy decode of 128 tokens at B=1 (KV 401..528)",
-                   "global_batch": world, "parallelism": f"replicas x{world} (independent sessions)",
-                   "l2": "inputs larger than L2 (3.44 GB of weights streamed per token)"},
-        "per_token_ms": tok_ms,
-        "step_hbm": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes / (tok_ms * 1e-3) / 1e9,
-                     "frac": step_bytes / (tok_ms * 1e-3) / 1e9 / hbm},
-        "roofline": {"bound": "hbm", "kernel": "gemv_kernel (lm_head launch, 622 MB)",
-                     "achieved": lm_gbs, "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
-                     "frac": lm_gbs / hbm, "traffic": None,
-                     "per_class_ms": prof},
-        "e2e": {"value": NEW_TOKENS * args.steps * world / (e2e_ms / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": PROMPT_ROWS * HIDDEN * 4,
-                "d2h_bytes_per_step": NEW_TOKENS * 4,
-                "note": "per step: Prefill(host 400x2048 fp32) + DecodeGreedy(128, batch 32) through the C ABI"},
-        "gpu_launches": args.steps * 2,  # seed argmax + one persistent decode launch per step
-        "clocks": clocks,
-    }
-    if ragged is not None:
-        line["ragged"] = ragged
-    if world == 1 and not args.no_cpu_baseline:
-        rate, threads, _ = cpu_oracle_rate(args.cpu_sample)
-        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": f"{args.cpu_sample} greedy decode tokens at KV 401.. "
-                                          "after a 400-row prefill (oracle restatement, fp32 torch)"}
-    print(json.dumps(line), flush=True)
-    if dist:
-        dist.destroy_process_group()
-
-
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
