@@ -344,9 +344,23 @@ def run_ours(args):
                      "gemv_kernel_lm_head": {"achieved_gbs": lm_gbs, "frac": lm_gbs / hbm,
                                              "note": "per-kernel path, 622 MB launch, CUDA events"},
                      "per_class_ms_per_kernel_path": prof},
-        "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+        "e2e": {"value": NEW_TOKENS * args.steps * world / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": PROMPT_ROWS * HIDDEN * 4,
+                "d2h_bytes_per_step": NEW_TOKENS * 4,
+                "note": "per step: Prefill(host 400x2048 fp32) + DecodeGreedy(128, batch 32) through the C ABI"},
+        "gpu_launches": args.steps * 2,  # seed argmax + one persistent decode launch per step
+        "clocks": clocks,
+    }
+    if ragged is not None:
+        line["ragged"] = ragged
+    if world == 1 and not args.no_cpu_baseline:
+        rate, threads, _ = cpu_oracle_rate(args.cpu_sample)
+        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": f"{args.cpu_sample} greedy decode tokens at KV 401.. "
+                                          "after a 400-row prefill (oracle restatement, fp32 torch)"}
     print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
 
 
 def main():
