@@ -22,11 +22,24 @@ void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int
   if (T <= 0) return;
   const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   const int tiles = (N / 128) * ((T + bn - 1) / bn);
-  // about two CTAs per SM, at least 256 of K per split
+  // Split-K by a small cost model of the persistent GEMM: rounds of items per
+  // CTA x k-blocks per item x time per k-block (weight + activation bytes at
+  // the per-SM share of HBM bandwidth, or the tensor time of the tile), plus
+  // the reduce kernel's extra traffic and launch.
+  auto cost = [&](int sp) {
+    const int items = tiles * sp, active = items < num_sms ? items : num_sms;
+    const double rounds = (items + num_sms - 1) / num_sms;
+    const double kb = K / 64.0 / sp;
+    const double bytes = (128.0 + bn) * 64 * 2;
+    const double per_sm_bw = std::min(6.4e12 / active, 90e9);
+    const double t_mem = bytes / per_sm_bw;
+    const double t_mma = 2.0 * 128 * bn * 64 / 10.8e12;
+    const double red = sp > 1 ? (sp * 8.0 * T * N) / 6.4e12 + 3e-6 : 0.0;
+    return rounds * kb * std::max(t_mem, t_mma) + red;
+  };
   int splits = 1;
-  while (tiles * splits * 2 <= 2 * num_sms && (K % (64 * splits * 2)) == 0 &&
-         K / (splits * 2) >= 256)
-    splits *= 2;
+  for (int sp = 2; sp <= 16; sp *= 2)
+    if (K % (64 * sp) == 0 && K / sp >= 128 && cost(sp) < cost(splits)) splits = sp;
   TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err, nullptr, nullptr};
   if (splits > 1) {
     const size_t need = (size_t)splits * T * N;

@@ -92,24 +92,32 @@ struct TcSmem {
   alignas(1024) uint8_t b[STAGES][BN * kBK * 2];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t done;
+  uint64_t acc_full[2];   // MMA -> epilogue: accumulator buffer ready
+  uint64_t acc_empty[2];  // epilogue -> MMA: accumulator buffer drained
   uint32_t tmem_base;
-  float swap[64][33];  // SwiGLU: up rows handed from warps 2-3 to warps 0-1
+  float swap[64][33];     // SwiGLU: up rows handed to the gate-row warps
 };
 
+// Persistent, warp-specialised GEMM. Work items (m tile, n tile, k split) are
+// strided over the CTAs; warp 0 streams TMA stages continuously across items,
+// warp 1 issues the MMAs into one of two TMEM accumulators, and warps 2-5 run
+// the epilogue of item i while the MMAs of item i + 1 proceed.
+constexpr int kTcWarps = 6;
+constexpr int kTcThreadsP = kTcWarps * 32;
+
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreadsP, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                   TcArgs g) {
+                   TcArgs g, int splits) {
   extern __shared__ uint8_t tc_raw[];
   TcSmem<BN, STAGES>& sm = *reinterpret_cast<TcSmem<BN, STAGES>*>(
       (reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * 128, n0 = blockIdx.y * BN;
-  const int kper = g.K / gridDim.z;
-  const int kbeg = blockIdx.z * kper;
-  const int KT = kper / kBK;
-  constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  const int mt = g.N / 128, nt = (g.T + BN - 1) / BN;
+  const int items = mt * nt * splits;
+  const int kper = g.K / splits, KT = kper / kBK;
+  constexpr int kTmemCols = 2 * (BN < 32 ? 32 : BN);  // two accumulators
+  constexpr int kAccCols = kTmemCols / 2;
   int* err = g.err;
 
   if (warp == 0) {
@@ -118,7 +126,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_init(&sm.full[s], 1);
         mbar_init(&sm.empty[s], 1);
       }
-      mbar_init(&sm.done, 1);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&sm.acc_full[b], 1);
+        mbar_init(&sm.acc_empty[b], 4);  // one arrival per epilogue warp
+      }
       fence_mbar_init();
     }
     __syncwarp();
@@ -134,95 +145,128 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem = sm.tmem_base;
   pdl_trigger();
 
-  if (warp == 0 && lane == 0) {
-    // ---- TMA producer (weights do not depend on the previous kernel) ----
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES;
-      if (kt >= STAGES && !mbar_wait(&sm.empty[s], ((kt / STAGES) - 1) & 1, err, 31)) break;
-      mbar_arrive_expect_tx(&sm.full[s], kATileB + BN * kBK * 2);
-      tma_load_2d(sm.a[s], &tmW, kbeg + kt * kBK, m0, &sm.full[s]);
-      if (kt == 0) pdl_wait();  // activations come from the previous kernel
-      tma_load_2d(sm.b[s], &tmX, kbeg + kt * kBK, n0, &sm.full[s]);
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer ----
-    constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) |
-                               (static_cast<uint32_t>(BN >> 3) << 17) | (8u << 24);
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES;
-      if (!mbar_wait(&sm.full[s], (kt / STAGES) & 1, err, 32)) break;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint64_t ad = umma_desc_sw128(smem_u32(sm.a[s]));
-      const uint64_t bd = umma_desc_sw128(smem_u32(sm.b[s]));
-#pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes per K=16 step inside the atom
-        umma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kt | kk) != 0);
-      umma_commit(&sm.empty[s]);
-    }
-    umma_commit(&sm.done);
-  }
-  __syncwarp();
+  auto decode_item = [&](int it, int& m0, int& n0, int& kz) {
+    kz = it % splits;
+    const int r = it / splits;
+    m0 = (r % mt) * 128;
+    n0 = (r / mt) * BN;
+  };
 
-  // ---- epilogue: all warps; warp w owns TMEM lanes (weight rows) 32w..32w+31 ----
-  pdl_wait();
-  mbar_wait(&sm.done, 0, err, 33);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const int row = m0 + warp * 32 + lane;
-  const uint32_t tbase = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  // Epilogue on 32 columns (tokens n0 + c0 .. +31) of this thread's weight row.
-  auto epilogue = [&](const float* v, int c0) {
-    if (g.epi == kEpiSwiglu) {
-      __syncthreads();
-      if (warp >= 2) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sm.swap[(warp - 2) * 32 + lane][i] = v[i];
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer: stages of all of this CTA's items back to back ----
+      int q = 0;  // stage sequence number
+      bool waited = false, ok = true;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        int m0, n0, kz;
+        decode_item(it, m0, n0, kz);
+        for (int kt = 0; kt < KT; ++kt, ++q) {
+          const int s = q % STAGES;
+          if (q >= STAGES && !mbar_wait(&sm.empty[s], ((q / STAGES) - 1) & 1, err, 31)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sm.full[s], kATileB + BN * kBK * 2);
+          const int k = kz * kper + kt * kBK;
+          tma_load_2d(sm.a[s], &tmW, k, m0, &sm.full[s]);
+          if (!waited) {
+            pdl_wait();  // activations come from the previous kernel
+            waited = true;
+          }
+          tma_load_2d(sm.b[s], &tmX, k, n0, &sm.full[s]);
+        }
       }
-      __syncthreads();
-      if (warp < 2) {
-        const int r = warp * 32 + lane;  // gate row within the tile
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                                 (static_cast<uint32_t>(BN >> 3) << 17) | (8u << 24);
+      int q = 0, j = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(&sm.acc_empty[b], ((j >> 1) - 1) & 1, err, 34)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc = tmem + b * kAccCols;
+        for (int kt = 0; kt < KT; ++kt, ++q) {
+          const int s = q % STAGES;
+          if (!mbar_wait(&sm.full[s], (q / STAGES) & 1, err, 32)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint64_t ad = umma_desc_sw128(smem_u32(sm.a[s]));
+          const uint64_t bd = umma_desc_sw128(smem_u32(sm.b[s]));
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int t = n0 + c0 + i;
-          if (c0 + i < BN && t < g.T) {
-            const float gt = v[i], up = sm.swap[r][i];
-            g.out_bf16[(long long)t * g.ldo + (m0 >> 1) + r] = f2bf((gt / (1.0f + expf(-gt))) * up);
+          for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes per K=16 step inside the atom
+            umma_f16(acc, ad + 2 * kk, bd + 2 * kk, idesc, (kt | kk) != 0);
+          umma_commit(&sm.empty[s]);
+        }
+        umma_commit(&sm.acc_full[b]);
+      }
+    }
+  } else {
+    // ---- epilogue warps 2..5: TMEM lane quarter = warp % 4 ----
+    pdl_wait();
+    const int quarter = warp & 3;
+    const int ew = warp - 2;  // 0..3 for the named barrier
+    (void)ew;
+    int j = 0;
+    for (int it = blockIdx.x; it < items; it += gridDim.x, ++j) {
+      int m0, n0, kz;
+      decode_item(it, m0, n0, kz);
+      const int b = j & 1;
+      mbar_wait(&sm.acc_full[b], (j >> 1) & 1, err, 33);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int rloc = quarter * 32 + lane;  // row within the 128-row tile
+      const int row = m0 + rloc;
+      const uint32_t tbase = tmem + b * kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tbase + c0, v);
+        if (splits > 1) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = n0 + c0 + i;
+            if (c0 + i < BN && t < g.T) g.ws[((long long)kz * g.T + t) * g.N + row] = v[i];
+          }
+        } else if (g.epi == kEpiSwiglu) {
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (rloc >= 64) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sm.swap[rloc - 64][i] = v[i];
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (rloc < 64) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int t = n0 + c0 + i;
+              if (c0 + i < BN && t < g.T) {
+                const float gt = v[i], up = sm.swap[rloc][i];
+                g.out_bf16[(long long)t * g.ldo + (m0 >> 1) + rloc] =
+                    f2bf((gt / (1.0f + expf(-gt))) * up);
+              }
+            }
+          }
+        } else {
+          float r[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = n0 + c0 + i;
+            r[i] = (g.epi == kEpiResid && c0 + i < BN && t < g.T)
+                       ? g.out_f32[(long long)t * g.ldo + row] : 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = n0 + c0 + i;
+            if (c0 + i < BN && t < g.T) g.out_f32[(long long)t * g.ldo + row] = r[i] + v[i];
           }
         }
       }
-    } else {
-      // residual: issue all 32 loads before any store (independent, pipelined)
-      float r[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int t = n0 + c0 + i;
-        r[i] = (g.epi == kEpiResid && c0 + i < BN && t < g.T)
-                   ? g.out_f32[(long long)t * g.ldo + row] : 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int t = n0 + c0 + i;
-        if (c0 + i < BN && t < g.T) g.out_f32[(long long)t * g.ldo + row] = r[i] + v[i];
-      }
-    }
-  };
-  if (gridDim.z == 1) {
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      float v[32];
-      tmem_ld32(tbase + c0, v);
-      epilogue(v, c0);
-    }
-  } else {
-    // Split over K: each split stores its partial tile to the workspace;
-    // splitk_reduce_kernel sums them in split order (deterministic) and runs
-    // the epilogue.
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      float v[32];
-      tmem_ld32(tbase + c0, v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int t = n0 + c0 + i;
-        if (c0 + i < BN && t < g.T) g.ws[((long long)blockIdx.z * g.T + t) * g.N + row] = v[i];
-      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -302,14 +346,20 @@ template <int BN, int STAGES>
 void launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& g, int splits,
                cudaStream_t s) {
   static bool configured = false;
+  static int sms = 148;
   const size_t smem = sizeof(TcSmem<BN, STAGES>) + 1024;
   if (!configured) {
     cudaFuncSetAttribute(tc_gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     configured = true;
   }
-  launch_pdl(tc_gemm_kernel<BN, STAGES>, dim3(g.N / 128, (g.T + BN - 1) / BN, splits),
-             dim3(kTcThreads), smem, s, mw, mx, g);
+  const int items = (g.N / 128) * ((g.T + BN - 1) / BN) * splits;
+  const int grid = items < sms ? items : sms;
+  launch_pdl(tc_gemm_kernel<BN, STAGES>, dim3(grid), dim3(kTcThreadsP), smem, s, mw, mx, g,
+             splits);
 }
 
 }  // namespace
@@ -341,7 +391,7 @@ void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int s
   switch (bn) {
     case 16: launch_bn<16, 8>(mw, mx, g, splits, s); break;
     case 32: launch_bn<32, 8>(mw, mx, g, splits, s); break;
-    case 64: launch_bn<64, 4>(mw, mx, g, splits, s); break;
+    case 64: launch_bn<64, 8>(mw, mx, g, splits, s); break;
     case 128: launch_bn<128, 6>(mw, mx, g, splits, s); break;
     default: launch_bn<256, 4>(mw, mx, g, splits, s); break;
   }
