@@ -13,6 +13,11 @@ Under torchrun every rank decodes its own independent session on its own GPU
 `--impl reference` times the reference's CPU path for this decoder -- the
 oracle restatement in oracle/ (the reference runtime itself is CUDA-only) --
 on the host cores.
+
+`roofline.traffic` is DRAM bytes from an ncu capture (dram__bytes_read.sum +
+dram__bytes_write.sum) of a 4-token decode_mk_kernel launch of this workload,
+3.4924 GB per token, scaled to the 128-token launch (weights exceed L2, so
+traffic grows in proportion to tokens).
 """
 from __future__ import annotations
 
@@ -38,6 +43,9 @@ HIDDEN, LAYERS, VOCAB = 2048, 28, 151936
 WEIGHT_BYTES = 3_440_902_144 + 495_616
 KV_BYTES_PER_POS = 28 * 2 * 8 * 128 * 2
 METRIC = "decode tokens/s (B=1, Qwen3-ASR-1.7B text decoder, bf16)"
+
+
+NCU_BYTES_PER_TOKEN = 3.4924e9  # DRAM bytes per decode token, from ncu
 
 
 def peaks():
@@ -339,7 +347,9 @@ def run_ours(args):
                      "achieved": step_bytes * NEW_TOKENS / (ms / args.steps * 1e-3) / 1e9,
                      "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": step_bytes * NEW_TOKENS / (ms / args.steps * 1e-3) / 1e9 / hbm,
-                     "traffic": None,
+                     # ncu dram__bytes_read+write of a 4-token launch (config 2,
+                     # KV 401..404) = 3.4924 GB per token, scaled to this launch
+                     "traffic": NCU_BYTES_PER_TOKEN * NEW_TOKENS,
                      "algorithmic_bytes_per_launch": step_bytes * NEW_TOKENS,
                      "gemv_kernel_lm_head": {"achieved_gbs": lm_gbs, "frac": lm_gbs / hbm,
                                              "note": "per-kernel path, 622 MB launch, CUDA events"},

@@ -40,6 +40,11 @@ void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int
   int splits = 1;
   for (int sp = 2; sp <= 16; sp *= 2)
     if (K % (64 * sp) == 0 && K / sp >= 128 && cost(sp) < cost(splits)) splits = sp;
+  static const int forced = [] {
+    const char* e = getenv("ORX_TC_SPLITS");  // tuning knob: force one split count
+    return e ? atoi(e) : 0;
+  }();
+  if (forced > 0 && K % (64 * forced) == 0) splits = forced;
   TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err, nullptr, nullptr};
   if (splits > 1) {
     const size_t need = (size_t)splits * T * N;

@@ -155,26 +155,40 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---- TMA producer: stages of all of this CTA's items back to back ----
-      int q = 0;  // stage sequence number
-      bool waited = false, ok = true;
-      for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-        int m0, n0, kz;
-        decode_item(it, m0, n0, kz);
-        for (int kt = 0; kt < KT; ++kt, ++q) {
-          const int s = q % STAGES;
-          if (q >= STAGES && !mbar_wait(&sm.empty[s], ((q / STAGES) - 1) & 1, err, 31)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&sm.full[s], kATileB + BN * kBK * 2);
-          const int k = kz * kper + kt * kBK;
-          tma_load_2d(sm.a[s], &tmW, k, m0, &sm.full[s]);
-          if (!waited) {
-            pdl_wait();  // activations come from the previous kernel
-            waited = true;
-          }
-          tma_load_2d(sm.b[s], &tmX, k, n0, &sm.full[s]);
-        }
+      // Weight tiles do not depend on the previous kernel, so the first
+      // STAGES of them are issued before griddepcontrol.wait; the matching
+      // activation tiles follow once the producer of X has finished.
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+      const int my_items = blockIdx.x < items ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+      const int total = my_items * KT;
+      const int pre = total < STAGES ? total : STAGES;
+      auto coords = [&](int q, int& k, int& m0, int& n0) {
+        const int j = q / KT, kt = q - j * KT;
+        int kz;
+        decode_item(blockIdx.x + j * gridDim.x, m0, n0, kz);
+        k = kz * kper + kt * kBK;
+      };
+      for (int q = 0; q < pre; ++q) {
+        int k, m0, n0;
+        coords(q, k, m0, n0);
+        mbar_arrive_expect_tx(&sm.full[q], kATileB + BN * kBK * 2);
+        tma_load_2d(sm.a[q], &tmW, k, m0, &sm.full[q]);
+      }
+      pdl_wait();  // activations come from the previous kernel
+      for (int q = 0; q < pre; ++q) {
+        int k, m0, n0;
+        coords(q, k, m0, n0);
+        tma_load_2d(sm.b[q], &tmX, k, n0, &sm.full[q]);
+      }
+      for (int q = pre; q < total; ++q) {
+        const int s = q % STAGES;
+        if (!mbar_wait(&sm.empty[s], ((q / STAGES) - 1) & 1, err, 31)) break;
+        int k, m0, n0;
+        coords(q, k, m0, n0);
+        mbar_arrive_expect_tx(&sm.full[s], kATileB + BN * kBK * 2);
+        tma_load_2d(sm.a[s], &tmW, k, m0, &sm.full[s]);
+        tma_load_2d(sm.b[s], &tmX, k, n0, &sm.full[s]);
       }
     }
   } else if (warp == 1) {

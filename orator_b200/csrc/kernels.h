@@ -119,18 +119,6 @@ void launch_qk_norm_rope_store(float* qkv, int rows, const float* qn, const floa
 void launch_rmsnorm_bf16(const float* x, const float* w, uint16_t* out, int rows, float eps,
                          cudaStream_t s);
 
-// Tensor-core GEMM out = A[M,K] * W[N,K]^T with fused epilogue.
-struct GemmArgs {
-  const uint16_t* A;  // [M, K] bf16
-  const uint16_t* W;  // [N, K] bf16
-  int M, N, K;
-  int epi;            // kEpiStore (fp32 out[M,N]), kEpiResid (out += ), kEpiSwiglu
-  float* out_f32;
-  uint16_t* out_bf16;  // SwiGLU: [M, N/2]
-  int ldo;             // leading dimension of the output
-};
-void launch_gemm(const GemmArgs& a, cudaStream_t s);
-
 // tcgen05 GEMM (gemm_tc.cu): out[t, n] (op)= sum_k X[t, k] W[n, k].
 struct TcArgs {
   int N, K, T;         // weight rows (multiple of 128), depth (multiple of 64 * splits), tokens
