@@ -149,6 +149,12 @@ int orx_decoder_profile_kernels(orx_decoder* d, int iters, void* stream, float* 
  * (returned in *launches_per_step). Advances cache_len by `steps`. */
 int orx_decoder_trace_decode(orx_decoder* d, int steps, void* stream, unsigned long long* out,
                              int* launches_per_step);
+/* Diagnostic (no reference counterpart), persistent decode kernel only: like
+ * trace_decode, but per phase and per CTA: out[(k * grid + cta) * 2 + {0, 1}]
+ * = {inputs of phase k ready, phase k done} for k < steps * L, global-timer ns;
+ * *grid receives the CTA count. ORX_EINVAL when the persistent kernel is off. */
+int orx_decoder_trace_ctas(orx_decoder* d, int steps, void* stream, unsigned long long* out,
+                           size_t out_len, int* grid);
 
 /* Allocation-free banned argmax (no counterpart in the reference; same result
  * as orx_decoder_argmax_to_device / asr_ops::ArgmaxBanned on the same logits).

@@ -71,6 +71,8 @@ _SIGS = {
                                             C.c_void_p]),
     "orx_decoder_trace_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                            C.POINTER(C.c_int)]),
+    "orx_decoder_trace_ctas": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_size_t,
+                                         C.POINTER(C.c_int)]),
     "orx_batch_create": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                    C.POINTER(C.c_void_p)]),
     "orx_batch_destroy": (None, [C.c_void_p]),

@@ -302,6 +302,18 @@ int orx_decoder_trace_decode(orx_decoder* d, int steps, void* stream,
   });
 }
 
+int orx_decoder_trace_ctas(orx_decoder* d, int steps, void* stream, unsigned long long* out,
+                           size_t out_len, int* grid) {
+  return guard([&] {
+    need(d, "decoder");
+    need(out, "out");
+    if (steps < 1) throw std::invalid_argument("steps must be >= 1");
+    DeviceScope ds(d->device);
+    const int g = d->dec->trace_ctas(steps, out, out_len, S(stream));
+    if (grid) *grid = g;
+  });
+}
+
 int orx_batch_create(orx_decoder* weights, int max_sessions, int max_batch, int pool_pages,
                      int max_pages_per_session, orx_batch** out) {
   return guard([&] {

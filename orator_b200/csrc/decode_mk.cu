@@ -54,8 +54,8 @@ struct MkSmem {
   float qs[2][kHeadDim];
   float sm_m[kW][2], sm_l[kW][2];
   float sm_acc[kW][2][kHeadDim];
-  float split_m[kQHeads][kMkMaxSplit];  // per q head: split maxima, then weights
-  float split_l[kQHeads][kMkMaxSplit];
+  int ptab[kMkMaxSplit * kP];                    // the page table, read once per launch
+  float xown[kMkOwnRows];  // this CTA's rows of the residual x (master copy)
 };
 
 // Units of a phase held by CTA `b` of `G` and the warp's count of chunks.
@@ -85,32 +85,32 @@ __device__ __forceinline__ int warp_units(int n, int warp) {
   return n > warp ? (n - warp + kW - 1) / kW : 0;
 }
 
-// Grid barrier #k: every CTA adds one arrival; passes when the counter holds
-// (k + 1) * G. Bounded: on timeout the error word is set and all later
-// barriers return at once.
+// Grid barrier #k: every CTA adds one arrival (a release reduction: no
+// round trip) and spins with acquire loads until the counter holds
+// (k + 1) * G. Bounded: the shared error word is consulted only after 20 us
+// of waiting (an earlier failure ends the wait then), and after the time
+// limit the error word is set; no trap.
 __device__ __forceinline__ void grid_barrier(unsigned int* ctr, unsigned int target, int* err) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(ctr, 1u);
-    if (*reinterpret_cast<volatile int*>(err) == 0) {
-      const unsigned long long t0 = global_ns();
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+    const unsigned long long t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
       unsigned int v;
-      for (;;) {
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
-        if (v >= target) break;
-        if (global_ns() - t0 > kBarrierNs) {
-          atomicExch(err, 21);
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+      if (v >= target) break;
+      if ((i & 63) == 0) {
+        const unsigned long long dt = global_ns() - t0;
+        if (dt > 20000ull && *reinterpret_cast<volatile int*>(err) != 0) break;
+        if (dt > kBarrierNs) {
+          atomicCAS(err, 0, 21);
           break;
         }
       }
     }
-    __threadfence();
   }
   __syncthreads();
 }
-
-
 
 __device__ __forceinline__ void cp_async16_mk(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
@@ -126,9 +126,13 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
   const int b = blockIdx.x, G = gridDim.x;
   int* err = &a.st->err;
   unsigned int bar_k = 0;  // barriers passed so far
+  auto ready = [&]() {  // this CTA's inputs of the coming phase are in place
+    if (a.trace_cta && tid == 0) a.trace_cta[((bar_k + 1) * G + b) * 2] = global_ns();
+  };
   auto barrier = [&]() {
     ++bar_k;
     if (a.trace && b == 0 && tid == 0) a.trace[2 * bar_k] = global_ns();   // arrive
+    if (a.trace_cta && tid == 0) a.trace_cta[(bar_k * G + b) * 2 + 1] = global_ns();
     grid_barrier(a.bar, bar_k * static_cast<unsigned int>(G), err);
     if (a.trace && b == 0 && tid == 0) a.trace[2 * bar_k + 1] = global_ns();  // depart
   };
@@ -239,7 +243,14 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
   };
 
   // RMSNorm of a fp32 row of 2048 (global, or given values) into sm.xs as bf16.
-  auto norm_to_xs = [&](const float* v8, const float* w) {
+  auto load_w8 = [&](const float* w, float* wv) {
+    const float4 w0 = reinterpret_cast<const float4*>(w)[tid * 2];
+    const float4 w1 = reinterpret_cast<const float4*>(w)[tid * 2 + 1];
+    wv[0] = w0.x; wv[1] = w0.y; wv[2] = w0.z; wv[3] = w0.w;
+    wv[4] = w1.x; wv[5] = w1.y; wv[6] = w1.z; wv[7] = w1.w;
+  };
+  // `wv`: this thread's 8 norm weights, loaded ahead (before the barrier).
+  auto norm_to_xs = [&](const float* v8, const float* wv) {
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) ss += v8[j] * v8[j];
@@ -250,9 +261,6 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
 #pragma unroll
     for (int w2 = 0; w2 < kW; ++w2) tot += sm.red[w2];
     const float inv = rsqrtf(tot / kHidden + a.eps);
-    const float4 w0 = reinterpret_cast<const float4*>(w)[tid * 2];
-    const float4 w1 = reinterpret_cast<const float4*>(w)[tid * 2 + 1];
-    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
     uint32_t pk[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
@@ -269,6 +277,41 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
   };
 
   const float scale = 0.08838834764831845f;  // 1/sqrt(128) as float
+  // rows of x this CTA owns in the o and down phases (same split of 2048)
+  const int u_own = u0ph[kPhO];
+  int n_own;
+  {
+    int u0;
+    unit_range(kHidden, b, G, u0, n_own);
+  }
+  float wn[8];  // norm weights of the coming phase
+  // Stage this CTA's first attention item of `layer` at position p into
+  // sm.pages (cache entries older than p are final; the owner of the last
+  // page patches row p itself). Issued one layer ahead, right after the
+  // previous attention phase, so the copies run under the o/gate-up/down
+  // phases instead of delaying the next qkv phase.
+  auto stage_first = [&](int layer, int p) {
+    const int np = (p + kPage) / kPage, ns = (np + kP - 1) / kP;
+    if (b >= kKvHeads * ns) return;
+    const int h0 = b / ns, s0 = b % ns;
+    const uint16_t* kvl = a.kv + (long long)layer * a.kv_layer_stride;
+    const int pb = s0 * kP, pe = pb + kP < np ? pb + kP : np;
+    const int n16 = (pe - pb) * 2 * kPage * 16;
+    for (int i = tid; i < n16; i += kT) {
+      const int pg = i / (2 * kPage * 16), rem = i % (2 * kPage * 16);
+      const int isv = rem / (kPage * 16), r = (rem / 16) % kPage, c = rem % 16;
+      const uint16_t* src = kvl + (long long)sm.ptab[pb + pg] * kPageElems +
+                            (isv ? kHalfPageElems : 0) + (h0 * kPage + r) * kHeadDim + c * 8;
+      uint8_t* base = sm.pages[pg];
+      cp_async16_mk(smem_u32(isv ? base + kKTileB + r * kHeadDim * 2 + c * 16
+                                 : base + r * kKRowB + c * 16), src);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int i = tid; i < kMkMaxSplit * kP; i += kT) sm.ptab[i] = i < a.max_pages ? a.page_table[i] : 0;
+  __syncthreads();
+  stage_first(0, a.pos0);
+
   for (int t = 0; t < a.steps; ++t) {
     const int pos = a.pos0 + t;
     int tok;
@@ -288,25 +331,6 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
     for (int l = 0; l < a.L; ++l) {
       const MkLayerW& Lw = a.layers[l];
       uint16_t* kvl = a.kv + (long long)l * a.kv_layer_stride;
-      // Stage this CTA's first attention item (cache entries older than `pos`
-      // are final) while the qkv phase streams.
-      const bool has_item = b < items;
-      const int h0 = has_item ? b / nsplit : 0, s0 = has_item ? b % nsplit : 0;
-      if (has_item) {
-        const int pb = s0 * kP, pe = pb + kP < npages ? pb + kP : npages;
-        const int n16 = (pe - pb) * 2 * kPage * 16;
-        for (int i = tid; i < n16; i += kT) {
-          const int pg = i / (2 * kPage * 16), rem = i % (2 * kPage * 16);
-          const int isv = rem / (kPage * 16), r = (rem / 16) % kPage, c = rem % 16;
-          const uint16_t* src = kvl + (long long)a.page_table[pb + pg] * kPageElems +
-                                (isv ? kHalfPageElems : 0) + (h0 * kPage + r) * kHeadDim + c * 8;
-          uint8_t* base = sm.pages[pg];
-          cp_async16_mk(smem_u32(isv ? base + kKTileB + r * kHeadDim * 2 + c * 16
-                                     : base + r * kKRowB + c * 16), src);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-      }
-
       // ---------------- qkv ----------------
       {
         float v8[8];
@@ -315,15 +339,13 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
           const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) { v8[2 * j] = bf_lo(ww[j]); v8[2 * j + 1] = bf_hi(ww[j]); }
-          if (b == 0) {
-            float4* xo = reinterpret_cast<float4*>(a.x) + tid * 2;
-            xo[0] = make_float4(v8[0], v8[1], v8[2], v8[3]);
-            xo[1] = make_float4(v8[4], v8[5], v8[6], v8[7]);
-          }
+          if (tid < n_own) sm.xown[tid] = bf2f(a.embed[(long long)tok * kHidden + u_own + tid]);
+          load_w8(Lw.in_ln, wn);
         } else {
           load_x8(v8);
         }
-        norm_to_xs(v8, Lw.in_ln);
+        norm_to_xs(v8, wn);
+        ready();
         run_phase(kPhQkv, [&](int u, float acc, float) { a.qkv[u] = acc; });
       }
       barrier();
@@ -339,7 +361,7 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
           for (int i = tid; i < n16; i += kT) {
             const int pg = i / (2 * kPage * 16), rem = i % (2 * kPage * 16);
             const int isv = rem / (kPage * 16), r = (rem / 16) % kPage, c = rem % 16;
-            const uint16_t* src = kvl + (long long)a.page_table[pb + pg] * kPageElems +
+            const uint16_t* src = kvl + (long long)sm.ptab[pb + pg] * kPageElems +
                                   (isv ? kHalfPageElems : 0) + (h * kPage + r) * kHeadDim + c * 8;
             uint8_t* base = sm.pages[pg];
             cp_async16_mk(smem_u32(isv ? base + kKTileB + r * kHeadDim * 2 + c * 16
@@ -387,7 +409,7 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
             knew[i] = lo * c - hi * sn;
             knew[i + 2] = hi * c + lo * sn;
           }
-          uint16_t* dst = kvl + (long long)a.page_table[pos / kPage] * kPageElems +
+          uint16_t* dst = kvl + (long long)sm.ptab[pos / kPage] * kPageElems +
                           (h * kPage + pos % kPage) * kHeadDim;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -397,6 +419,7 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();
+        if (it == b) ready();
         if (owner && warp == 2) {
           uint8_t* base = sm.pages[pos / kPage - pb];
           uint16_t* kd = reinterpret_cast<uint16_t*>(base + (pos % kPage) * kKRowB);
@@ -485,44 +508,35 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
           if (d == 0) { part[128] = mm; part[129] = ll; }
         }
       }
-      if (!has_item) asm volatile("cp.async.wait_all;" ::: "memory");
+      // pages are free again (the last item's reads precede its final sync)
+      if (l + 1 < a.L) stage_first(l + 1, pos);
+      else if (t + 1 < a.steps) stage_first(0, pos + 1);
       barrier();
 
       // ---------------- o (merges the attention splits) ----------------
       {
-        for (int idx = tid; idx < kQHeads * nsplit; idx += kT) {
-          const int qh = idx / nsplit, sp = idx % nsplit;
-          const float* ps = a.part + ((long long)(qh >> 1) * kMaxSplit + sp) * kPart + (qh & 1) * 132;
-          sm.split_m[qh][sp] = __ldcg(ps + 128);
-          sm.split_l[qh][sp] = __ldcg(ps + 129);
-        }
-        __syncthreads();
-        if (tid < kQHeads) {
-          float mm = -INFINITY;
-          for (int sp = 0; sp < nsplit; ++sp) mm = fmaxf(mm, sm.split_m[tid][sp]);
-          float ll = 0.f;
-          for (int sp = 0; sp < nsplit; ++sp) {
-            const float e = expf(sm.split_m[tid][sp] - mm);
-            ll += sm.split_l[tid][sp] * e;
-            sm.split_m[tid][sp] = e;
-          }
-          sm.split_l[tid][0] = ll;
-        }
-        __syncthreads();
+        // Every thread merges the splits of its 8 output dims in one pass of
+        // independent loads (running max, rescaled sums): one L2 round trip.
         const int d0 = tid * 8, qh = d0 / kHeadDim, h = qh >> 1, kk = qh & 1;
         const float* pbase = a.part + (long long)h * kMaxSplit * kPart + kk * 132;
         const int dd = d0 % kHeadDim;
         float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float mm = -INFINITY, ll = 0.f;
 #pragma unroll 4
         for (int sp = 0; sp < nsplit; ++sp) {
           const float* ps = pbase + sp * kPart;
-          const float e = sm.split_m[qh][sp];
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(ps + 128));
           const float4 q0 = __ldcg(reinterpret_cast<const float4*>(ps + dd));
           const float4 q1 = __ldcg(reinterpret_cast<const float4*>(ps + dd + 4));
-          o8[0] += q0.x * e; o8[1] += q0.y * e; o8[2] += q0.z * e; o8[3] += q0.w * e;
-          o8[4] += q1.x * e; o8[5] += q1.y * e; o8[6] += q1.z * e; o8[7] += q1.w * e;
+          const float mn = fmaxf(mm, ml.x);
+          const float co = expf(mm - mn), cs = expf(ml.x - mn);
+          ll = ll * co + ml.y * cs;
+          o8[0] = o8[0] * co + q0.x * cs; o8[1] = o8[1] * co + q0.y * cs;
+          o8[2] = o8[2] * co + q0.z * cs; o8[3] = o8[3] * co + q0.w * cs;
+          o8[4] = o8[4] * co + q1.x * cs; o8[5] = o8[5] * co + q1.y * cs;
+          o8[6] = o8[6] * co + q1.z * cs; o8[7] = o8[7] * co + q1.w * cs;
+          mm = mn;
         }
-        const float ll = sm.split_l[qh][0];
         const float inv = 1.0f / ll;
         uint32_t pk[4];
 #pragma unroll
@@ -531,15 +545,22 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
                   (static_cast<uint32_t>(f2bf(o8[2 * j + 1] * inv)) << 16);
         reinterpret_cast<uint4*>(sm.xs)[tid] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         __syncthreads();
-        run_phase(kPhO, [&](int u, float acc, float) { a.x[u] = __ldcg(a.x + u) + acc; });
+        ready();
+        run_phase(kPhO, [&](int u, float acc, float) {
+          const float xn = sm.xown[u - u_own] + acc;  // this lane wrote it last (down phase)
+          sm.xown[u - u_own] = xn;
+          a.x[u] = xn;
+        });
       }
+      load_w8(Lw.post_ln, wn);
       barrier();
 
       // ---------------- gate/up + SwiGLU ----------------
       {
         float v8[8];
         load_x8(v8);
-        norm_to_xs(v8, Lw.post_ln);
+        norm_to_xs(v8, wn);
+        ready();
         run_phase(kPhGu, [&](int u, float g, float up) {
           a.act_g[u] = f2bf((g / (1.0f + expf(-g))) * up);
         });
@@ -551,8 +572,14 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
         const uint4* src = reinterpret_cast<const uint4*>(a.act_g);
         for (int i = tid; i < kInter / 8; i += kT) reinterpret_cast<uint4*>(sm.xs)[i] = __ldcg(src + i);
         __syncthreads();
-        run_phase(kPhDown, [&](int u, float acc, float) { a.x[u] = __ldcg(a.x + u) + acc; });
+        ready();
+        run_phase(kPhDown, [&](int u, float acc, float) {
+          const float xn = sm.xown[u - u_own] + acc;
+          sm.xown[u - u_own] = xn;
+          a.x[u] = xn;
+        });
       }
+      load_w8(l + 1 < a.L ? a.layers[l + 1].in_ln : a.final_norm, wn);
       barrier();
     }
 
@@ -560,11 +587,12 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
     {
       float v8[8];
       load_x8(v8);
-      norm_to_xs(v8, a.final_norm);
+      norm_to_xs(v8, wn);
       const int count_after = a.record ? a.count0 + t + 1 : a.count0;
       const bool ban = count_after < a.ban_steps;
       const int bn0 = ban ? a.ban0 : -1, bn1 = ban ? a.ban1 : -1;
       unsigned long long best = 0ull;
+      ready();
       run_phase(kPhLm, [&](int u, float acc, float) {
         a.logits[u] = acc;
         if (u != bn0 && u != bn1 && !(acc != acc)) {
@@ -620,7 +648,7 @@ int decode_mk_max_grid() {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   launch_decode_mk_config();
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_mk_kernel, kT, decode_mk_smem());
-  return per >= 1 ? sms : 0;
+  return (per >= 1 && sms * kMkOwnRows >= kHidden) ? sms : 0;
 }
 
 }  // namespace orx

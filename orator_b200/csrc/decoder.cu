@@ -389,6 +389,7 @@ void Decoder::launch_mk(const int* tok_ptr, int steps, int pos0, int count0, boo
   a.bar = reinterpret_cast<unsigned int*>(mk_sync_ + 2);
   a.eps = c.rms_norm_eps;
   a.trace = mk_trace_;
+  a.trace_cta = mk_trace_cta_;
   ORX_CHECK(launch_decode_mk(a, model->num_sms, s));
 }
 
@@ -551,6 +552,25 @@ void Decoder::profile_kernels(int iters, float* ms, cudaStream_t s) {
   }
   ORX_CHECK(cudaEventDestroy(e0));
   ORX_CHECK(cudaEventDestroy(e1));
+}
+
+int Decoder::trace_ctas(int steps, unsigned long long* host_out, size_t out_len, cudaStream_t s) {
+  if (!use_mk_) throw std::invalid_argument("the persistent decode kernel is not in use");
+  const int per = 5 * model->cfg.num_layers + 1, G = model->num_sms;
+  const size_t n = ((size_t)steps * per + 1) * G * 2;
+  if (out_len < (size_t)steps * per * G * 2) throw std::invalid_argument("out_len too small");
+  unsigned long long* buf = dalloc<unsigned long long>(n);
+  ORX_CHECK(cudaMemset(buf, 0, n * 8));
+  mk_trace_cta_ = buf;
+  launch_mk(&st_->tok, steps, cache_len_, 0, false, true, 0, -1, -1, s);
+  mk_trace_cta_ = nullptr;
+  ORX_CHECK(cudaStreamSynchronize(s));
+  // slot k + 1 of the device buffer holds phase k (barrier numbers start at 1)
+  ORX_CHECK(cudaMemcpy(host_out, buf + (size_t)G * 2, (size_t)steps * per * G * 2 * 8,
+                       cudaMemcpyDeviceToHost));
+  cudaFree(buf);
+  cache_len_ += steps;
+  return G;
 }
 
 // Debug timeline of `steps` eager decode bodies from the current cache end:

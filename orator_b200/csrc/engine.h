@@ -116,6 +116,7 @@ class Decoder {
                    int only = -1);
   void profile_kernels(int iters, float* ms, cudaStream_t s);
   int trace_decode(int steps, unsigned long long* host_out, cudaStream_t s);
+  int trace_ctas(int steps, unsigned long long* host_out, size_t out_len, cudaStream_t s);
   void launch_mk(const int* tok_ptr, int steps, int pos0, int count0, bool record, bool finalize,
                  int ban_steps, int ban0, int ban1, cudaStream_t s);
   bool use_mk_ = false;
@@ -123,6 +124,7 @@ class Decoder {
   float* mk_part_ = nullptr;
   unsigned long long* mk_sync_ = nullptr;  // [best0, best1, barrier counter]
   unsigned long long* mk_trace_ = nullptr;
+  unsigned long long* mk_trace_cta_ = nullptr;
   unsigned long long* trace_ = nullptr;
 
   Model* model;

@@ -152,6 +152,7 @@ void launch_embed_rows(const uint16_t* table, const int* ids, float* out, int ro
 // Persistent cooperative decode kernel (decode_mk.cu).
 constexpr int kMkMaxSplit = 32;  // attention splits per kv head: 32 x 8 pages = 4096 positions
 constexpr int kMkPart = 2 * 132;
+constexpr int kMkOwnRows = 16;   // rows of x per CTA: needs a grid of at least 128 CTAs
 struct MkLayerW {
   const uint16_t *qkv, *o, *gu, *down;
   const float *in_ln, *post_ln, *qn, *kn;
@@ -181,6 +182,7 @@ struct MkArgs {
   unsigned int* bar;           // arrival counter, zero at launch
   float eps;
   unsigned long long* trace;   // optional: CTA 0 barrier arrive/depart times
+  unsigned long long* trace_cta;  // optional: per barrier k and CTA, {inputs ready, arrive}
 };
 cudaError_t launch_decode_mk(const MkArgs& a, int grid, cudaStream_t s);
 int decode_mk_max_grid();

@@ -193,6 +193,18 @@ class AsrTextDecoder:
              out.ctypes.data_as(C.c_void_p), C.byref(n))
         return out.reshape(steps, per, 3)
 
+    def trace_ctas(self, steps: int = 2, stream=None) -> np.ndarray:
+        """Per phase and CTA of the persistent decode kernel: [steps, per, grid, 2]
+        global-timer ns of {inputs ready, phase done} (diagnostic)."""
+        per = 5 * self.config.num_layers + 1
+        grid = C.c_int()
+        cap = steps * per * 1024 * 2
+        out = np.zeros(cap, np.uint64)
+        call("orx_decoder_trace_ctas", self._h, steps, _stream(stream),
+             out.ctypes.data_as(C.c_void_p), C.c_size_t(cap), C.byref(grid))
+        g = grid.value
+        return out[: steps * per * g * 2].reshape(steps, per, g, 2)
+
     def device_error(self) -> int:
         v = C.c_int()
         call("orx_decoder_device_error", self._h, C.byref(v))
