@@ -256,6 +256,61 @@ def run_ragged(dec, torch, world, dist):
             "device_error": err}
 
 
+def run_config1(torch, hbm, cpu: bool):
+    """Config 1: one fp32 decoder layer (seed 0), KV of 512 past positions built
+    by the layer itself from 512 N(0,1) rows, then one decode row at position
+    512, timed with CUDA events (truncate back to 512 between reps); the CPU
+    leg times the fp32 oracle restatement of the same step (100 reps, median)."""
+    from orator_b200 import AsrTextConfig, Layer32
+    past_rows, reps = 512, 100
+    g = torch.Generator().manual_seed(0)
+    past = torch.randn(past_rows, HIDDEN, generator=g).numpy()
+    query = torch.randn(1, HIDDEN, generator=g).numpy()
+    lay = Layer32(AsrTextConfig(num_layers=1, max_seq_len=past_rows + 16))
+    lay.init_synthetic(0, 0)
+    lay.forward(past, 0)
+    dq = torch.from_numpy(query).cuda()
+    dout = torch.empty_like(dq)
+    s = torch.cuda.current_stream()
+    for _ in range(5):
+        lay.truncate(past_rows)
+        lay.forward_device(dq.data_ptr(), 1, past_rows, dout.data_ptr(), s)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(reps):
+        lay.truncate(past_rows)
+        e0.record(s)
+        lay.forward_device(dq.data_ptr(), 1, past_rows, dout.data_ptr(), s)
+        e1.record(s)
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    lay.close()
+    us = statistics.median(ts)
+    nbytes = 201326592 + (2 * HIDDEN + 256) * 4 + 2 * (past_rows + 1) * 1024 * 4
+    out = {"workload": "config1: one fp32 Qwen3-1.7B-shaped layer, decode row at position 512 "
+                       "(KV 513 fp32), seed 0, B=1",
+           "gpu_us_per_step": us, "bytes_per_step": nbytes,
+           "achieved_gbs": nbytes / (us * 1e-6) / 1e9, "frac": nbytes / (us * 1e-6) / 1e9 / hbm,
+           "note": "6 launches per row (norm+qkv GEMV, q/k norm+RoPE+KV store, attention, "
+                   "o GEMV, norm+gate/up GEMV, down GEMV), median of 100 reps, L2 not flushed"}
+    if cpu:
+        from oracle import decoder_oracle as D
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        cfg = D.Config(num_layers=1, vocab_size=16, max_seq_len=past_rows + 16)
+        o = D.OracleDecoder(cfg, D.synthetic_weights(cfg, 0, bf16=False), quantize=False)
+        o.forward(past, 0)
+        ct = []
+        for _ in range(reps):
+            o.truncate(past_rows)
+            t0 = time.perf_counter()
+            o.forward(query, past_rows)
+            ct.append((time.perf_counter() - t0) * 1e6)
+        out["cpu_baseline"] = {"us_per_step": statistics.median(ct), "cores": threads,
+                               "kind": "port", "sample": "100 decode rows of the fp32 oracle layer"}
+    return out
+
+
 def run_ours(args):
     import torch
     rank, local, world = dist_env()
@@ -363,6 +418,8 @@ def run_ours(args):
     }
     if ragged is not None:
         line["ragged"] = ragged
+    if not args.no_config1:
+        line["config1"] = run_config1(torch, hbm, cpu=world == 1 and not args.no_cpu_baseline)
     if world == 1 and not args.no_cpu_baseline:
         rate, threads, _ = cpu_oracle_rate(args.cpu_sample)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -382,6 +439,7 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ragged", action="store_true", help="skip the config-3 ragged batch run")
+    ap.add_argument("--no-config1", action="store_true", help="skip the config-1 fp32 layer run")
     ap.add_argument("--tokens", type=int, default=128,
                     help="decode tokens per step (128 = config 2; smaller only for profiler runs)")
     args = ap.parse_args()

@@ -128,6 +128,31 @@ int orx_batch_prefill(orx_batch* b, const int* sids, const int* lens, int n,
 int orx_batch_step(orx_batch* b, const int* sids, int n, int* tokens_out, void* stream);
 int orx_batch_device_error(const orx_batch* b, int* out);
 
+/* ---- fp32 single decoder layer (correctness configuration; no reference GPU
+ * counterpart: the reference checks this layer in fp32 on its CPU oracle).
+ * One Qwen3-1.7B-shaped layer with fp32 weights, activations and KV cache and
+ * no bf16 rounding; rows are processed causally, each appending its K/V.
+ * Tensor names are layer-relative ("self_attn.q_proj", "mlp.down_proj", ...,
+ * as in thinker.model.layers.N.<name>.weight), fp32. */
+typedef struct orx_layer32 orx_layer32;
+/* Geometry from cfg must be the decoder's; uses max_seq_len, rms_norm_eps,
+ * rope_theta (max_seq_len <= 51200). */
+int orx_layer32_create(const orx_config* cfg, orx_layer32** out);
+void orx_layer32_destroy(orx_layer32* l);
+int orx_layer32_set_tensor(orx_layer32* l, const char* name, const float* data, size_t numel,
+                           int on_device);
+/* Seeded synthetic weights of decoder layer `layer`: the generator of
+ * orx_decoder_init_synthetic without the bf16 rounding. */
+int orx_layer32_init_synthetic(orx_layer32* l, int seed, int layer);
+/* T rows [T, 2048] at positions pos0.. (pos0 <= cache length) -> layer
+ * outputs [T, 2048]; host pointers, synchronous. */
+int orx_layer32_forward(orx_layer32* l, const float* x, int T, int pos0, float* out, void* stream);
+/* Same with device pointers, asynchronous on `stream`. */
+int orx_layer32_forward_device(orx_layer32* l, const float* d_x, int T, int pos0, float* d_out,
+                               void* stream);
+int orx_layer32_cache_len(const orx_layer32* l, int* out);
+int orx_layer32_truncate(orx_layer32* l, int len);
+
 /* asr_gemm::LinearPre (include/model/asr_gemm.h:36-38): out[M,N] = in[M,K] @ W[N,K]^T
  * with bf16 operands and fp32 accumulation, on the tcgen05 tensor cores.
  * Device pointers; asynchronous on `stream`. Supported here: bias == NULL,

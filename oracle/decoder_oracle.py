@@ -253,10 +253,12 @@ class OracleDecoder:
         return out
 
 
-def synthetic_weights(cfg: Config, seed: int) -> dict:
+def synthetic_weights(cfg: Config, seed: int, bf16: bool = True) -> dict:
+    """The seeded synthetic checkpoint; ``bf16=False`` keeps the unrounded fp32
+    values (the fp32 single-layer configuration)."""
     w = {}
     for name, tid, shape, is_norm in synth.model_tensors(
             seed, cfg.num_layers, cfg.vocab_size, cfg.hidden_size, cfg.num_q_heads,
             cfg.num_kv_heads, cfg.head_dim, cfg.intermediate_size):
-        w[name] = synth.make_tensor(seed, tid, shape, is_norm)
+        w[name] = synth.make_tensor(seed, tid, shape, is_norm, bf16=bf16)
     return w

@@ -7,3 +7,4 @@ in ``liborator_b200.so`` built from ``orator_b200/csrc``.
 from ._lib import OrxError, LIB_PATH  # noqa: F401
 from .decoder import AsrTextConfig, AsrTextDecoder, synth_f32  # noqa: F401
 from .batch import BatchDecoder  # noqa: F401
+from .layer32 import Layer32  # noqa: F401

@@ -85,6 +85,16 @@ _SIGS = {
                                     C.c_void_p]),
     "orx_batch_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "orx_batch_device_error": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "orx_layer32_create": (C.c_int, [C.POINTER(Config), C.POINTER(C.c_void_p)]),
+    "orx_layer32_destroy": (None, [C.c_void_p]),
+    "orx_layer32_set_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t, C.c_int]),
+    "orx_layer32_init_synthetic": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "orx_layer32_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                      C.c_void_p]),
+    "orx_layer32_forward_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                             C.c_void_p, C.c_void_p]),
+    "orx_layer32_cache_len": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "orx_layer32_truncate": (C.c_int, [C.c_void_p, C.c_int]),
     "orx_linear_pre": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                  C.c_int, C.c_int, C.c_void_p]),
     "orx_synth_f32": (C.c_int, [C.c_void_p, C.c_longlong, C.c_int, C.c_int, C.c_double,

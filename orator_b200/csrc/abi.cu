@@ -14,6 +14,13 @@ struct orx_decoder {
   int device = 0;
 };
 
+struct orx_layer32 {
+  orx::Layer32* l = nullptr;
+  int device = 0;
+  float* d_io = nullptr;  // staging for host calls: [cap rows in | cap rows out]
+  int cap = 0;
+};
+
 struct orx_batch {
   orx::BatchDecoder* b = nullptr;
   int device = 0;
@@ -391,6 +398,106 @@ int orx_batch_device_error(const orx_batch* b, int* out) {
     need(out, "out");
     DeviceScope ds(b->device);
     *out = b->b->device_error();
+  });
+}
+
+int orx_layer32_create(const orx_config* cfg, orx_layer32** out) {
+  return guard([&] {
+    need(cfg, "cfg");
+    need(out, "out");
+    *out = nullptr;
+    if (cfg->hidden_size != orx::kHidden || cfg->num_q_heads != orx::kQHeads ||
+        cfg->num_kv_heads != orx::kKvHeads || cfg->head_dim != orx::kHeadDim ||
+        cfg->intermediate_size != orx::kInter)
+      throw std::invalid_argument("only the Qwen3-ASR-1.7B head geometry is supported");
+    auto* h = new orx_layer32;
+    try {
+      orx::check(cudaGetDevice(&h->device), "cudaGetDevice");
+      h->l = orx::layer32_create(cfg->max_seq_len, cfg->rms_norm_eps, cfg->rope_theta);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+void orx_layer32_destroy(orx_layer32* l) {
+  if (!l) return;
+  DeviceScope ds(l->device);
+  orx::layer32_destroy(l->l);
+  if (l->d_io) cudaFree(l->d_io);
+  delete l;
+}
+
+int orx_layer32_set_tensor(orx_layer32* l, const char* name, const float* data, size_t numel,
+                           int on_device) {
+  return guard([&] {
+    need(l, "layer");
+    need(name, "name");
+    need(data, "data");
+    DeviceScope ds(l->device);
+    orx::layer32_set_tensor(l->l, name, data, numel, on_device != 0);
+  });
+}
+
+int orx_layer32_init_synthetic(orx_layer32* l, int seed, int layer) {
+  return guard([&] {
+    need(l, "layer");
+    if (layer < 0 || layer > 4000) throw std::invalid_argument("layer index out of range");
+    DeviceScope ds(l->device);
+    orx::layer32_init_synthetic(l->l, seed, layer);
+  });
+}
+
+int orx_layer32_forward_device(orx_layer32* l, const float* d_x, int T, int pos0, float* d_out,
+                               void* stream) {
+  return guard([&] {
+    need(l, "layer");
+    if (T <= 0) return;
+    need(d_x, "x");
+    need(d_out, "out");
+    DeviceScope ds(l->device);
+    orx::layer32_forward(l->l, d_x, T, pos0, d_out, S(stream));
+  });
+}
+
+int orx_layer32_forward(orx_layer32* l, const float* x, int T, int pos0, float* out, void* stream) {
+  return guard([&] {
+    need(l, "layer");
+    if (T <= 0) return;
+    need(x, "x");
+    need(out, "out");
+    DeviceScope ds(l->device);
+    if (T > l->cap) {
+      if (l->d_io) cudaFree(l->d_io);
+      l->d_io = nullptr;
+      l->cap = 0;
+      orx::check(cudaMalloc(&l->d_io, (size_t)2 * T * orx::kHidden * 4), "cudaMalloc");
+      l->cap = T;
+    }
+    const size_t n = (size_t)T * orx::kHidden;
+    float* din = l->d_io;
+    float* dout = l->d_io + (size_t)l->cap * orx::kHidden;
+    orx::check(cudaMemcpyAsync(din, x, n * 4, cudaMemcpyHostToDevice, S(stream)), "cudaMemcpyAsync");
+    orx::layer32_forward(l->l, din, T, pos0, dout, S(stream));
+    orx::check(cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, S(stream)), "cudaMemcpyAsync");
+    orx::check(cudaStreamSynchronize(S(stream)), "cudaStreamSynchronize");
+  });
+}
+
+int orx_layer32_cache_len(const orx_layer32* l, int* out) {
+  return guard([&] {
+    need(l, "layer");
+    need(out, "out");
+    *out = orx::layer32_len(l->l);
+  });
+}
+
+int orx_layer32_truncate(orx_layer32* l, int len) {
+  return guard([&] {
+    need(l, "layer");
+    orx::layer32_truncate(l->l, len);
   });
 }
 

@@ -235,4 +235,14 @@ class BatchDecoder {
   long long graph_gen_ = -1, buf_gen_ = 0;
 };
 
+// fp32 single decoder layer (layer32.cu): fp32 weights, activations and KV.
+struct Layer32;
+Layer32* layer32_create(int max_seq_len, float eps, float theta);
+void layer32_destroy(Layer32* l);
+void layer32_set_tensor(Layer32* l, const char* name, const float* src, size_t n, bool device_src);
+void layer32_init_synthetic(Layer32* l, int seed, int layer);
+void layer32_forward(Layer32* l, const float* d_in, int T, int pos0, float* d_out, cudaStream_t s);
+int layer32_len(const Layer32* l);
+void layer32_truncate(Layer32* l, int n);
+
 }  // namespace orx

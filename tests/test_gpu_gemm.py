@@ -38,3 +38,24 @@ def test_tc_gemm_rejects_unsupported(cuda):
     from orator_b200._lib import OrxError, call
     with pytest.raises(OrxError):
         call("orx_linear_pre", C.c_void_p(1), C.c_void_p(1), None, C.c_void_p(1), 4, 100, 128, 0, None)
+
+
+def test_gemm_deterministic(cuda):
+    """Repeated launches give bit-identical results."""
+    import torch
+    from orator_b200._lib import call
+    g = np.random.default_rng(7)
+    for M, K, N in [(64, 6144, 2048), (16, 2048, 2048), (1, 2048, 4096)]:
+        x = torch.from_numpy(g.uniform(-1, 1, (M, K)).astype(np.float32)).to(torch.bfloat16).cuda()
+        w = torch.from_numpy(g.uniform(-1, 1, (N, K)).astype(np.float32)).to(torch.bfloat16).cuda()
+        outs = []
+        for _ in range(2):
+            out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+            call("orx_linear_pre", C.c_void_p(x.data_ptr()), C.c_void_p(w.data_ptr()), None,
+                 C.c_void_p(out.data_ptr()), M, K, N, 0, None)
+            outs.append(out)
+        torch.cuda.synchronize()
+        assert torch.equal(outs[0], outs[1])
+        ref = x.double() @ w.double().T
+        err = (outs[0].double() - ref).abs().max() / ref.pow(2).mean().sqrt()
+        assert err < 5e-4
