@@ -174,18 +174,26 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_ragged(dec, torch, world, dist):
-    """BASELINE config 3 on this GPU: 64 concurrent sessions, initial KV lengths
+def run_ragged(dec, torch, world, dist, rank=0, strong=False):
+    """64 concurrent sessions, initial KV lengths
     U[128, 2048] (seed 2), 16-token pages; every 16 steps 8 sessions (drawn
     with the same generator) leave and 8 join with a 400-row prefill; 256 steps.
-    Returns decode tokens / wall time including the joins' prefills."""
+    weak: every GPU runs its own 64 sessions. strong: the 64 sessions are
+    sharded over the GPUs by SessionRouter (least total KV length with room),
+    joins included; every rank draws the same generator, so all agree on the
+    placement without messages. Returns decode tokens / wall time including
+    the joins' prefills (device time, max over ranks)."""
     from orator_b200 import BatchDecoder, synth_f32
+    from orator_b200.router import SessionRouter
     rng = np.random.default_rng(2)
     B, STEPS, PAGE = 64, 256, 16
     init = rng.integers(128, 2049, B)
     max_pages = (2048 + STEPS + 400 + PAGE) // PAGE + 1
-    bd = BatchDecoder(dec, max_sessions=B + 8, max_batch=B, pool_pages=(B + 8) * max_pages,
+    pool = (B + 8) * max_pages
+    bd = BatchDecoder(dec, max_sessions=B + 8, max_batch=B, pool_pages=pool,
                       max_pages_per_session=max_pages)
+    router = SessionRouter(world if strong else 1, pool, PAGE)
+    me = rank if strong else 0
     rows_buf = torch.empty(2048 * HIDDEN, dtype=torch.float32, device="cuda")
 
     def embeds(n, tid):
@@ -193,18 +201,27 @@ def run_ragged(dec, torch, world, dist):
         torch.cuda.synchronize()
         return rows_buf[: n * HIDDEN].cpu().numpy().reshape(n, HIDDEN)
 
-    sids = []
+    gids = list(range(B))            # global session ids, in draw order
+    local = {}                       # global id -> this rank's BatchDecoder session
+    next_gid = B
     for i in range(B):  # initial histories (untimed)
-        sid = bd.create_session()
-        bd.prefill([sid], [embeds(int(init[i]), 61000 + i)])
-        sids.append(sid)
+        if router.place(i, int(init[i]), STEPS) == me:
+            sid = bd.create_session()
+            bd.prefill([sid], [embeds(int(init[i]), 61000 + i)])
+            local[i] = sid
     joins = [embeds(PROMPT_ROWS, 62000 + j) for j in range(8)]
+
+    def my_sids():
+        return [local[g] for g in gids if g in local]
+
     for _ in range(3):  # warm-up: eager step, graph capture, replay (state is advanced)
-        bd.step(sids)
+        if my_sids():
+            bd.step(my_sids())
+        for g in gids:
+            router.grow(g)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    lens = {s: bd.cache_len(s) for s in sids}
     sum_s = []
     s0 = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -212,47 +229,56 @@ def run_ragged(dec, torch, world, dist):
     e0.record(s0)
     for step in range(STEPS):
         if step and step % 16 == 0:
-            leave = rng.choice(len(sids), 8, replace=False)
+            leave = rng.choice(len(gids), 8, replace=False)
             p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             p0.record(s0)
             for k in sorted(leave, reverse=True):
-                bd.free_session(sids[k])
-                lens.pop(sids[k])
-                sids.pop(k)
-            new = [bd.create_session() for _ in range(8)]
-            bd.prefill(new, joins)
+                g = gids.pop(k)
+                router.release(g)
+                if g in local:
+                    bd.free_session(local.pop(g))
+            mine = []
+            for j in range(8):
+                g = next_gid
+                next_gid += 1
+                gids.append(g)
+                if router.place(g, PROMPT_ROWS, STEPS) == me:
+                    local[g] = bd.create_session()
+                    mine.append((local[g], joins[j]))
+            if mine:
+                bd.prefill([m[0] for m in mine], [m[1] for m in mine])
             p1.record(s0)
             p1.synchronize()
             pre_ms += p0.elapsed_time(p1)
-            for n_ in new:
-                lens[n_] = PROMPT_ROWS
-            sids += new
-        sum_s.append(sum(lens[s] + 1 for s in sids))
-        bd.step(sids)
-        for s in sids:
-            lens[s] += 1
+        sum_s.append(sum(router.lens[g] + 1 for g in gids if g in local))
+        if my_sids():
+            bd.step(my_sids())
+        for g in gids:
+            router.grow(g)
     e1.record(s0)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     err = bd.device_error()
     bd.close()
-    if dist:
-        t = torch.tensor([ms, pre_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, pre_ms = t.tolist()
-    tokens = B * STEPS * world
     step_bytes = [WEIGHT_BYTES + KV_BYTES_PER_POS * x for x in sum_s]
     dec_ms = ms - pre_ms
+    if dist:
+        t = torch.tensor([ms, pre_ms, dec_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, pre_ms, dec_ms = t.tolist()
+    tokens = B * STEPS * (1 if strong else world)
     hbm, kind = peaks()
-    return {"workload": "config3: 64 ragged sessions per GPU, KV U[128,2048] (seed 2), "
-                        "8 leave + 8 join (400-row prefill) every 16 steps, 256 steps",
+    label = ("config3 strong: 64 ragged sessions sharded over the GPUs by least total KV length"
+             if strong else "config3: 64 ragged sessions per GPU")
+    return {"workload": label + ", KV U[128,2048] (seed 2), 8 leave + 8 join (400-row prefill) "
+                                "every 16 steps, 256 steps",
             "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
-            "scaling": "weak", "ms_total": ms, "ms_prefill_joins": pre_ms,
+            "scaling": "strong" if strong else "weak", "ms_total": ms, "ms_prefill_joins": pre_ms,
             "decode_only_tokens_per_s": tokens / (dec_ms / 1e3),
-            "mean_sum_kv": float(np.mean(sum_s)),
-            "step_hbm": {"bytes_per_step_mean": float(np.mean(step_bytes)),
-                         "achieved_gbs": float(np.sum(step_bytes)) / (dec_ms * 1e-3) / 1e9,
-                         "frac": float(np.sum(step_bytes)) / (dec_ms * 1e-3) / 1e9 / hbm},
+            "mean_sum_kv_rank": float(np.mean(sum_s)),
+            "step_hbm_rank": {"bytes_per_step_mean": float(np.mean(step_bytes)),
+                              "achieved_gbs": float(np.sum(step_bytes)) / (dec_ms * 1e-3) / 1e9,
+                              "frac": float(np.sum(step_bytes)) / (dec_ms * 1e-3) / 1e9 / hbm},
             "device_error": err}
 
 
@@ -368,7 +394,9 @@ def run_ours(args):
     e2e_ms = f0.elapsed_time(f1)
 
     prof = dec.profile_kernels(iters=20)
-    ragged = None if args.no_ragged else run_ragged(dec, torch, world, dist)
+    ragged = None if args.no_ragged else run_ragged(dec, torch, world, dist, rank)
+    ragged_strong = (run_ragged(dec, torch, world, dist, rank, strong=True)
+                     if world > 1 and not args.no_ragged else None)
     if dist:
         t = torch.tensor([ms, e2e_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -418,6 +446,8 @@ def run_ours(args):
     }
     if ragged is not None:
         line["ragged"] = ragged
+    if ragged_strong is not None:
+        line["ragged_strong"] = ragged_strong
     if not args.no_config1:
         line["config1"] = run_config1(torch, hbm, cpu=world == 1 and not args.no_cpu_baseline)
     if world == 1 and not args.no_cpu_baseline:
