@@ -174,7 +174,7 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_ragged(dec, torch, world, dist, rank=0, strong=False):
+def run_ragged(dec, torch, world, dist, rank=0, strong=False, steps=256):
     """64 concurrent sessions, initial KV lengths
     U[128, 2048] (seed 2), 16-token pages; every 16 steps 8 sessions (drawn
     with the same generator) leave and 8 join with a 400-row prefill; 256 steps.
@@ -186,7 +186,7 @@ def run_ragged(dec, torch, world, dist, rank=0, strong=False):
     from orator_b200 import BatchDecoder, synth_f32
     from orator_b200.router import SessionRouter
     rng = np.random.default_rng(2)
-    B, STEPS, PAGE = 64, 256, 16
+    B, STEPS, PAGE = 64, steps, 16
     init = rng.integers(128, 2049, B)
     max_pages = (2048 + STEPS + 400 + PAGE) // PAGE + 1
     pool = (B + 8) * max_pages
@@ -271,7 +271,7 @@ def run_ragged(dec, torch, world, dist, rank=0, strong=False):
     label = ("config3 strong: 64 ragged sessions sharded over the GPUs by least total KV length"
              if strong else "config3: 64 ragged sessions per GPU")
     return {"workload": label + ", KV U[128,2048] (seed 2), 8 leave + 8 join (400-row prefill) "
-                                "every 16 steps, 256 steps",
+                                f"every 16 steps, {STEPS} steps",
             "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
             "scaling": "strong" if strong else "weak", "ms_total": ms, "ms_prefill_joins": pre_ms,
             "decode_only_tokens_per_s": tokens / (dec_ms / 1e3),
@@ -344,7 +344,10 @@ def run_ours(args):
     dist = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        import datetime
+        # a rank that fails ends the others' next collective within 2 minutes
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=120))
     from orator_b200 import AsrTextConfig, AsrTextDecoder
 
     dec = AsrTextDecoder(AsrTextConfig(max_seq_len=2816))  # room for config 3's longest session
@@ -394,8 +397,8 @@ def run_ours(args):
     e2e_ms = f0.elapsed_time(f1)
 
     prof = dec.profile_kernels(iters=20)
-    ragged = None if args.no_ragged else run_ragged(dec, torch, world, dist, rank)
-    ragged_strong = (run_ragged(dec, torch, world, dist, rank, strong=True)
+    ragged = None if args.no_ragged else run_ragged(dec, torch, world, dist, rank, steps=args.ragged_steps)
+    ragged_strong = (run_ragged(dec, torch, world, dist, rank, strong=True, steps=args.ragged_steps)
                      if world > 1 and not args.no_ragged else None)
     if dist:
         t = torch.tensor([ms, e2e_ms], device="cuda")
@@ -470,6 +473,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ragged", action="store_true", help="skip the config-3 ragged batch run")
     ap.add_argument("--no-config1", action="store_true", help="skip the config-1 fp32 layer run")
+    ap.add_argument("--ragged-steps", type=int, default=256,
+                    help="decode steps of the config-3 runs (256 = the config; fewer for profiling)")
     ap.add_argument("--tokens", type=int, default=128,
                     help="decode tokens per step (128 = config 2; smaller only for profiler runs)")
     args = ap.parse_args()
