@@ -127,6 +127,13 @@ int orx_batch_prefill(orx_batch* b, const int* sids, const int* lens, int n,
  * batched step; tokens_out (host, n ints, may be NULL) receives them. */
 int orx_batch_step(orx_batch* b, const int* sids, int n, int* tokens_out, void* stream);
 int orx_batch_device_error(const orx_batch* b, int* out);
+/* Ban window of DecodeGreedy (asr_text_decoder.cu:698-857) per session: the
+ * session's next `steps` argmaxes (the one closing a prefill, then one per
+ * step) exclude token ids ban0 and ban1 (-1: none). Ordered on `stream`. */
+int orx_batch_set_ban(orx_batch* b, int sid, int ban0, int ban1, int steps, void* stream);
+/* Each listed session's pending greedy token (produced by its last prefill or
+ * step, fed by its next step), to host out[n]. Waits for `stream`. */
+int orx_batch_next_tokens(orx_batch* b, const int* sids, int n, int* out, void* stream);
 
 /* ---- fp32 single decoder layer (correctness configuration; no reference GPU
  * counterpart: the reference checks this layer in fp32 on its CPU oracle).

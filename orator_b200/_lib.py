@@ -85,6 +85,8 @@ _SIGS = {
                                     C.c_void_p]),
     "orx_batch_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "orx_batch_device_error": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "orx_batch_set_ban": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "orx_batch_next_tokens": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "orx_layer32_create": (C.c_int, [C.POINTER(Config), C.POINTER(C.c_void_p)]),
     "orx_layer32_destroy": (None, [C.c_void_p]),
     "orx_layer32_set_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t, C.c_int]),

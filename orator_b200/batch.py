@@ -70,6 +70,18 @@ class BatchDecoder:
              out.ctypes.data_as(C.c_void_p), _stream(stream))
         return out[:len(sids)]
 
+    def set_ban(self, sid: int, ban0: int, ban1: int, steps: int, stream=None):
+        """The session's next `steps` argmaxes exclude ban0 / ban1 (DecodeGreedy's ban window)."""
+        call("orx_batch_set_ban", self._h, sid, ban0, ban1, steps, _stream(stream))
+
+    def next_tokens(self, sids, stream=None) -> np.ndarray:
+        """Pending greedy token of each session (fed by its next step)."""
+        sids = np.ascontiguousarray(sids, np.int32)
+        out = np.zeros(max(len(sids), 1), np.int32)
+        call("orx_batch_next_tokens", self._h, sids.ctypes.data_as(C.c_void_p), len(sids),
+             out.ctypes.data_as(C.c_void_p), _stream(stream))
+        return out[:len(sids)]
+
     def device_error(self) -> int:
         v = C.c_int()
         call("orx_batch_device_error", self._h, C.byref(v))

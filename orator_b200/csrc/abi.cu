@@ -392,6 +392,25 @@ int orx_batch_step(orx_batch* b, const int* sids, int n, int* tokens_out, void* 
   });
 }
 
+int orx_batch_set_ban(orx_batch* b, int sid, int ban0, int ban1, int steps, void* stream) {
+  return guard([&] {
+    need(b, "batch");
+    DeviceScope ds(b->device);
+    b->b->set_ban(sid, ban0, ban1, steps, S(stream));
+  });
+}
+
+int orx_batch_next_tokens(orx_batch* b, const int* sids, int n, int* out, void* stream) {
+  return guard([&] {
+    need(b, "batch");
+    if (n <= 0) return;
+    need(sids, "sids");
+    need(out, "out");
+    DeviceScope ds(b->device);
+    b->b->next_tokens(sids, n, out, S(stream));
+  });
+}
+
 int orx_batch_device_error(const orx_batch* b, int* out) {
   return guard([&] {
     need(b, "batch");

@@ -34,18 +34,25 @@ __global__ void gather_tokens_embed(const int* next_tok, const int* row_table, c
   for (int i = threadIdx.x; i < kHidden; i += blockDim.x) x[(long long)r * kHidden + i] = bf2f(src[i]);
 }
 
-// Row-wise banned-free argmax of logits [rows, n]; writes next_tok[row_table[r]]
-// and out[r]. Exact ties resolve to the lowest index.
+// Row-wise argmax of logits [rows, n]; writes next_tok[row_table[r]] and
+// out[r]. Exact ties resolve to the lowest index. Session sid = row_table[r]
+// excludes ids ban[sid].x and .y while ban[sid].z > 0, and each argmax of
+// the session counts ban[sid].z down by one (the ban window of DecodeGreedy,
+// src/model/asr_text_decoder.cu:698-857: the argmax producing token k bans
+// the EOS ids iff k < ban_steps).
 __global__ void __launch_bounds__(1024) rows_argmax(const float* logits, int n, const int* row_table,
-                                                    int* next_tok, int* out) {
+                                                    int* next_tok, int* out, int4* ban) {
   pdl_wait();
   __shared__ unsigned long long sb[32];
   const int r = blockIdx.x;
   const float* x = logits + (long long)r * n;
+  const int sid = row_table[r];
+  const int4 bn = ban[sid];
+  const int b0 = bn.z > 0 ? bn.x : -1, b1 = bn.z > 0 ? bn.y : -1;
   unsigned long long best = 0ull;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const float v = x[i];
-    if (v != v) continue;
+    if (v != v || i == b0 || i == b1) continue;
     const unsigned long long k = argmax_key(v, i);
     best = k > best ? k : best;
   }
@@ -60,8 +67,9 @@ __global__ void __launch_bounds__(1024) rows_argmax(const float* logits, int n, 
     unsigned long long b = 0;
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) b = sb[w] > b ? sb[w] : b;
     const int tok = b ? argmax_key_index(b) : 0;
-    if (row_table) next_tok[row_table[r]] = tok;
+    next_tok[sid] = tok;
     if (out) out[r] = tok;
+    if (bn.z > 0) ban[sid].z = bn.z - 1;
   }
 }
 
@@ -89,6 +97,8 @@ BatchDecoder::BatchDecoder(Model* m, int max_sessions, int max_batch, int pool_p
   d_table_ = dalloc<int>((size_t)max_sessions * mps_);
   ORX_CHECK(cudaMemset(d_table_, 0, sizeof(int) * (size_t)max_sessions * mps_));
   d_next_tok_ = dalloc<int>(max_sessions);
+  d_ban_ = dalloc<int4>(max_sessions);
+  ORX_CHECK(cudaMemset(d_ban_, 0, sizeof(int4) * max_sessions));
   ORX_CHECK(cudaMemset(d_next_tok_, 0, sizeof(int) * max_sessions));
   st_ = dalloc<StepState>(1);
   StepState init = {};
@@ -106,7 +116,7 @@ BatchDecoder::BatchDecoder(Model* m, int max_sessions, int max_batch, int pool_p
 
 BatchDecoder::~BatchDecoder() {
   delete kv_;
-  for (void* p : {(void*)d_table_, (void*)d_next_tok_, (void*)st_, (void*)x_, (void*)xn_, (void*)qkv_,
+  for (void* p : {(void*)d_table_, (void*)d_next_tok_, (void*)d_ban_, (void*)st_, (void*)x_, (void*)xn_, (void*)qkv_,
                   (void*)attn_, (void*)act_, (void*)logits_, (void*)part_, (void*)counters_,
                   (void*)d_rows_, (void*)d_tokens_, (void*)d_out_, (void*)d_tiles_})
     if (p) cudaFree(p);
@@ -173,6 +183,24 @@ void BatchDecoder::free_session(int sid) {
   check_sid(sid);
   for (int p : sessions_[sid].pages) free_pages_.push_back(p);
   sessions_[sid] = Session{};
+  const int4 none = {-1, -1, 0, 0};
+  ORX_CHECK(cudaMemcpy(d_ban_ + sid, &none, sizeof(none), cudaMemcpyHostToDevice));
+}
+
+void BatchDecoder::next_tokens(const int* sids, int n, int* out, cudaStream_t s) const {
+  for (int i = 0; i < n; ++i) check_sid(sids[i]);
+  std::vector<int> all(max_sessions_);
+  ORX_CHECK(cudaStreamSynchronize(s));
+  ORX_CHECK(cudaMemcpy(all.data(), d_next_tok_, sizeof(int) * max_sessions_, cudaMemcpyDeviceToHost));
+  for (int i = 0; i < n; ++i) out[i] = all[sids[i]];
+}
+
+void BatchDecoder::set_ban(int sid, int ban0, int ban1, int steps, cudaStream_t s) {
+  check_sid(sid);
+  if (steps < 0) throw std::invalid_argument("negative ban window");
+  const int4 v = {ban0, ban1, steps, 0};
+  // pageable source: the copy has consumed `v` when the call returns
+  ORX_CHECK(cudaMemcpyAsync(d_ban_ + sid, &v, sizeof(v), cudaMemcpyHostToDevice, s));
 }
 
 int BatchDecoder::cache_len(int sid) const {
@@ -365,7 +393,7 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
   run_proj(gws_, xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr, c.vocab_size,
            &st_->err, model->num_sms, s);
   launch_pdl(rows_argmax, dim3(n), dim3(1024), 0, s, (const float*)logits_, c.vocab_size,
-             (const int*)d_out_, d_next_tok_, (int*)nullptr);
+             (const int*)d_out_, d_next_tok_, (int*)nullptr, d_ban_);
   ORX_CHECK(cudaGetLastError());
   ORX_CHECK(cudaStreamSynchronize(s));  // h_rows_ is reused by the next call
   for (int i = 0; i < n; ++i) sessions_[sids[i]].len += lens[i];
@@ -383,7 +411,7 @@ void BatchDecoder::record_step(int n, cudaStream_t s) {
   run_proj(gws_, xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr,
            c.vocab_size, &st_->err, model->num_sms, s);
   launch_pdl(rows_argmax, dim3(n), dim3(1024), 0, s, (const float*)logits_, c.vocab_size,
-             (const int*)d_rows_, d_next_tok_, d_out_);
+             (const int*)d_rows_, d_next_tok_, d_out_, d_ban_);
 }
 
 void BatchDecoder::step(const int* sids, int n, int* host_tokens_out, cudaStream_t s) {

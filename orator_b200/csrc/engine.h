@@ -186,6 +186,10 @@ class BatchDecoder {
   void prefill(const int* sids, const int* lens, int n, const float* host_embeds, cudaStream_t s);
   // One greedy token for each listed session (ragged lengths), batched.
   void step(const int* sids, int n, int* host_tokens_out, cudaStream_t s);
+  // The session's next `steps` argmaxes (prefill or step) exclude ban0/ban1.
+  void set_ban(int sid, int ban0, int ban1, int steps, cudaStream_t s);
+  // Each session's pending greedy token (the one its next step will feed).
+  void next_tokens(const int* sids, int n, int* out, cudaStream_t s) const;
   int free_pages() const { return static_cast<int>(free_pages_.size()); }
   int device_error() const;
   Model* model;
@@ -213,6 +217,7 @@ class BatchDecoder {
   bool dirty_ = true;
   int* d_table_ = nullptr;
   int* d_next_tok_ = nullptr;
+  int4* d_ban_ = nullptr;  // per session {ban0, ban1, argmaxes left to ban}
   StepState* st_ = nullptr;
   int* h_rows_ = nullptr;  // pinned staging
   int rows_cap_ = 0, logits_cap_ = 0;
