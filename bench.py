@@ -1,6 +1,6 @@
 """Benchmark of the Qwen3-ASR text-decoder hot path on B200.
 
-Workload: the 28-layer Qwen3-ASR-1.7B-shaped decoder in
+Workload (config 2 of the benchmark set): the 28-layer Qwen3-ASR-1.7B-shaped decoder in
 bf16 with seeded synthetic weights (seed 1); a 400-row prompt (375 audio rows
 N(0,1) + 25 token embeddings) is prefilled, then one bench step greedily
 decodes 128 tokens at batch 1 (KV length 401..528). Every step replays the
@@ -175,7 +175,7 @@ def run_reference(args):
 
 
 def run_ragged(dec, torch, world, dist, rank=0, strong=False, steps=256):
-    """64 concurrent sessions, initial KV lengths
+    """Config 3 of the benchmark set: 64 concurrent sessions, initial KV lengths
     U[128, 2048] (seed 2), 16-token pages; every 16 steps 8 sessions (drawn
     with the same generator) leave and 8 join with a 400-row prefill; 256 steps.
     weak: every GPU runs its own 64 sessions. strong: the 64 sessions are

@@ -9,7 +9,7 @@ greedy tokens and its logits at sampled vocabulary indices.
 
 Cases:
   l2   : 2 layers, prompt = 40 audio rows (seed 1), 16 greedy steps
-  cfg2 : 28 layers: 375 audio rows + 25 prompt token ids
+  cfg2 : 28 layers (benchmark config 2): 375 audio rows + 25 prompt token ids
          (seed 1), greedy decode of 128 tokens (no stop rule: the reference is
          stepped with DecodeStepDevice + its own argmax)
 """

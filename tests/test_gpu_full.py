@@ -1,4 +1,4 @@
-"""BASELINE config 2 on the GPU: the full 28-layer decoder against golden
+"""Benchmark config 2 on the GPU: the full 28-layer decoder against golden
 vectors produced by the reference build itself (tests/golden/ref_cfg2.npz).
 
 * teacher-forced: every one of the 128 steps is fed the reference's token;

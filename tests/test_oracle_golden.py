@@ -52,7 +52,7 @@ def test_oracle_matches_reference_two_layers():
 
 
 def test_oracle_matches_reference_config2_prefill():
-    """BASELINE config 2 (28 layers, 400-row prompt): prefill and two decode steps."""
+    """Benchmark config 2 (28 layers, 400-row prompt): prefill and two decode steps."""
     z = load("cfg2")
     cfg = D.Config(num_layers=28, vocab_size=151936, max_seq_len=420)
     o = D.OracleDecoder.synthetic(cfg, int(z["seed"]))
