@@ -45,6 +45,8 @@ KV_BYTES_PER_POS = 28 * 2 * 8 * 128 * 2
 METRIC = "decode tokens/s (B=1, Qwen3-ASR-1.7B text decoder, bf16)"
 
 
+WORKLOAD2 = ("config2: 28-layer Qwen3-ASR-1.7B decoder, 400-row prefill, "
+             "greedy decode of 128 tokens at B=1 (KV 401..528)")
 NCU_BYTES_PER_TOKEN = 3.4924e9  # DRAM bytes per decode token, from ncu
 
 
@@ -164,7 +166,8 @@ def run_reference(args):
             "ms_per_step": 1e3 * statistics.median(times), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16-rounded operands)",
             "data": "synthetic (seeded random-init weights, seeded N(0,1) audio rows)",
-            "config": {"workload": "config2: 28-layer decoder, 400-row prefill, greedy decode at B=1",
+            "config": {"workload": WORKLOAD2, "global_batch": 1,
+                       "parallelism": "host cores (rank 0 only)",
                        "sample": f"{args.cpu_sample} greedy tokens at KV 401..{400 + args.cpu_sample} per step",
                        "l2": "n/a (CPU)"},
             "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -421,8 +424,7 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random-init weights, seeded N(0,1) audio rows)",
-        "config": {"workload": "config2: 28-layer Qwen3-ASR-1.7B decoder, 400-row prefill, "
-                               "greedy decode of 128 tokens at B=1 (KV 401..528)",
+        "config": {"workload": WORKLOAD2,
                    "global_batch": world, "parallelism": f"replicas x{world} (independent sessions)",
                    "l2": "inputs larger than L2 (3.44 GB of weights streamed per token)"},
         "per_token_ms": tok_ms,
