@@ -34,23 +34,32 @@ __global__ void gather_tokens_embed(const int* next_tok, const int* row_table, c
   for (int i = threadIdx.x; i < kHidden; i += blockDim.x) x[(long long)r * kHidden + i] = bf2f(src[i]);
 }
 
-// Row-wise argmax of logits [rows, n]; writes next_tok[row_table[r]] and
-// out[r]. Exact ties resolve to the lowest index. Session sid = row_table[r]
-// excludes ids ban[sid].x and .y while ban[sid].z > 0, and each argmax of
-// the session counts ban[sid].z down by one (the ban window of DecodeGreedy,
+// Row-wise argmax of logits [rows, n], split over kArgmaxChunks CTAs per row
+// (grid (chunks, rows)): each CTA folds its slice into a 64-bit key
+// (orderable value << 32 | ~index, so equal values resolve to the lowest
+// index) with atomicMax on keys[r]; the last CTA of the row (ticket on
+// cnt[r]) writes next_tok[row_table[r]] and out[r] and resets keys[r] and
+// cnt[r] for the next launch. Session sid = row_table[r] excludes ids
+// ban[sid].x and .y while ban[sid].z > 0, and each argmax of the session
+// counts ban[sid].z down by one (the ban window of DecodeGreedy,
 // src/model/asr_text_decoder.cu:698-857: the argmax producing token k bans
 // the EOS ids iff k < ban_steps).
-__global__ void __launch_bounds__(1024) rows_argmax(const float* logits, int n, const int* row_table,
-                                                    int* next_tok, int* out, int4* ban) {
+constexpr int kArgmaxChunks = 16;
+
+__global__ void __launch_bounds__(512) rows_argmax(const float* logits, int n, const int* row_table,
+                                                   int* next_tok, int* out, int4* ban,
+                                                   unsigned long long* keys, int* cnt) {
   pdl_wait();
-  __shared__ unsigned long long sb[32];
-  const int r = blockIdx.x;
+  __shared__ unsigned long long sb[16];
+  const int r = blockIdx.y;
   const float* x = logits + (long long)r * n;
   const int sid = row_table[r];
   const int4 bn = ban[sid];
   const int b0 = bn.z > 0 ? bn.x : -1, b1 = bn.z > 0 ? bn.y : -1;
+  const int per = (n + gridDim.x - 1) / gridDim.x;
+  const int i0 = blockIdx.x * per, i1 = i0 + per < n ? i0 + per : n;
   unsigned long long best = 0ull;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
     const float v = x[i];
     if (v != v || i == b0 || i == b1) continue;
     const unsigned long long k = argmax_key(v, i);
@@ -66,10 +75,17 @@ __global__ void __launch_bounds__(1024) rows_argmax(const float* logits, int n, 
   if (threadIdx.x == 0) {
     unsigned long long b = 0;
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) b = sb[w] > b ? sb[w] : b;
-    const int tok = b ? argmax_key_index(b) : 0;
-    next_tok[sid] = tok;
-    if (out) out[r] = tok;
-    if (bn.z > 0) ban[sid].z = bn.z - 1;
+    if (b) atomicMax(keys + r, b);
+    __threadfence();
+    if (atomicAdd(cnt + r, 1) == static_cast<int>(gridDim.x) - 1) {
+      __threadfence();
+      const unsigned long long k = atomicExch(keys + r, 0ull);
+      const int tok = k ? argmax_key_index(k) : 0;
+      next_tok[sid] = tok;
+      if (out) out[r] = tok;
+      if (bn.z > 0) ban[sid].z = bn.z - 1;
+      cnt[r] = 0;
+    }
   }
 }
 
@@ -99,6 +115,13 @@ BatchDecoder::BatchDecoder(Model* m, int max_sessions, int max_batch, int pool_p
   d_next_tok_ = dalloc<int>(max_sessions);
   d_ban_ = dalloc<int4>(max_sessions);
   ORX_CHECK(cudaMemset(d_ban_, 0, sizeof(int4) * max_sessions));
+  {  // argmax scratch, one key and one ticket per row; reset by its last CTA
+    const int rows = std::max(max_sessions, max_batch);
+    d_amax_keys_ = dalloc<unsigned long long>(rows);
+    d_amax_cnt_ = dalloc<int>(rows);
+    ORX_CHECK(cudaMemset(d_amax_keys_, 0, sizeof(unsigned long long) * rows));
+    ORX_CHECK(cudaMemset(d_amax_cnt_, 0, sizeof(int) * rows));
+  }
   ORX_CHECK(cudaMemset(d_next_tok_, 0, sizeof(int) * max_sessions));
   st_ = dalloc<StepState>(1);
   StepState init = {};
@@ -116,7 +139,8 @@ BatchDecoder::BatchDecoder(Model* m, int max_sessions, int max_batch, int pool_p
 
 BatchDecoder::~BatchDecoder() {
   delete kv_;
-  for (void* p : {(void*)d_table_, (void*)d_next_tok_, (void*)d_ban_, (void*)st_, (void*)x_, (void*)xn_, (void*)qkv_,
+  for (void* p : {(void*)d_table_, (void*)d_next_tok_, (void*)d_ban_, (void*)d_amax_keys_,
+                  (void*)d_amax_cnt_, (void*)st_, (void*)x_, (void*)xn_, (void*)qkv_,
                   (void*)attn_, (void*)act_, (void*)logits_, (void*)part_, (void*)counters_,
                   (void*)d_rows_, (void*)d_tokens_, (void*)d_out_, (void*)d_tiles_})
     if (p) cudaFree(p);
@@ -275,7 +299,8 @@ void BatchDecoder::layers(int rows, int max_len, bool fused, cudaStream_t s) {
   for (int l = 0; l < c.num_layers; ++l) {
     const Model::Layer& L = model->layers[l];
     uint16_t* kvl = kv_->layer(l);
-    launch_rmsnorm_bf16(x_, L.in_ln, xn_, rows, c.rms_norm_eps, s);
+    // later layers' input norm comes fused with the previous down projection
+    if (l == 0) launch_rmsnorm_bf16(x_, L.in_ln, xn_, rows, c.rms_norm_eps, s);
     run_proj(gws_, xn_, L.qkv, kQkvDim, kHidden, rows, kEpiStore, qkv_, nullptr, kQkvDim, err, sms, s);
     if (!fused)
       launch_qk_norm_rope_store(qkv_, rows, L.q_norm, L.k_norm, model->rope_cos, model->rope_sin,
@@ -316,10 +341,14 @@ void BatchDecoder::layers(int rows, int max_len, bool fused, cudaStream_t s) {
       launch_attn_prefill(pa, ntiles_, kv_->base,
                           (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
     }
-    run_proj(gws_, attn_, L.o, kHidden, kQDim, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s);
-    launch_rmsnorm_bf16(x_, L.post_ln, xn_, rows, c.rms_norm_eps, s);
+    run_proj(gws_, attn_, L.o, kHidden, kQDim, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s,
+             L.post_ln, xn_, c.rms_norm_eps);
     run_proj(gws_, xn_, L.gateup, 2 * kInter, kHidden, rows, kEpiSwiglu, nullptr, act_, kInter, err, sms, s);
-    run_proj(gws_, act_, L.down, kHidden, kInter, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s);
+    // the next layer's input norm, or in a decode step the final norm
+    const float* next_norm = l + 1 < c.num_layers ? model->layers[l + 1].in_ln
+                                                   : (fused ? model->final_norm : nullptr);
+    run_proj(gws_, act_, L.down, kHidden, kInter, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s,
+             next_norm, xn_, c.rms_norm_eps);
   }
 }
 
@@ -392,8 +421,9 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
   launch_rmsnorm_bf16(qkv_, model->final_norm, xn_, n, c.rms_norm_eps, s);
   run_proj(gws_, xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr, c.vocab_size,
            &st_->err, model->num_sms, s);
-  launch_pdl(rows_argmax, dim3(n), dim3(1024), 0, s, (const float*)logits_, c.vocab_size,
-             (const int*)d_out_, d_next_tok_, (int*)nullptr, d_ban_);
+  launch_pdl(rows_argmax, dim3(kArgmaxChunks, n), dim3(512), 0, s, (const float*)logits_,
+             c.vocab_size, (const int*)d_out_, d_next_tok_, (int*)nullptr, d_ban_, d_amax_keys_,
+             d_amax_cnt_);
   ORX_CHECK(cudaGetLastError());
   ORX_CHECK(cudaStreamSynchronize(s));  // h_rows_ is reused by the next call
   for (int i = 0; i < n; ++i) sessions_[sids[i]].len += lens[i];
@@ -405,13 +435,13 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
 void BatchDecoder::record_step(int n, cudaStream_t s) {
   launch_pdl(gather_tokens_embed, dim3(n), dim3(256), 0, s, (const int*)d_next_tok_,
              (const int*)d_rows_, (const uint16_t*)model->embed, d_tokens_, x_);
-  layers(n, mps_ * kPage, true, s);
+  layers(n, mps_ * kPage, true, s);  // ends with the final norm of every row in xn_
   const auto& c = model->cfg;
-  launch_rmsnorm_bf16(x_, model->final_norm, xn_, n, c.rms_norm_eps, s);
   run_proj(gws_, xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr,
            c.vocab_size, &st_->err, model->num_sms, s);
-  launch_pdl(rows_argmax, dim3(n), dim3(1024), 0, s, (const float*)logits_, c.vocab_size,
-             (const int*)d_rows_, d_next_tok_, d_out_, d_ban_);
+  launch_pdl(rows_argmax, dim3(kArgmaxChunks, n), dim3(512), 0, s, (const float*)logits_,
+             c.vocab_size, (const int*)d_rows_, d_next_tok_, d_out_, d_ban_, d_amax_keys_,
+             d_amax_cnt_);
 }
 
 void BatchDecoder::step(const int* sids, int n, int* host_tokens_out, cudaStream_t s) {

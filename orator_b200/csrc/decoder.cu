@@ -18,7 +18,8 @@ GemmWs::~GemmWs() {
 }
 
 void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi,
-              float* out_f32, uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s) {
+              float* out_f32, uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s,
+              const float* norm_w, uint16_t* norm_out, float eps) {
   if (T <= 0) return;
   const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   const int tiles = (N / 128) * ((T + bn - 1) / bn);
@@ -31,7 +32,7 @@ void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int
     const double rounds = (items + num_sms - 1) / num_sms;
     const double kb = K / 64.0 / sp;
     const double bytes = (128.0 + bn) * 64 * 2;
-    const double per_sm_bw = std::min(6.4e12 / active, 90e9);
+    const double per_sm_bw = std::min(6.4e12 / active, 55e9);  // measured per-CTA stream rate
     const double t_mem = bytes / per_sm_bw;
     const double t_mma = 2.0 * 128 * bn * 64 / 10.8e12;
     const double red = sp > 1 ? (sp * 8.0 * T * N) / 6.4e12 + 3e-6 : 0.0;
@@ -45,7 +46,7 @@ void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int
     return e ? atoi(e) : 0;
   }();
   if (forced > 0 && K % (64 * forced) == 0) splits = forced;
-  TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err, nullptr, nullptr};
+  TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err, nullptr, nullptr, norm_w, norm_out, eps};
   if (splits > 1) {
     const size_t need = (size_t)splits * T * N;
     if (need > w.cap) {

@@ -47,8 +47,11 @@ struct GemmWs {
   int cnt_cap = 0;
   ~GemmWs();
 };
+// norm_w / norm_out: RMSNorm of the residual output rows to bf16 right after
+// the projection (fused into the split-K reduction when there is one).
 void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi,
-              float* out_f32, uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s);
+              float* out_f32, uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s,
+              const float* norm_w = nullptr, uint16_t* norm_out = nullptr, float eps = 0.f);
 
 class Model {
  public:
@@ -218,6 +221,8 @@ class BatchDecoder {
   int* d_table_ = nullptr;
   int* d_next_tok_ = nullptr;
   int4* d_ban_ = nullptr;  // per session {ban0, ban1, argmaxes left to ban}
+  unsigned long long* d_amax_keys_ = nullptr;  // split argmax: per-row packed best
+  int* d_amax_cnt_ = nullptr;                  // split argmax: per-row CTA tickets
   StepState* st_ = nullptr;
   int* h_rows_ = nullptr;  // pinned staging
   int rows_cap_ = 0, logits_cap_ = 0;

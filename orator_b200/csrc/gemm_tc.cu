@@ -336,6 +336,53 @@ __global__ void splitk_reduce_kernel(TcArgs g, int splits) {
   }
 }
 
+// Split-K reduction of residual rows of 2048 fused with the RMSNorm that
+// follows (one CTA per token row, 8 columns per thread): x += sum of the
+// partials in split order, then xn = bf16(x * rsqrtf(mean(x^2) + eps) * w),
+// the same operations in the same order as splitk_reduce_kernel followed by
+// rmsnorm_bf16_kernel.
+__global__ void __launch_bounds__(256) splitk_reduce_norm_kernel(TcArgs g, int splits) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[8];
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const long long n = (long long)g.T * g.N;
+  const long long off = (long long)t * g.N + tid * 8;
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int z = 0; z < splits; ++z) {
+    const float4* p = reinterpret_cast<const float4*>(g.ws + z * n + off);
+    const float4 p0 = p[0], p1 = p[1];
+    a[0] += p0.x; a[1] += p0.y; a[2] += p0.z; a[3] += p0.w;
+    a[4] += p1.x; a[5] += p1.y; a[6] += p1.z; a[7] += p1.w;
+  }
+  float4* xo = reinterpret_cast<float4*>(g.out_f32 + (long long)t * g.ldo + tid * 8);
+  const float4 x0 = xo[0], x1 = xo[1];
+  const float v[8] = {x0.x + a[0], x0.y + a[1], x0.z + a[2], x0.w + a[3],
+                      x1.x + a[4], x1.y + a[5], x1.z + a[6], x1.w + a[7]};
+  xo[0] = make_float4(v[0], v[1], v[2], v[3]);
+  xo[1] = make_float4(v[4], v[5], v[6], v[7]);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float inv = rsqrtf(tot / kHidden + g.eps);
+  const float4* wi = reinterpret_cast<const float4*>(g.norm_w) + tid * 2;
+  const float4 w0 = wi[0], w1 = wi[1];
+  const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  uint32_t pk[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    pk[j] = static_cast<uint32_t>(f2bf(v[2 * j] * inv * wv[2 * j])) |
+            (static_cast<uint32_t>(f2bf(v[2 * j + 1] * inv * wv[2 * j + 1])) << 16);
+  reinterpret_cast<uint4*>(g.norm_out + (long long)t * kHidden)[tid] =
+      make_uint4(pk[0], pk[1], pk[2], pk[3]);
+}
+
 // SwiGLU after split-K: output j of token t pairs gate row (j/64)*128 + j%64
 // with the up row 64 further in the same 128-row tile.
 __global__ void splitk_swiglu_kernel(TcArgs g, int splits) {
@@ -409,13 +456,22 @@ void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int s
     case 128: launch_bn<128, 6>(mw, mx, g, splits, s); break;
     default: launch_bn<256, 4>(mw, mx, g, splits, s); break;
   }
+  const bool norm = g.norm_w != nullptr;
+  if (norm && (g.N != kHidden || g.ldo != kHidden || g.epi != kEpiResid)) {
+    fprintf(stderr, "orx: fused RMSNorm needs residual rows of 2048\n");
+    return;
+  }
   if (splits > 1) {
     const long long n = (long long)g.T * g.N;
     const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, 148 * 16));
     if (g.epi == kEpiSwiglu)
       launch_pdl(splitk_swiglu_kernel, dim3(grid), dim3(256), 0, s, g, splits);
+    else if (norm)
+      launch_pdl(splitk_reduce_norm_kernel, dim3(g.T), dim3(256), 0, s, g, splits);
     else
       launch_pdl(splitk_reduce_kernel, dim3(grid), dim3(256), 0, s, g, splits);
+  } else if (norm) {
+    launch_rmsnorm_bf16(g.out_f32, g.norm_w, g.norm_out, g.T, g.eps, s);
   }
 }
 

@@ -129,6 +129,11 @@ struct TcArgs {
   int* err;
   float* ws;           // split-K partials [splits, T, N]
   int* unused;
+  // Optional RMSNorm of the (residual) output rows to bf16 (N == 2048):
+  // fused into the split-K reduction, else a separate row kernel.
+  const float* norm_w;
+  uint16_t* norm_out;
+  float eps;
 };
 // X: [T, K] bf16 row-major (device), W: [N, K] bf16. splits divides K / 64.
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
