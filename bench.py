@@ -213,6 +213,10 @@ def run_ragged(dec, torch, world, dist, rank=0, strong=False, steps=256):
             bd.prefill([sid], [embeds(int(init[i]), 61000 + i)])
             local[i] = sid
     joins = [embeds(PROMPT_ROWS, 62000 + j) for j in range(8)]
+    # the join rows sit in pinned host memory, as an encoder's output would
+    joins_pinned = torch.empty((8 * PROMPT_ROWS, HIDDEN), dtype=torch.float32, pin_memory=True)
+    joins_pinned.copy_(torch.from_numpy(np.concatenate(joins, 0)))
+    joins_cat = joins_pinned.numpy()
 
     def my_sids():
         return [local[g] for g in gids if g in local]
@@ -248,7 +252,9 @@ def run_ragged(dec, torch, world, dist, rank=0, strong=False, steps=256):
                 if router.place(g, PROMPT_ROWS, STEPS) == me:
                     local[g] = bd.create_session()
                     mine.append((local[g], joins[j]))
-            if mine:
+            if len(mine) == 8:
+                bd.prefill([m[0] for m in mine], joins_cat, lens=[PROMPT_ROWS] * 8)
+            elif mine:
                 bd.prefill([m[0] for m in mine], [m[1] for m in mine])
             p1.record(s0)
             p1.synchronize()

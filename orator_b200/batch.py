@@ -55,10 +55,19 @@ class BatchDecoder:
         call("orx_batch_free_pages", self._h, C.byref(v))
         return v.value
 
-    def prefill(self, sids, embeds_list, stream=None):
+    def prefill(self, sids, embeds_list, stream=None, lens=None):
+        """Appends rows to each session: `embeds_list` is one [T_i, 2048] array
+        per session, or (with `lens`) the rows of all sessions already
+        concatenated (e.g. in pinned memory, copied as is)."""
         sids = np.ascontiguousarray(sids, np.int32)
-        lens = np.array([len(e) for e in embeds_list], np.int32)
-        x = np.ascontiguousarray(np.concatenate(embeds_list, 0), np.float32)
+        if lens is None:
+            lens = np.array([len(e) for e in embeds_list], np.int32)
+            x = np.ascontiguousarray(np.concatenate(embeds_list, 0), np.float32)
+        else:
+            lens = np.ascontiguousarray(lens, np.int32)
+            x = embeds_list
+            if x.dtype != np.float32 or not x.flags["C_CONTIGUOUS"] or len(x) != int(lens.sum()):
+                raise ValueError("concatenated rows must be contiguous fp32 [sum(lens), 2048]")
         call("orx_batch_prefill", self._h, sids.ctypes.data_as(C.c_void_p),
              lens.ctypes.data_as(C.c_void_p), len(sids), x.ctypes.data_as(C.c_void_p),
              _stream(stream))

@@ -321,10 +321,16 @@ __global__ void __launch_bounds__(kAttnThreads, 3)
     part[d] = aav[q];
     if (d == 0) { part[128] = mmv[q]; part[129] = llv[q]; }
   }
-  __threadfence();
+  // One acquire-release ticket per CTA publishes the partial written by all
+  // its threads (ordered before it by the barrier) and, for the last CTA of
+  // the (row, head), acquires every other split's partial.
   __syncthreads();
   if (t == 0) {
-    const int ticket = atomicAdd(&a.counters[row * kKvHeads + h], 1);
+    int ticket;
+    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
+                 : "=r"(ticket)
+                 : "l"(&a.counters[row * kKvHeads + h])
+                 : "memory");
     sm_last = (ticket == nsplit - 1);
   }
   __syncthreads();
@@ -332,7 +338,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3)
     trace_mark(a.trace, 2);
     return;
   }
-  __threadfence();
   // Combine the splits: per-split (m, l) staged in shared memory, then every
   // thread sums its output dimensions over the splits.
   __shared__ float sw[2][kMaxSplits];
