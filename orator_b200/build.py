@@ -29,7 +29,8 @@ def _sources():
 
 def _headers_mtime():
     hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
-    hs.append(os.path.join(ROOT, "include", "orx.h"))
+    inc = os.path.join(ROOT, "include")
+    hs += [os.path.join(dp, f) for dp, _, fs in os.walk(inc) for f in fs if f.endswith(".h")]
     return max(os.path.getmtime(h) for h in hs if os.path.exists(h))
 
 
