@@ -127,3 +127,71 @@ def test_cpp_decoder_and_pool_match_python(tmp_path, cuda):
     assert cpp_pool == py_pool
     bd.close()
     d.close()
+
+
+STREAM_PROGRAM = r"""
+#include <cstdio>
+#include <vector>
+#include "orator_b200/asr_stream.h"
+using namespace orator::model;
+int main(int argc, char** argv) {
+  if (argc < 2) return 2;
+  const int T = 20;
+  std::vector<float> x(2 * T * 2048);
+  FILE* f = std::fopen(argv[1], "rb");
+  if (!f || std::fread(x.data(), 4, x.size(), f) != x.size()) return 2;
+  std::fclose(f);
+  AsrTextConfig c;
+  c.num_layers = 2;
+  c.max_seq_len = 256;
+  AsrTextDecoder d(c);
+  d.InitSynthetic(9);
+  AsrSessionPool pool(d, 4, 4, 64, 16);
+  AsrStreamPool s(d, pool, 10, 3);
+  const int a = s.Open({1000, 1001});
+  const int b = s.Open({1002});
+  s.AppendAudio({a, b}, {x.data(), x.data() + T * 2048}, {T, T});
+  AsrStreamPool::Request r;
+  r.language = {3000};
+  r.committed = {4000, 4001};
+  std::map<int, AsrStreamPool::Request> req;
+  req[a] = r;
+  req[b] = r;
+  auto out = s.Decode(req);
+  for (int sid : {a, b}) {
+    for (int t : out[sid]) std::printf("%d ", t);
+    std::printf("\n");
+  }
+  std::printf("%d %d %d %d\n", s.checkpoint(a), pool.cache_len(a), s.checkpoint(b), pool.cache_len(b));
+  return 0;
+}
+"""
+
+
+@pytest.mark.gpu
+def test_cpp_stream_pool_matches_python(tmp_path, cuda):
+    _need_build()
+    from oracle import synth
+    from orator_b200 import AsrTextConfig, AsrTextDecoder, BatchDecoder
+    from orator_b200 import stream as S
+    x = synth.audio_rows(9, 40, 2048).astype(np.float32)
+    rows = tmp_path / "rows.f32"
+    x.tofile(rows)
+    exe = _compile(tmp_path, STREAM_PROGRAM, "stream_api")
+    r = subprocess.run([str(exe), str(rows)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    lines = r.stdout.split("\n")
+    cpp = [[int(t) for t in lines[0].split()], [int(t) for t in lines[1].split()]]
+    ck = [int(v) for v in lines[2].split()]
+    assert ck[0] == ck[1] and ck[2] == ck[3]
+    d = AsrTextDecoder(AsrTextConfig(num_layers=2, max_seq_len=256))
+    d.init_synthetic(9)
+    bd = BatchDecoder(d, max_sessions=4, max_batch=4, pool_pages=64, max_pages_per_session=16)
+    pool = S.AsrStreamPool(d, bd, max_new=10, ban_steps=3)
+    a, b = pool.open([1000, 1001]), pool.open([1002])
+    pool.append_audio([a, b], [x[:20], x[20:]])
+    out = pool.decode({a: ([3000], [4000, 4001]), b: ([3000], [4000, 4001])})
+    assert [out[a], out[b]] == cpp
+    assert [pool.ckpt[a], pool.ckpt[b]] == [ck[0], ck[2]]
+    bd.close()
+    d.close()
