@@ -128,7 +128,10 @@ def build_prompt_gpu(dec, torch):
     audio = buf.cpu().numpy().reshape(AUDIO_ROWS, HIDDEN)
     toks = prompt_token_ids(PROMPT_ROWS - AUDIO_ROWS)
     emb = np.stack([dec.Embed(int(t)) for t in toks])
-    return np.ascontiguousarray(np.concatenate([audio, emb], 0), dtype=np.float32)
+    # the prompt rows live in pinned host memory (the e2e leg copies them in)
+    pinned = torch.empty((PROMPT_ROWS, HIDDEN), dtype=torch.float32, pin_memory=True)
+    pinned.copy_(torch.from_numpy(np.concatenate([audio, emb], 0).astype(np.float32)))
+    return pinned.numpy()
 
 
 def cpu_oracle_rate(sample_tokens: int, warm: int = 1, reps: int = 1):
