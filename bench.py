@@ -221,6 +221,13 @@ def run_ragged(dec, torch, world, dist, rank=0, strong=False, steps=256):
     joins_pinned.copy_(torch.from_numpy(np.concatenate(joins, 0)))
     joins_cat = joins_pinned.numpy()
 
+    # warm-up join (untimed): sizes the row buffers and split-K workspace for
+    # an 8 x 400-row prefill, as the W warm-up steps do for the decode step
+    warm = [bd.create_session() for _ in range(8)]
+    bd.prefill(warm, joins_cat, lens=[PROMPT_ROWS] * 8)
+    for w in warm:
+        bd.free_session(w)
+
     def my_sids():
         return [local[g] for g in gids if g in local]
 
