@@ -529,7 +529,7 @@ int orx_linear_pre(const uint16_t* in_bf16, const uint16_t* W_bf16, const float*
     need(out_f32, "out");
     if (bias || act != 0) throw std::invalid_argument("bias / activation epilogues are not supported");
     if (N % 128 != 0 || K % 64 != 0) throw std::invalid_argument("N must be a multiple of 128 and K of 64");
-    orx::TcArgs g = {N, K, M, orx::kEpiStore, out_f32, nullptr, N, nullptr, nullptr, nullptr};
+    orx::TcArgs g = {N, K, M, orx::kEpiStore, out_f32, nullptr, N, nullptr, nullptr};
     static int* d_err = nullptr;
     if (!d_err) {
       orx::check(cudaMalloc(&d_err, sizeof(int)), "cudaMalloc");

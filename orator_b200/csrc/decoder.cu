@@ -46,7 +46,7 @@ void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int
     return e ? atoi(e) : 0;
   }();
   if (forced > 0 && K % (64 * forced) == 0) splits = forced;
-  TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err, nullptr, nullptr, norm_w, norm_out, eps};
+  TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err, nullptr, norm_w, norm_out, eps};
   if (splits > 1) {
     const size_t need = (size_t)splits * T * N;
     if (need > w.cap) {

@@ -128,7 +128,6 @@ struct TcArgs {
   int ldo;
   int* err;
   float* ws;           // split-K partials [splits, T, N]
-  int* unused;
   // Optional RMSNorm of the (residual) output rows to bf16 (N == 2048):
   // fused into the split-K reduction, else a separate row kernel.
   const float* norm_w;
