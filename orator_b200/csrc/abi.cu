@@ -1,6 +1,7 @@
 // extern "C" entry points declared in include/orx.h.
 #include <cstring>
 #include <exception>
+#include <mutex>
 #include <new>
 #include <string>
 
@@ -530,12 +531,20 @@ int orx_linear_pre(const uint16_t* in_bf16, const uint16_t* W_bf16, const float*
     if (bias || act != 0) throw std::invalid_argument("bias / activation epilogues are not supported");
     if (N % 128 != 0 || K % 64 != 0) throw std::invalid_argument("N must be a multiple of 128 and K of 64");
     orx::TcArgs g = {N, K, M, orx::kEpiStore, out_f32, nullptr, N, nullptr, nullptr};
-    static int* d_err = nullptr;
-    if (!d_err) {
-      orx::check(cudaMalloc(&d_err, sizeof(int)), "cudaMalloc");
-      orx::check(cudaMemset(d_err, 0, sizeof(int)), "cudaMemset");
+    // one device error word per device, made on first use (thread-safe)
+    static std::mutex mu;
+    static int* err_of[64] = {};
+    int dev = 0;
+    orx::check(cudaGetDevice(&dev), "cudaGetDevice");
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      int*& e = err_of[dev & 63];
+      if (!e) {
+        orx::check(cudaMalloc(&e, sizeof(int)), "cudaMalloc");
+        orx::check(cudaMemset(e, 0, sizeof(int)), "cudaMemset");
+      }
+      g.err = e;
     }
-    g.err = d_err;
     orx::launch_gemm_tc(in_bf16, W_bf16, g, 1, S(stream));
     orx::check(cudaGetLastError(), "tcgen05 gemm");
   });

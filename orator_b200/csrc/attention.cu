@@ -426,11 +426,10 @@ __global__ void __launch_bounds__(256) qk_norm_rope_store_kernel(
 
 void launch_attention(const AttnArgs& a, const uint16_t* kv_pool, long long pool_rows,
                       cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
+  static std::atomic<unsigned long long> configured{0};
+  once_per_device(configured, [] {
     cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
-    configured = true;
-  }
+  });
   // one map per pool; encoding is a host-side operation of about a microsecond
   CUtensorMap map;
   if (!make_tmap_2d(&map, kv_pool, pool_rows, kHeadDim, 64, kPage)) return;

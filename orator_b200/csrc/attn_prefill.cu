@@ -191,11 +191,10 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 void launch_attn_prefill(const PrefillAttnArgs& a, int ntiles, const uint16_t* kv_pool,
                          long long pool_rows, cudaStream_t s) {
   if (ntiles <= 0) return;
-  static bool configured = false;
-  if (!configured) {
+  static std::atomic<unsigned long long> configured{0};
+  once_per_device(configured, [] {
     cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
-    configured = true;
-  }
+  });
   CUtensorMap map;
   if (!make_tmap_2d(&map, kv_pool, pool_rows, kHeadDim, 64, kPage)) return;
   launch_pdl(attn_prefill_kernel, dim3(ntiles, kKvHeads), dim3(kPfThreads), kPfSmem, s, map, a);

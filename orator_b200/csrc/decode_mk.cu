@@ -625,12 +625,11 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
 size_t decode_mk_smem() { return sizeof(MkSmem) + 128; }
 
 void launch_decode_mk_config() {
-  static bool done = false;
-  if (!done) {
+  static std::atomic<unsigned long long> done{0};
+  once_per_device(done, [] {
     cudaFuncSetAttribute(decode_mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(decode_mk_smem()));
-    done = true;
-  }
+  });
 }
 
 cudaError_t launch_decode_mk(const MkArgs& a, int grid, cudaStream_t s) {

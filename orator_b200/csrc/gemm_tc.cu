@@ -406,17 +406,17 @@ __global__ void splitk_swiglu_kernel(TcArgs g, int splits) {
 template <int BN, int STAGES>
 void launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& g, int splits,
                cudaStream_t s) {
-  static bool configured = false;
-  static int sms = 148;
+  static std::atomic<unsigned long long> configured{0};
+  static int sms_of[64];
   const size_t smem = sizeof(TcSmem<BN, STAGES>) + 1024;
-  if (!configured) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  once_per_device(configured, [&] {
     cudaFuncSetAttribute(tc_gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    configured = true;
-  }
+    cudaDeviceGetAttribute(&sms_of[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+  });
+  const int sms = sms_of[dev & 63] > 0 ? sms_of[dev & 63] : 148;
   const int items = (g.N / 128) * ((g.T + BN - 1) / BN) * splits;
   const int grid = items < sms ? items : sms;
   launch_pdl(tc_gemm_kernel<BN, STAGES>, dim3(grid), dim3(kTcThreadsP), smem, s, mw, mx, g,

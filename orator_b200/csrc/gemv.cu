@@ -250,13 +250,12 @@ __global__ void __launch_bounds__(kThreadsGemv, 2) gemv_kernel(GemvArgs a) {
 
 template <int D>
 void launch_depth(const GemvArgs& a, int grid, cudaStream_t s) {
-  static bool configured = false;
+  static std::atomic<unsigned long long> configured{0};
   const size_t smem = sizeof(GemvSmem<D>) + 128;
-  if (!configured) {
+  once_per_device(configured, [&] {
     cudaFuncSetAttribute(gemv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
-    configured = true;
-  }
+  });
   launch_pdl(gemv_kernel<D>, dim3(grid), dim3(kThreadsGemv), smem, s, a);
 }
 

@@ -4,6 +4,8 @@
 #include <cstdint>
 #include <utility>
 #include <cuda_runtime.h>
+#include <atomic>
+#include <mutex>
 
 namespace orx {
 
@@ -192,6 +194,21 @@ cudaError_t launch_decode_mk(const MkArgs& a, int grid, cudaStream_t s);
 int decode_mk_max_grid();
 size_t decode_mk_smem();
 void launch_decode_mk_config();
+
+// Runs `f` once per CUDA device (kernel attributes belong to a device's
+// context); thread-safe.
+template <typename F>
+inline void once_per_device(std::atomic<unsigned long long>& done, F&& f) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.load(std::memory_order_relaxed) & bit) return;
+  f();
+  done.fetch_or(bit, std::memory_order_release);
+}
 
 // Programmatic dependent launch is on unless ORX_NO_PDL=1 is set.
 bool pdl_enabled();

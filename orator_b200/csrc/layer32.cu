@@ -330,13 +330,12 @@ struct Layer32 {
 };
 
 Layer32* layer32_create(int max_seq_len, float eps, float theta) {
-  static bool configured = false;
-  if (!configured) {
+  static std::atomic<unsigned long long> configured{0};
+  once_per_device(configured, [] {
     cudaFuncSetAttribute(l32_gemv_kernel<kL32Resid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kInter * 4);
     cudaFuncSetAttribute(l32_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured = true;
-  }
+  });
   if (max_seq_len < 1 || (size_t)max_seq_len * 4 > 200 * 1024)
     throw std::invalid_argument("max_seq_len out of range for the fp32 layer");
   return new Layer32(max_seq_len, eps, theta);
