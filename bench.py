@@ -356,6 +356,37 @@ def run_config1(torch, hbm, cpu: bool):
     return out
 
 
+def measure_prefill(dec, torch, prompt, s, reps=5):
+    """Config 2's 400-row prefill from device-resident rows (tcgen05 GEMMs,
+    flash prefill attention, last-row lm_head), device time per prefill, and
+    its arithmetic rate against the measured bf16 GEMM peak."""
+    d_prompt = torch.from_numpy(prompt).cuda()
+    for _ in range(2):
+        dec.ResetCache()
+        dec.PrefillAtDevice(d_prompt.data_ptr(), PROMPT_ROWS, 0, s)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        dec.ResetCache()
+        dec.PrefillAtDevice(d_prompt.data_ptr(), PROMPT_ROWS, 0, s)
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    layer_params = (4096 + 2048 + 12288) * 2048 + 2048 * 6144  # qkv, o, gate/up, down
+    flops = (2 * PROMPT_ROWS * LAYERS * layer_params          # projections
+             + 4 * LAYERS * 16 * 128 * PROMPT_ROWS * (PROMPT_ROWS + 1) // 2  # causal attention
+             + 2 * VOCAB * HIDDEN)                              # last-row lm_head
+    try:
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        peak = 1590.0
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"workload": "config2 prefill: 400 rows (375 audio + 25 token embeddings), 28 layers",
+            "ms": ms, "tflops": tf, "flops": flops, "bf16_peak_tflops": peak, "frac": tf / peak,
+            "note": "device-resident rows, CUDA events, mean of 5"}
+
+
 def run_ours(args):
     import torch
     rank, local, world = dist_env()
@@ -416,6 +447,7 @@ def run_ours(args):
     e2e_ms = f0.elapsed_time(f1)
 
     prof = dec.profile_kernels(iters=20)
+    prefill = measure_prefill(dec, torch, prompt, s)
     ragged = None if args.no_ragged else run_ragged(dec, torch, world, dist, rank, steps=args.ragged_steps)
     ragged_strong = (run_ragged(dec, torch, world, dist, rank, strong=True, steps=args.ragged_steps)
                      if world > 1 and not args.no_ragged else None)
@@ -463,6 +495,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": NEW_TOKENS * 4,
                 "note": "per step: Prefill(host 400x2048 fp32) + DecodeGreedy(128, batch 32) through the C ABI"},
         "gpu_launches": args.steps * 2,  # seed argmax + one persistent decode launch per step
+        "prefill": prefill,
         "clocks": clocks,
     }
     if ragged is not None:
