@@ -533,8 +533,15 @@ def main():
     NEW_TOKENS = args.tokens
     if args.impl == "reference":
         run_reference(args)
-    else:
+        return
+    try:
         run_ours(args)
+    except BaseException:
+        import traceback
+        rank = dist_env()[0]
+        sys.stderr.write(f"[rank {rank}] bench failed:\n{traceback.format_exc()}")
+        sys.stderr.flush()
+        raise
 
 
 if __name__ == "__main__":

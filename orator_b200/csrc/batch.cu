@@ -134,19 +134,30 @@ BatchDecoder::BatchDecoder(Model* m, int max_sessions, int max_batch, int pool_p
     ORX_CHECK(cudaEventCreateWithFlags(&ev_table_[b], cudaEventDisableTiming));
   }
   ORX_CHECK(cudaMallocHost(&h_out_, sizeof(int) * max_batch));
-  ensure_rows(max_batch);
+  // Step buffers and the step workspace, sized once for every batch size up
+  // to max_batch: the four layer projections and the lm_head.
+  alloc_rows(stepb_, max_batch);
+  ensure_logits(stepb_, max_batch);
+  size_t need = 0;
+  const int sms = m->num_sms;
+  for (int n = 1; n <= max_batch; ++n)
+    for (size_t f : {proj_ws_floats(kQkvDim, kHidden, n, sms), proj_ws_floats(kHidden, kQDim, n, sms),
+                     proj_ws_floats(2 * kInter, kHidden, n, sms), proj_ws_floats(kHidden, kInter, n, sms),
+                     proj_ws_floats(m->cfg.vocab_size, kHidden, n, sms)})
+      need = std::max(need, f);
+  step_ws_.reserve(need, nullptr);
 }
 
 BatchDecoder::~BatchDecoder() {
   delete kv_;
+  graphs_.clear();
+  stepb_.release();
+  preb_.release();
   for (void* p : {(void*)d_table_, (void*)d_next_tok_, (void*)d_ban_, (void*)d_amax_keys_,
-                  (void*)d_amax_cnt_, (void*)st_, (void*)x_, (void*)xn_, (void*)qkv_,
-                  (void*)attn_, (void*)act_, (void*)logits_, (void*)part_, (void*)counters_,
-                  (void*)d_rows_, (void*)d_tokens_, (void*)d_out_, (void*)d_tiles_})
+                  (void*)d_amax_cnt_, (void*)st_, (void*)d_tiles_})
     if (p) cudaFree(p);
   if (h_rows_) cudaFreeHost(h_rows_);
   if (h_tiles_) cudaFreeHost(h_tiles_);
-  for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
   for (int b = 0; b < 2; ++b) {
     if (h_step_[b]) cudaFreeHost(h_step_[b]);
     if (h_tbl_[b]) cudaFreeHost(h_tbl_[b]);
@@ -156,36 +167,50 @@ BatchDecoder::~BatchDecoder() {
   if (h_out_) cudaFreeHost(h_out_);
 }
 
-void BatchDecoder::ensure_rows(int rows) {
-  if (rows <= rows_cap_) return;
-  cudaDeviceSynchronize();
-  const int cap = std::max(rows, 64);
-  for (void* p : {(void*)x_, (void*)xn_, (void*)qkv_, (void*)attn_, (void*)act_, (void*)part_,
-                  (void*)counters_, (void*)d_rows_, (void*)d_tokens_, (void*)d_out_})
+void BatchDecoder::RowBufs::release() {
+  for (void* p : {(void*)x, (void*)xn, (void*)qkv, (void*)attn, (void*)act, (void*)part,
+                  (void*)counters, (void*)rows, (void*)tokens, (void*)out, (void*)logits})
     if (p) cudaFree(p);
-  x_ = dalloc<float>((size_t)cap * kHidden);
-  xn_ = dalloc<uint16_t>((size_t)cap * kHidden);
-  qkv_ = dalloc<float>((size_t)cap * kQkvDim);
-  attn_ = dalloc<uint16_t>((size_t)cap * kQDim);
-  act_ = dalloc<uint16_t>((size_t)cap * kInter);
-  const int nsplit_cap = (mps_ + kSplitPages - 1) / kSplitPages;
-  part_ = dalloc<float>((size_t)cap * kKvHeads * nsplit_cap * kPartFloats);
-  counters_ = dalloc<int>((size_t)cap * kKvHeads);
-  ORX_CHECK(cudaMemset(counters_, 0, sizeof(int) * (size_t)cap * kKvHeads));
-  d_rows_ = dalloc<int>((size_t)cap * 2);
-  d_tokens_ = dalloc<int>(cap);
-  d_out_ = dalloc<int>(cap);
-  rows_cap_ = cap;
-  ++buf_gen_;
+  *this = RowBufs{};
 }
 
-void BatchDecoder::ensure_logits(int rows) {
-  if (rows <= logits_cap_) return;
-  cudaDeviceSynchronize();
-  if (logits_) cudaFree(logits_);
-  logits_ = dalloc<float>((size_t)rows * model->cfg.vocab_size);
-  logits_cap_ = rows;
-  ++buf_gen_;
+// (Re)allocates `b` for at least `rows` rows; the caller has made sure that no
+// queued work still uses the old buffers.
+void BatchDecoder::alloc_rows(RowBufs& b, int rows) {
+  if (rows <= b.cap) return;
+  if (b.cap > 0) ORX_CHECK(cudaDeviceSynchronize());
+  const int cap = std::max(rows, 64);
+  float* lg = b.logits;
+  const int lcap = b.logits_cap;
+  b.logits = nullptr;
+  b.release();
+  b.logits = lg;
+  b.logits_cap = lcap;
+  b.x = dalloc<float>((size_t)cap * kHidden);
+  b.xn = dalloc<uint16_t>((size_t)cap * kHidden);
+  b.qkv = dalloc<float>((size_t)cap * kQkvDim);
+  b.attn = dalloc<uint16_t>((size_t)cap * kQDim);
+  b.act = dalloc<uint16_t>((size_t)cap * kInter);
+  const int nsplit_cap = (mps_ + kSplitPages - 1) / kSplitPages;
+  b.part = dalloc<float>((size_t)cap * kKvHeads * nsplit_cap * kPartFloats);
+  b.counters = dalloc<int>((size_t)cap * kKvHeads);
+  ORX_CHECK(cudaMemset(b.counters, 0, sizeof(int) * (size_t)cap * kKvHeads));
+  b.rows = dalloc<int>((size_t)cap * 4);
+  b.tokens = dalloc<int>(cap);
+  b.out = dalloc<int>(cap);
+  b.cap = cap;
+  if (&b == &stepb_) ++step_realloc_;
+}
+
+void BatchDecoder::ensure_logits(RowBufs& b, int rows) {
+  if (rows <= b.logits_cap) return;
+  if (b.logits) {
+    ORX_CHECK(cudaDeviceSynchronize());
+    cudaFree(b.logits);
+  }
+  b.logits = dalloc<float>((size_t)rows * model->cfg.vocab_size);
+  b.logits_cap = rows;
+  if (&b == &stepb_) ++step_realloc_;
 }
 
 int BatchDecoder::create_session() {
@@ -286,13 +311,14 @@ void BatchDecoder::upload_table(cudaStream_t st) {
   dirty_ = false;
 }
 
-// Shared per-layer body over `rows` rows of x_ whose (session, position) are in
-// d_rows_ = [row_table | row_pos]. fused: decode mode (q/k norm, RoPE and the
+// Shared per-layer body over `rows` rows of b.x whose (session, position) are in
+// b.rows = [row_table | row_pos]. fused: decode mode (q/k norm, RoPE and the
 // K/V store inside attention); otherwise the prefill store kernel runs first.
-void BatchDecoder::layers(int rows, int max_len, bool fused, cudaStream_t s) {
+void BatchDecoder::layers(RowBufs& b, GemmWs& ws, int rows, int max_len, bool fused,
+                          cudaStream_t s) {
   const auto& c = model->cfg;
-  const int* row_table = d_rows_;
-  const int* row_pos = d_rows_ + rows_cap_;
+  const int* row_table = b.rows;
+  const int* row_pos = b.rows + b.cap;
   const int sms = model->num_sms;
   const int nsplit = ((max_len + kPage - 1) / kPage + kSplitPages - 1) / kSplitPages;
   int* err = &st_->err;
@@ -300,14 +326,14 @@ void BatchDecoder::layers(int rows, int max_len, bool fused, cudaStream_t s) {
     const Model::Layer& L = model->layers[l];
     uint16_t* kvl = kv_->layer(l);
     // later layers' input norm comes fused with the previous down projection
-    if (l == 0) launch_rmsnorm_bf16(x_, L.in_ln, xn_, rows, c.rms_norm_eps, s);
-    run_proj(gws_, xn_, L.qkv, kQkvDim, kHidden, rows, kEpiStore, qkv_, nullptr, kQkvDim, err, sms, s);
+    if (l == 0) launch_rmsnorm_bf16(b.x, L.in_ln, b.xn, rows, c.rms_norm_eps, s);
+    run_proj(ws, b.xn, L.qkv, kQkvDim, kHidden, rows, kEpiStore, b.qkv, nullptr, kQkvDim, err, sms, s);
     if (!fused)
-      launch_qk_norm_rope_store(qkv_, rows, L.q_norm, L.k_norm, model->rope_cos, model->rope_sin,
+      launch_qk_norm_rope_store(b.qkv, rows, L.q_norm, L.k_norm, model->rope_cos, model->rope_sin,
                                 kvl, d_table_, mps_, row_table, row_pos, 0, s);
     if (fused) {
       AttnArgs a = {};
-      a.qkv = qkv_;
+      a.qkv = b.qkv;
       a.qkv_stride = kQkvDim;
       a.q_norm_w = L.q_norm;
       a.k_norm_w = L.k_norm;
@@ -322,33 +348,33 @@ void BatchDecoder::layers(int rows, int max_len, bool fused, cudaStream_t s) {
       a.fused_kv = fused ? 1 : 0;
       a.nsplit_max = nsplit;
       a.pages_per_split = kSplitPages;
-      a.part = part_;
-      a.counters = counters_;
-      a.out = attn_;
+      a.part = b.part;
+      a.counters = b.counters;
+      a.out = b.attn;
       a.err = err;
       a.kv_row0 = l * kv_->pages * 2 * kKvHeads * kPage;
       launch_attention(a, kv_->base, (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
     } else {
       PrefillAttnArgs pa = {};
-      pa.qkv = qkv_;
+      pa.qkv = b.qkv;
       pa.qkv_stride = kQkvDim;
       pa.tiles = d_tiles_;
       pa.page_table = d_table_;
       pa.max_pages = mps_;
       pa.kv_row0 = l * kv_->pages * 2 * kKvHeads * kPage;
-      pa.out = attn_;
+      pa.out = b.attn;
       pa.err = err;
       launch_attn_prefill(pa, ntiles_, kv_->base,
                           (long long)kv_->num_layers * kv_->pages * 2 * kKvHeads * kPage, s);
     }
-    run_proj(gws_, attn_, L.o, kHidden, kQDim, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s,
-             L.post_ln, xn_, c.rms_norm_eps);
-    run_proj(gws_, xn_, L.gateup, 2 * kInter, kHidden, rows, kEpiSwiglu, nullptr, act_, kInter, err, sms, s);
+    run_proj(ws, b.attn, L.o, kHidden, kQDim, rows, kEpiResid, b.x, nullptr, kHidden, err, sms, s,
+             L.post_ln, b.xn, c.rms_norm_eps);
+    run_proj(ws, b.xn, L.gateup, 2 * kInter, kHidden, rows, kEpiSwiglu, nullptr, b.act, kInter, err, sms, s);
     // the next layer's input norm, or in a decode step the final norm
     const float* next_norm = l + 1 < c.num_layers ? model->layers[l + 1].in_ln
                                                    : (fused ? model->final_norm : nullptr);
-    run_proj(gws_, act_, L.down, kHidden, kInter, rows, kEpiResid, x_, nullptr, kHidden, err, sms, s,
-             next_norm, xn_, c.rms_norm_eps);
+    run_proj(ws, b.act, L.down, kHidden, kInter, rows, kEpiResid, b.x, nullptr, kHidden, err, sms, s,
+             next_norm, b.xn, c.rms_norm_eps);
   }
 }
 
@@ -366,16 +392,18 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
   if (total > 65536 / 2) throw std::invalid_argument("too many prefill rows in one call");
   if (!fits(sids, lens, n)) throw std::invalid_argument("KV page pool exhausted");
   for (int i = 0; i < n; ++i) reserve(sids[i], sessions_[sids[i]].len + lens[i]);
-  ensure_rows(std::max(total, n));
-  ensure_logits(n);
-  // rows: [row_table (rows_cap_) | row_pos (rows_cap_)], then the last-row list
+  RowBufs& b = preb_;
+  alloc_rows(b, std::max(total, n));
+  ensure_logits(b, n);
+  const int cap = b.cap;
+  // rows: [row_table (cap) | row_pos (cap)], then the last-row list
   int r = 0;
   std::vector<int> last(n);
   for (int i = 0; i < n; ++i) {
     const Session& ss = sessions_[sids[i]];
     for (int t = 0; t < lens[i]; ++t, ++r) {
       h_rows_[r] = sids[i];
-      h_rows_[rows_cap_ + r] = ss.len + t;
+      h_rows_[cap + r] = ss.len + t;
     }
     last[i] = r - 1;
     max_len = std::max(max_len, ss.len + lens[i]);
@@ -404,25 +432,25 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
                               cudaMemcpyHostToDevice, s));
   }
   upload_table(s);
-  ORX_CHECK(cudaMemcpyAsync(d_rows_, h_rows_, sizeof(int) * 2 * rows_cap_, cudaMemcpyHostToDevice, s));
-  ORX_CHECK(cudaMemcpyAsync(x_, host_embeds, sizeof(float) * (size_t)total * kHidden,
+  ORX_CHECK(cudaMemcpyAsync(b.rows, h_rows_, sizeof(int) * 2 * cap, cudaMemcpyHostToDevice, s));
+  ORX_CHECK(cudaMemcpyAsync(b.x, host_embeds, sizeof(float) * (size_t)total * kHidden,
                             cudaMemcpyHostToDevice, s));
-  layers(total, max_len, false, s);
+  layers(b, pre_ws_, total, max_len, false, s);
   // final norm + lm_head on each session's last row -> first decoded token
-  std::memcpy(h_rows_ + 2 * rows_cap_, last.data(), sizeof(int) * n);
-  for (int i = 0; i < n; ++i) h_rows_[2 * rows_cap_ + n + i] = sids[i];
-  ORX_CHECK(cudaMemcpyAsync(d_tokens_, h_rows_ + 2 * rows_cap_, sizeof(int) * n,
+  std::memcpy(h_rows_ + 2 * cap, last.data(), sizeof(int) * n);
+  for (int i = 0; i < n; ++i) h_rows_[2 * cap + n + i] = sids[i];
+  ORX_CHECK(cudaMemcpyAsync(b.tokens, h_rows_ + 2 * cap, sizeof(int) * n,
                             cudaMemcpyHostToDevice, s));
-  ORX_CHECK(cudaMemcpyAsync(d_out_, h_rows_ + 2 * rows_cap_ + n, sizeof(int) * n,
+  ORX_CHECK(cudaMemcpyAsync(b.out, h_rows_ + 2 * cap + n, sizeof(int) * n,
                             cudaMemcpyHostToDevice, s));
-  launch_pdl(gather_rows, dim3(n), dim3(256), 0, s, (const float*)x_, (const int*)d_tokens_,
-             (float*)qkv_);
+  launch_pdl(gather_rows, dim3(n), dim3(256), 0, s, (const float*)b.x, (const int*)b.tokens,
+             (float*)b.qkv);
   const auto& c = model->cfg;
-  launch_rmsnorm_bf16(qkv_, model->final_norm, xn_, n, c.rms_norm_eps, s);
-  run_proj(gws_, xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr, c.vocab_size,
-           &st_->err, model->num_sms, s);
-  launch_pdl(rows_argmax, dim3(kArgmaxChunks, n), dim3(512), 0, s, (const float*)logits_,
-             c.vocab_size, (const int*)d_out_, d_next_tok_, (int*)nullptr, d_ban_, d_amax_keys_,
+  launch_rmsnorm_bf16(b.qkv, model->final_norm, b.xn, n, c.rms_norm_eps, s);
+  run_proj(pre_ws_, b.xn, model->embed, c.vocab_size, kHidden, n, kEpiStore, b.logits, nullptr,
+           c.vocab_size, &st_->err, model->num_sms, s);
+  launch_pdl(rows_argmax, dim3(kArgmaxChunks, n), dim3(512), 0, s, (const float*)b.logits,
+             c.vocab_size, (const int*)b.out, d_next_tok_, (int*)nullptr, d_ban_, d_amax_keys_,
              d_amax_cnt_);
   ORX_CHECK(cudaGetLastError());
   ORX_CHECK(cudaStreamSynchronize(s));  // h_rows_ is reused by the next call
@@ -430,17 +458,18 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
 }
 
 // Kernels of one decode step for n rows whose (session, position) are in
-// d_rows_; every varying input lives in device memory, so the sequence is
+// stepb_.rows; every varying input lives in device memory, so the sequence is
 // captured once per batch size and replayed as a CUDA graph.
 void BatchDecoder::record_step(int n, cudaStream_t s) {
+  RowBufs& b = stepb_;
   launch_pdl(gather_tokens_embed, dim3(n), dim3(256), 0, s, (const int*)d_next_tok_,
-             (const int*)d_rows_, (const uint16_t*)model->embed, d_tokens_, x_);
-  layers(n, mps_ * kPage, true, s);  // ends with the final norm of every row in xn_
+             (const int*)b.rows, (const uint16_t*)model->embed, b.tokens, b.x);
+  layers(b, step_ws_, n, mps_ * kPage, true, s);  // ends with the final norm of every row in b.xn
   const auto& c = model->cfg;
-  run_proj(gws_, xn_, model->embed, c.vocab_size, kHidden, n, kEpiStore, logits_, nullptr,
+  run_proj(step_ws_, b.xn, model->embed, c.vocab_size, kHidden, n, kEpiStore, b.logits, nullptr,
            c.vocab_size, &st_->err, model->num_sms, s);
-  launch_pdl(rows_argmax, dim3(kArgmaxChunks, n), dim3(512), 0, s, (const float*)logits_,
-             c.vocab_size, (const int*)d_rows_, d_next_tok_, d_out_, d_ban_, d_amax_keys_,
+  launch_pdl(rows_argmax, dim3(kArgmaxChunks, n), dim3(512), 0, s, (const float*)b.logits,
+             c.vocab_size, (const int*)b.rows, d_next_tok_, b.out, d_ban_, d_amax_keys_,
              d_amax_cnt_);
 }
 
@@ -458,8 +487,8 @@ void BatchDecoder::step(const int* sids, int n, int* host_tokens_out, cudaStream
     if (!fits(sids, ones.data(), n)) throw std::invalid_argument("KV page pool exhausted");
   }
   for (int i = 0; i < n; ++i) reserve(sids[i], sessions_[sids[i]].len + 1);
-  ensure_logits(max_batch_);
   upload_table(s);
+  RowBufs& rb = stepb_;
   // double-buffered pinned staging: wait only for the copy issued two steps ago
   const int b = step_count_ & 1;
   ORX_CHECK(cudaEventSynchronize(ev_rows_[b]));
@@ -468,45 +497,42 @@ void BatchDecoder::step(const int* sids, int n, int* host_tokens_out, cudaStream
     stage[i] = sids[i];
     stage[max_batch_ + i] = sessions_[sids[i]].len;
   }
-  ORX_CHECK(cudaMemcpyAsync(d_rows_, stage, sizeof(int) * n, cudaMemcpyHostToDevice, s));
-  ORX_CHECK(cudaMemcpyAsync(d_rows_ + rows_cap_, stage + max_batch_, sizeof(int) * n,
+  ORX_CHECK(cudaMemcpyAsync(rb.rows, stage, sizeof(int) * n, cudaMemcpyHostToDevice, s));
+  ORX_CHECK(cudaMemcpyAsync(rb.rows + rb.cap, stage + max_batch_, sizeof(int) * n,
                             cudaMemcpyHostToDevice, s));
   ORX_CHECK(cudaEventRecord(ev_rows_[b], s));
   ++step_count_;
 
-  auto it = graphs_.find(n);
-  const bool stale = it != graphs_.end() && (graph_ws_ != gws_.ws || graph_gen_ != buf_gen_);
-  if (stale) {
-    for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
-    graphs_.clear();
-    it = graphs_.end();
-  }
-  if (it == graphs_.end() && warmed_.count(n) == 0) {
-    record_step(n, s);  // eager first run sizes every buffer
-    warmed_.insert(n);
+  // A graph is replayed only under the memory epoch it was captured in (the
+  // step buffers are sized for max_batch up front, so the epoch stays put;
+  // the check keeps any future reallocation from reaching a stale graph).
+  const uint64_t epoch = step_epoch();
+  cudaGraphExec_t g = graphs_.find(n, epoch);
+  if (!g && !graphs_.warmed(n)) {
+    record_step(n, s);  // eager first run
+    graphs_.mark_warmed(n);
   } else {
-    if (it == graphs_.end()) {
+    if (!g) {
       ORX_CHECK(cudaStreamSynchronize(s));
       cudaStream_t cs;
       ORX_CHECK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
       ORX_CHECK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
       record_step(n, cs);
-      cudaGraph_t g;
-      ORX_CHECK(cudaStreamEndCapture(cs, &g));
-      cudaGraphExec_t e;
-      ORX_CHECK(cudaGraphInstantiate(&e, g, 0));
-      ORX_CHECK(cudaGraphDestroy(g));
+      cudaGraph_t cg;
+      ORX_CHECK(cudaStreamEndCapture(cs, &cg));
+      ORX_CHECK(cudaGraphInstantiate(&g, cg, 0));
+      ORX_CHECK(cudaGraphDestroy(cg));
       ORX_CHECK(cudaStreamDestroy(cs));
-      it = graphs_.emplace(n, e).first;
-      graph_ws_ = gws_.ws;
-      graph_gen_ = buf_gen_;
+      if (step_epoch() != epoch)
+        throw CudaError("step buffers were reallocated while a step graph was captured");
+      graphs_.insert(n, epoch, g);
     }
-    ORX_CHECK(cudaGraphLaunch(it->second, s));
+    ORX_CHECK(cudaGraphLaunch(g, s));
   }
   ORX_CHECK(cudaGetLastError());
   for (int i = 0; i < n; ++i) sessions_[sids[i]].len += 1;
   if (host_tokens_out) {
-    ORX_CHECK(cudaMemcpyAsync(h_out_, d_out_, sizeof(int) * n, cudaMemcpyDeviceToHost, s));
+    ORX_CHECK(cudaMemcpyAsync(h_out_, rb.out, sizeof(int) * n, cudaMemcpyDeviceToHost, s));
     ORX_CHECK(cudaStreamSynchronize(s));
     std::memcpy(host_tokens_out, h_out_, sizeof(int) * n);
   }

@@ -14,13 +14,9 @@ namespace orx {
 // of CTAs covers the SMs (the short projections o / down / qkv at small T).
 GemmWs::~GemmWs() {
   if (ws) cudaFree(ws);
-  if (cnt) cudaFree(cnt);
 }
 
-void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi,
-              float* out_f32, uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s,
-              const float* norm_w, uint16_t* norm_out, float eps) {
-  if (T <= 0) return;
+int proj_splits(int N, int K, int T, int num_sms) {
   const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   const int tiles = (N / 128) * ((T + bn - 1) / bn);
   // Split-K by a small cost model of the persistent GEMM: rounds of items per
@@ -41,20 +37,31 @@ void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int
   int splits = 1;
   for (int sp = 2; sp <= 16; sp *= 2)
     if (K % (64 * sp) == 0 && K / sp >= 128 && cost(sp) < cost(splits)) splits = sp;
-  static const int forced = [] {
-    const char* e = getenv("ORX_TC_SPLITS");  // tuning knob: force one split count
-    return e ? atoi(e) : 0;
-  }();
-  if (forced > 0 && K % (64 * forced) == 0) splits = forced;
+  return splits;
+}
+
+size_t proj_ws_floats(int N, int K, int T, int num_sms) {
+  const int sp = proj_splits(N, K, T, num_sms);
+  return sp > 1 ? (size_t)sp * T * N : 0;
+}
+
+void GemmWs::reserve(size_t floats, cudaStream_t s) {
+  if (floats <= cap) return;
+  ORX_CHECK(cudaStreamSynchronize(s));
+  if (ws) cudaFree(ws);
+  ws = dalloc<float>(floats);
+  cap = floats;
+  ++gen;
+}
+
+void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi,
+              float* out_f32, uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s,
+              const float* norm_w, uint16_t* norm_out, float eps) {
+  if (T <= 0) return;
+  const int splits = proj_splits(N, K, T, num_sms);
   TcArgs g = {N, K, T, epi, out_f32, out_bf16, ldo, err, nullptr, norm_w, norm_out, eps};
   if (splits > 1) {
-    const size_t need = (size_t)splits * T * N;
-    if (need > w.cap) {
-      ORX_CHECK(cudaStreamSynchronize(s));
-      if (w.ws) cudaFree(w.ws);
-      w.ws = dalloc<float>(need);
-      w.cap = need;
-    }
+    w.reserve((size_t)splits * T * N, s);
     g.ws = w.ws;
   }
   launch_gemm_tc(X, W, g, splits, s);

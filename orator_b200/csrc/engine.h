@@ -11,6 +11,7 @@
 
 #include <cuda_runtime.h>
 
+#include "graph_cache.h"
 #include "kernels.h"
 
 namespace orx {
@@ -39,14 +40,23 @@ struct ModelConfig {
 // Device-resident weights of the 28-layer decoder (layout chosen for the
 // streaming GEMV and the GEMM epilogues; see set_tensor for the mapping from
 // the reference's thinker.model.* tensors).
-// Split-K workspace of one stream's projections (grown on demand).
+// Split-K workspace of one stream's projections. `reserve` grows it (after a
+// stream synchronize) and bumps `gen`, so owners of captured graphs can tell
+// that the old address is gone.
 struct GemmWs {
   float* ws = nullptr;
   size_t cap = 0;
-  int* cnt = nullptr;
-  int cnt_cap = 0;
+  uint64_t gen = 0;
+  void reserve(size_t floats, cudaStream_t s);
+  GemmWs() = default;
+  GemmWs(const GemmWs&) = delete;
+  GemmWs& operator=(const GemmWs&) = delete;
   ~GemmWs();
 };
+// Split count run_proj picks for an N x K projection over T token rows, and
+// the workspace floats it then needs (0 without a split).
+int proj_splits(int N, int K, int T, int num_sms);
+size_t proj_ws_floats(int N, int K, int T, int num_sms);
 // norm_w / norm_out: RMSNorm of the residual output rows to bf16 right after
 // the projection (fused into the split-K reduction when there is one).
 void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi,
@@ -203,14 +213,26 @@ class BatchDecoder {
     int len = 0;
     std::vector<int> pages;
   };
+  // Per-row activations of one pass over the layers. `rows` holds
+  // [row_table (cap) | row_pos (cap) | last rows / session ids (2 * cap)].
+  struct RowBufs {
+    int cap = 0;
+    float *x = nullptr, *qkv = nullptr, *part = nullptr, *logits = nullptr;
+    uint16_t *xn = nullptr, *attn = nullptr, *act = nullptr;
+    int *counters = nullptr, *rows = nullptr, *tokens = nullptr, *out = nullptr;
+    int logits_cap = 0;
+    void release();
+  };
   void check_sid(int sid) const;
   bool reserve(int sid, int new_len);
   bool fits(const int* sids, const int* lens, int n) const;
   void upload_table(cudaStream_t s);
-  void ensure_rows(int rows);
-  void ensure_logits(int rows);
-  void layers(int rows, int max_len, bool fused, cudaStream_t s);
+  void alloc_rows(RowBufs& b, int rows);
+  void ensure_logits(RowBufs& b, int rows);
+  void layers(RowBufs& b, GemmWs& ws, int rows, int max_len, bool fused, cudaStream_t s);
   void record_step(int n, cudaStream_t s);
+  // Device memory a captured step graph may reference changes only with this.
+  uint64_t step_epoch() const { return step_ws_.gen + step_realloc_; }
 
   int max_sessions_, max_batch_, mps_;
   KvPool* kv_ = nullptr;
@@ -225,11 +247,12 @@ class BatchDecoder {
   int* d_amax_cnt_ = nullptr;                  // split argmax: per-row CTA tickets
   StepState* st_ = nullptr;
   int* h_rows_ = nullptr;  // pinned staging
-  int rows_cap_ = 0, logits_cap_ = 0;
-  float *x_ = nullptr, *qkv_ = nullptr, *part_ = nullptr, *logits_ = nullptr;
-  uint16_t *xn_ = nullptr, *attn_ = nullptr, *act_ = nullptr;
-  int *counters_ = nullptr, *d_rows_ = nullptr, *d_tokens_ = nullptr, *d_out_ = nullptr;
-  GemmWs gws_;
+  // Decode steps use fixed buffers sized for max_batch at construction and a
+  // workspace reserved for every batch size up front, so captured step graphs
+  // never see a reallocation; prefill (any row count) has its own.
+  RowBufs stepb_, preb_;
+  GemmWs step_ws_, pre_ws_;
+  uint64_t step_realloc_ = 0;
   PrefillTile* d_tiles_ = nullptr;
   PrefillTile* h_tiles_ = nullptr;
   int tiles_cap_ = 0, ntiles_ = 0;
@@ -239,10 +262,7 @@ class BatchDecoder {
   cudaEvent_t ev_rows_[2] = {nullptr, nullptr};
   cudaEvent_t ev_table_[2] = {nullptr, nullptr};
   long long step_count_ = 0, table_count_ = 0;
-  std::map<int, cudaGraphExec_t> graphs_;
-  std::set<int> warmed_;
-  float* graph_ws_ = nullptr;
-  long long graph_gen_ = -1, buf_gen_ = 0;
+  GraphCache<cudaGraphExec_t, cudaError_t (*)(cudaGraphExec_t)> graphs_{cudaGraphExecDestroy};
 };
 
 // fp32 single decoder layer (layer32.cu): fp32 weights, activations and KV.

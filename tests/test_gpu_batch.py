@@ -99,3 +99,43 @@ def test_truncate_returns_pages(env):
     assert bd.free_pages() == free0 - 1 and bd.cache_len(sid) == 16
     bd.free_session(sid)
     assert bd.free_pages() == free0
+
+
+def test_batch_sizes_return_to_earlier_sizes(env):
+    """Regression for replaying a per-batch-size step graph after its buffers
+    changed: batch sizes go 3 -> 8 -> 3 -> 5 -> 8 -> 1 with a 100-row join in
+    between (which grows the prefill buffers and workspace), and every
+    session's tokens still match the oracle run of that session alone."""
+    from orator_b200 import BatchDecoder
+    cfg, w, dec, _ = env
+    bd = BatchDecoder(dec, max_sessions=9, max_batch=8, pool_pages=96, max_pages_per_session=12)
+    try:
+        lens = [3, 9, 20, 4, 7, 15, 2, 11, 100]
+        xs = [synth.audio_rows(SEED + 40 + i, L, 2048) for i, L in enumerate(lens)]
+        sids = [bd.create_session() for _ in lens]
+        out = {s: [] for s in sids}
+
+        def run(active, times):
+            for _ in range(times):
+                toks = bd.step(active)
+                for s, t in zip(active, toks):
+                    out[s].append(int(t))
+
+        bd.prefill(sids[:3], xs[:3])
+        run(sids[:3], 2)            # 3
+        bd.prefill(sids[3:8], xs[3:8])
+        run(sids[:8], 2)            # 8
+        run(sids[:3], 2)            # back to 3
+        bd.prefill([sids[8]], [xs[8]])  # a long join grows the prefill side
+        run(sids[3:8], 2)           # 5
+        run(sids[:8], 1)            # 8 again
+        run([sids[8]], 3)           # 1
+        run(sids[:3], 1)            # 3 again
+        assert bd.device_error() == 0
+        for i, s in enumerate(sids):
+            n = len(out[s])
+            ref, margins = oracle_greedy(cfg, w, xs[i], n + 1)
+            assert agree(out[s], ref[1:], margins[1:]), (i, out[s], ref[1:])
+            assert bd.cache_len(s) == lens[i] + n
+    finally:
+        bd.close()
