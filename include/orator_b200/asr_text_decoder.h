@@ -23,10 +23,13 @@
 namespace orator {
 namespace model {
 
+#ifndef ORATOR_B200_GPU_ERROR_DEFINED
+#define ORATOR_B200_GPU_ERROR_DEFINED
 class GpuError : public std::runtime_error {
  public:
   using std::runtime_error::runtime_error;
 };
+#endif
 
 // AsrTextConfig (asr_text_decoder.h:30-43).
 struct AsrTextConfig {

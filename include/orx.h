@@ -160,12 +160,46 @@ int orx_layer32_forward_device(orx_layer32* l, const float* d_x, int T, int pos0
 int orx_layer32_cache_len(const orx_layer32* l, int* out);
 int orx_layer32_truncate(orx_layer32* l, int len);
 
-/* asr_gemm::LinearPre (include/model/asr_gemm.h:36-38): out[M,N] = in[M,K] @ W[N,K]^T
- * with bf16 operands and fp32 accumulation, on the tcgen05 tensor cores.
- * Device pointers; asynchronous on `stream`. Supported here: bias == NULL,
- * act == 0, N % 128 == 0, K % 64 == 0 (every Qwen3-ASR decoder projection). */
+/* ---- The reference's free operators (device pointers, asynchronous on
+ * `stream`, row-major; empty sizes are no-ops as in the reference). ---- */
+
+/* asr_gemm::LinearPre (include/model/asr_gemm.h:36-38):
+ * out[M,N] = act(in[M,K] @ W[N,K]^T + bias[N]) with bf16 operands and fp32
+ * accumulation on the tcgen05 tensor cores. bias may be NULL; act 0 = none,
+ * 1 = GELU (exact, erf), 2 = ReLU. Any M, N; K a multiple of 8 with 16-byte
+ * aligned operands runs on the tensor cores, other K on a CUDA-core kernel. */
 int orx_linear_pre(const uint16_t* in_bf16, const uint16_t* W_bf16, const float* bias,
                    float* out_f32, int M, int K, int N, int act, void* stream);
+/* asr_gemm::Linear (asr_gemm.h:30-32): LinearPre after the fp32 -> bf16
+ * (round-to-nearest-even) cast of `in` into a per-thread buffer that grows on
+ * demand (as the reference's). */
+int orx_linear(const float* in_f32, const uint16_t* W_bf16, const float* bias, float* out_f32,
+               int M, int K, int N, int act, void* stream);
+/* asr_gemm::F32ToBf16 / Bf16ToF32 (asr_gemm.h:24-26). */
+int orx_f32_to_bf16(const float* in, uint16_t* out, long long n, void* stream);
+int orx_bf16_to_f32(const uint16_t* in, float* out, long long n, void* stream);
+/* asr_ops::RmsNorm (include/model/asr_ops.cuh:22-25): out = x * rsqrt(mean(x^2)
+ * + eps) * weight per row; in place allowed. */
+int orx_rms_norm(const float* x, const float* weight, float* out, int rows, int dim, float eps,
+                 void* stream);
+/* asr_ops::RopeHalf (asr_ops.cuh:41-48) and asr_ops::RopeInterleaved
+ * (asr_ops.cuh:27-34): rotary embedding in place over x [n_tokens, n_heads,
+ * head_dim] at positions [n_tokens] (device ints); head_dim even. */
+int orx_rope_half(float* x, const int* positions, int n_tokens, int n_heads, int head_dim,
+                  float theta_base, void* stream);
+int orx_rope_interleaved(float* x, const int* positions, int n_tokens, int n_heads, int head_dim,
+                         float theta_base, void* stream);
+/* asr_ops::SwiGLU (asr_ops.cuh:36-39): out = gate / (1 + exp(-gate)) * up. */
+int orx_swiglu(const float* gate, const float* up, float* out, long long n, void* stream);
+/* asr_ops::GqaAttention (asr_ops.cuh:50-56): q [T,Hq,D], k/v [T,Hkv,D] ->
+ * out [T,Hq,D], fp32, online softmax; Hq a multiple of Hkv, D <= 1024. */
+int orx_gqa_attention(const float* q, const float* k, const float* v, float* out, int T, int Hq,
+                      int Hkv, int head_dim, float scale, int causal, void* stream);
+/* asr_ops::ArgmaxBanned (asr_ops.cuh:58-62): index of the largest of n fp32
+ * logits, skipping ban0 / ban1 (-1 = none), into the device int d_out; exact
+ * ties, NaN and values <= -1e30 are handled as the reference kernel does.
+ * Uses no scratch memory (one CTA). */
+int orx_argmax_banned(const float* logits, int n, int ban0, int ban1, int* d_out, void* stream);
 
 /* Diagnostic (no reference counterpart): average device ms per launch of each
  * decode kernel class, ms[6] = {qkv GEMV, attention, o GEMV, gate/up GEMV,
@@ -188,13 +222,14 @@ int orx_decoder_trace_decode(orx_decoder* d, int steps, void* stream, unsigned l
 int orx_decoder_trace_ctas(orx_decoder* d, int steps, void* stream, unsigned long long* out,
                            size_t out_len, int* grid);
 
-/* Allocation-free banned argmax (no counterpart in the reference; same result
- * as orx_decoder_argmax_to_device / asr_ops::ArgmaxBanned on the same logits).
+/* Allocation-free banned argmax (no counterpart in the reference; the same
+ * index as orx_decoder_argmax_to_device and asr_ops::ArgmaxBanned on the same
+ * logits, exact ties included).
  * For callers that cannot allocate device memory: code inside a stream capture
  * it does not own, real-time threads that must not take the driver's
  * allocation locks, or processes whose device memory is reserved by another
  * allocator. Writes the index of the largest of `n` fp32 device logits,
- * skipping ban0/ban1 (-1 = none; exact ties -> lowest index), to the device
+ * skipping ban0/ban1 (-1 = none; ties resolved as asr_ops::ArgmaxBanned does), to the device
  * int `d_out`, asynchronously on `stream`. Its only scratch is a fixed 8,200-byte
  * array compiled into the library (held by every GPU that loads it until exit),
  * so n is limited to 8,388,608; larger n is rejected with ORX_EINVAL. The first

@@ -2,10 +2,14 @@
 # Compile the reference decoder from its own sources (read in place, never
 # copied) plus oracle/ref_harness.cc into oracle/_ref/libref_asr.so.
 # TEST INFRASTRUCTURE: the resulting library is a parity checker only.
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]
+# Usage: oracle/build_ref.sh REFERENCE_ROOT   (or ORATOR_REFERENCE=... oracle/build_ref.sh)
 set -euo pipefail
 HERE="$(cd "$(dirname "$0")" && pwd)"
-R="${1:-${ORATOR_REFERENCE:-/root/reference}}"
+R="${1:-${ORATOR_REFERENCE:-}}"
+if [ -z "$R" ]; then
+  echo "usage: $0 REFERENCE_ROOT (or set ORATOR_REFERENCE)" >&2
+  exit 2
+fi
 OUT="$HERE/_ref"
 if [ ! -f "$R/src/model/asr_text_decoder.cu" ]; then
   echo "reference sources not found under $R; skipping" >&2

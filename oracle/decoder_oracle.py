@@ -84,8 +84,9 @@ def rope_half(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Te
 
 def argmax_banned(logits: np.ndarray, ban0: int = -1, ban1: int = -1) -> int:
     """Reference tie rule (asr_ops.cu:300-325): thread t of 256 keeps the first
-    strict max of i = t (mod 256); the tree keeps the lower slot on ties, so
-    equal maxima resolve to the lowest thread index."""
+    strict max of i = t (mod 256) above -1e30; the shared-memory tree pairs
+    slot t with t + s (s = 128 .. 1) and takes t + s only when strictly
+    greater. Restated step by step, so no closed form is assumed here."""
     x = np.asarray(logits, dtype=np.float32).copy()
     n = x.shape[0]
     for b in (ban0, ban1):

@@ -15,6 +15,8 @@
 #include <cuda_runtime.h>
 
 #include "io/sharded_safetensor.h"
+#include "model/asr_gemm.h"
+#include "model/asr_ops.cuh"
 #include "model/asr_text_decoder.h"
 
 namespace {
@@ -106,6 +108,46 @@ int ref_decode_greedy(void* p, int start_pos, int max_new, int eos0, int eos1,
     g_err = e.what();
     return 1;
   }
+}
+
+// ---- the reference's free operators on device pointers (asr_ops.cuh:24-62,
+// asr_gemm.h:24-41), called unmodified; the caller owns every buffer. Each
+// returns 0 after a device synchronize, 1 on an exception or CUDA error.
+#define REF_OP(body)                                           \
+  try {                                                        \
+    body;                                                      \
+    return cudaDeviceSynchronize() == cudaSuccess ? 0 : 1;     \
+  } catch (const std::exception& e) {                          \
+    g_err = e.what();                                          \
+    return 1;                                                  \
+  }
+namespace ops = orator::model::asr_ops;
+namespace gm = orator::model::asr_gemm;
+int ref_op_rmsnorm(const float* x, const float* w, float* out, int rows, int dim, float eps) {
+  REF_OP(ops::RmsNorm(x, w, out, rows, dim, eps))
+}
+int ref_op_rope_half(float* x, const int* pos, int n, int heads, int dim, float theta) {
+  REF_OP(ops::RopeHalf(x, pos, n, heads, dim, theta))
+}
+int ref_op_swiglu(const float* g, const float* u, float* out, int n) {
+  REF_OP(ops::SwiGLU(g, u, out, n))
+}
+int ref_op_gqa(const float* q, const float* k, const float* v, float* out, int T, int hq,
+               int hkv, int dh, float scale, int causal) {
+  REF_OP(ops::GqaAttention(q, k, v, out, T, hq, hkv, dh, scale, causal != 0))
+}
+int ref_op_argmax_banned(const float* x, int n, int ban0, int ban1, int* out) {
+  REF_OP(ops::ArgmaxBanned(x, n, ban0, ban1, out))
+}
+int ref_op_f32_to_bf16(const float* in, uint16_t* out, long n) { REF_OP(gm::F32ToBf16(in, out, n)) }
+int ref_op_bf16_to_f32(const uint16_t* in, float* out, long n) { REF_OP(gm::Bf16ToF32(in, out, n)) }
+int ref_op_linear(const float* in, const uint16_t* w, const float* bias, float* out, int M, int K,
+                  int N, int act) {
+  REF_OP(gm::Linear(in, w, bias, out, M, K, N, act))
+}
+int ref_op_linear_pre(const uint16_t* in, const uint16_t* w, const float* bias, float* out, int M,
+                      int K, int N, int act) {
+  REF_OP(gm::LinearPre(in, w, bias, out, M, K, N, act))
 }
 
 void ref_truncate(void* p, int len) { static_cast<RefHandle*>(p)->dec->TruncateCache(len); }

@@ -521,6 +521,64 @@ int orx_layer32_truncate(orx_layer32* l, int len) {
   });
 }
 
+}  // extern "C"
+
+namespace {
+// One device error word per device for the GEMM's bounded waits (made on
+// first use, thread-safe).
+int* gemm_err_word() {
+  static std::mutex mu;
+  static int* err_of[64] = {};
+  int dev = 0;
+  orx::check(cudaGetDevice(&dev), "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(mu);
+  int*& e = err_of[dev & 63];
+  if (!e) {
+    orx::check(cudaMalloc(&e, sizeof(int)), "cudaMalloc");
+    orx::check(cudaMemset(e, 0, sizeof(int)), "cudaMemset");
+  }
+  return e;
+}
+
+void linear_pre(const uint16_t* in_bf16, const uint16_t* W_bf16, const float* bias,
+                float* out_f32, int M, int K, int N, int act, cudaStream_t s) {
+  if (act < 0 || act > 2) throw std::invalid_argument("act must be 0 (none), 1 (GELU) or 2 (ReLU)");
+  if (K % 8 != 0 || !orx::tc_available() ||
+      reinterpret_cast<uintptr_t>(in_bf16) % 16 != 0 || reinterpret_cast<uintptr_t>(W_bf16) % 16 != 0) {
+    // shapes a tensor map cannot describe (rows must be 16-byte multiples)
+    orx::op_linear_simt(in_bf16, W_bf16, bias, out_f32, M, K, N, act, s);
+    orx::check(cudaGetLastError(), "linear");
+    return;
+  }
+  orx::TcArgs g = {};
+  g.N = N;
+  g.K = K;
+  g.T = M;
+  g.epi = orx::kEpiLinear;
+  g.out_f32 = out_f32;
+  g.ldo = N;
+  g.err = gemm_err_word();
+  g.bias = bias;
+  g.act = act;
+  orx::launch_gemm_tc(in_bf16, W_bf16, g, 1, s);
+  orx::check(cudaGetLastError(), "tcgen05 gemm");
+}
+
+// The bf16 copy of Linear's fp32 input, one buffer per calling thread (as
+// the reference keeps it, asr_gemm.cu:24-44), grown on demand.
+struct CastScratch {
+  uint16_t* p = nullptr;
+  long long cap = 0;
+  int dev = -1;
+  ~CastScratch() {
+    if (p) cudaFree(p);
+  }
+};
+thread_local CastScratch g_cast;
+}  // namespace
+
+extern "C" {
+
 int orx_linear_pre(const uint16_t* in_bf16, const uint16_t* W_bf16, const float* bias,
                    float* out_f32, int M, int K, int N, int act, void* stream) {
   return guard([&] {
@@ -528,25 +586,127 @@ int orx_linear_pre(const uint16_t* in_bf16, const uint16_t* W_bf16, const float*
     need(in_bf16, "in");
     need(W_bf16, "W");
     need(out_f32, "out");
-    if (bias || act != 0) throw std::invalid_argument("bias / activation epilogues are not supported");
-    if (N % 128 != 0 || K % 64 != 0) throw std::invalid_argument("N must be a multiple of 128 and K of 64");
-    orx::TcArgs g = {N, K, M, orx::kEpiStore, out_f32, nullptr, N, nullptr, nullptr};
-    // one device error word per device, made on first use (thread-safe)
-    static std::mutex mu;
-    static int* err_of[64] = {};
+    linear_pre(in_bf16, W_bf16, bias, out_f32, M, K, N, act, S(stream));
+  });
+}
+
+int orx_linear(const float* in_f32, const uint16_t* W_bf16, const float* bias, float* out_f32,
+               int M, int K, int N, int act, void* stream) {
+  return guard([&] {
+    if (M <= 0 || K <= 0 || N <= 0) return;
+    need(in_f32, "in");
+    need(W_bf16, "W");
+    need(out_f32, "out");
+    const long long n = static_cast<long long>(M) * K;
     int dev = 0;
     orx::check(cudaGetDevice(&dev), "cudaGetDevice");
-    {
-      std::lock_guard<std::mutex> lock(mu);
-      int*& e = err_of[dev & 63];
-      if (!e) {
-        orx::check(cudaMalloc(&e, sizeof(int)), "cudaMalloc");
-        orx::check(cudaMemset(e, 0, sizeof(int)), "cudaMemset");
+    if (n > g_cast.cap || dev != g_cast.dev) {
+      // the previous buffer may still feed queued work of this thread
+      if (g_cast.p) {
+        orx::check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        cudaFree(g_cast.p);
+        g_cast.p = nullptr;
       }
-      g.err = e;
+      orx::check(cudaMalloc(&g_cast.p, sizeof(uint16_t) * (n + 8)), "cudaMalloc");
+      g_cast.cap = n;
+      g_cast.dev = dev;
     }
-    orx::launch_gemm_tc(in_bf16, W_bf16, g, 1, S(stream));
-    orx::check(cudaGetLastError(), "tcgen05 gemm");
+    orx::launch_f32_to_bf16(in_f32, g_cast.p, n, S(stream));
+    orx::check(cudaGetLastError(), "f32 -> bf16");
+    linear_pre(g_cast.p, W_bf16, bias, out_f32, M, K, N, act, S(stream));
+  });
+}
+
+int orx_f32_to_bf16(const float* in, uint16_t* out, long long n, void* stream) {
+  return guard([&] {
+    if (n <= 0) return;
+    need(in, "in");
+    need(out, "out");
+    orx::launch_f32_to_bf16(in, out, n, S(stream));
+    orx::check(cudaGetLastError(), "f32 -> bf16");
+  });
+}
+
+int orx_bf16_to_f32(const uint16_t* in, float* out, long long n, void* stream) {
+  return guard([&] {
+    if (n <= 0) return;
+    need(in, "in");
+    need(out, "out");
+    orx::launch_bf16_to_f32(in, out, n, S(stream));
+    orx::check(cudaGetLastError(), "bf16 -> f32");
+  });
+}
+
+int orx_rms_norm(const float* x, const float* weight, float* out, int rows, int dim, float eps,
+                 void* stream) {
+  return guard([&] {
+    if (rows <= 0 || dim <= 0) return;
+    need(x, "x");
+    need(weight, "weight");
+    need(out, "out");
+    orx::op_rms_norm(x, weight, out, rows, dim, eps, S(stream));
+    orx::check(cudaGetLastError(), "rms_norm");
+  });
+}
+
+static int rope(float* x, const int* positions, int n_tokens, int n_heads, int head_dim,
+                float theta, bool half, void* stream) {
+  return guard([&] {
+    if (n_tokens <= 0 || n_heads <= 0 || head_dim <= 0) return;
+    need(x, "x");
+    need(positions, "positions");
+    if (head_dim % 2) throw std::invalid_argument("head_dim must be even");
+    if (n_heads > 65535) throw std::invalid_argument("too many heads");
+    orx::op_rope(x, positions, n_tokens, n_heads, head_dim, theta, half, S(stream));
+    orx::check(cudaGetLastError(), "rope");
+  });
+}
+
+int orx_rope_half(float* x, const int* positions, int n_tokens, int n_heads, int head_dim,
+                  float theta_base, void* stream) {
+  return rope(x, positions, n_tokens, n_heads, head_dim, theta_base, true, stream);
+}
+
+int orx_rope_interleaved(float* x, const int* positions, int n_tokens, int n_heads, int head_dim,
+                         float theta_base, void* stream) {
+  return rope(x, positions, n_tokens, n_heads, head_dim, theta_base, false, stream);
+}
+
+int orx_swiglu(const float* gate, const float* up, float* out, long long n, void* stream) {
+  return guard([&] {
+    if (n <= 0) return;
+    need(gate, "gate");
+    need(up, "up");
+    need(out, "out");
+    orx::op_swiglu(gate, up, out, n, S(stream));
+    orx::check(cudaGetLastError(), "swiglu");
+  });
+}
+
+int orx_gqa_attention(const float* q, const float* k, const float* v, float* out, int T, int Hq,
+                      int Hkv, int head_dim, float scale, int causal, void* stream) {
+  return guard([&] {
+    if (T <= 0 || Hq <= 0 || Hkv <= 0 || head_dim <= 0) return;
+    need(q, "q");
+    need(k, "k");
+    need(v, "v");
+    need(out, "out");
+    if (Hq % Hkv) throw std::invalid_argument("Hq must be a multiple of Hkv");
+    if (head_dim > 1024) throw std::invalid_argument("head_dim must be <= 1024");
+    if (Hkv > 65535) throw std::invalid_argument("too many kv heads");
+    orx::check(orx::op_gqa_attention(q, k, v, out, T, Hq, Hkv, head_dim, scale, causal != 0,
+                                     S(stream)),
+               "gqa attention");
+  });
+}
+
+int orx_argmax_banned(const float* logits, int n, int ban0, int ban1, int* d_out, void* stream) {
+  return guard([&] {
+    if (n <= 0) return;  // as in the reference: nothing is written
+    need(logits, "logits");
+    need(d_out, "out");
+    orx::op_argmax_banned(logits, n, ban0, ban1, d_out, S(stream));
+    orx::check(cudaGetLastError(), "argmax");
   });
 }
 

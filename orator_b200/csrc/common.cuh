@@ -55,16 +55,40 @@ __device__ __forceinline__ float fma2_bf16(uint32_t a, uint32_t b, float acc) {
   return acc;
 }
 
-// Monotone key for (value, index) so a 64-bit atomicMax yields the largest
-// value and, among exact ties, the smallest index.
-__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
-  uint32_t u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return (static_cast<unsigned long long>(u) << 32) |
-         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
+// Banned argmax with the tie rule of the reference's single-block
+// ArgmaxBannedKernel (src/model/asr_ops.cu:300-325), packed into one monotone
+// 64-bit key so that any reduction order (warp shuffles, CTA partials,
+// atomicMax across CTAs) yields the same winner as that kernel:
+//  * thread t of its 256 scans i = t, t + 256, ... and keeps the first strict
+//    maximum above its -1e30 start, so values <= -1e30 (and NaN) never win and
+//    an all-excluded input returns index 0 (key 0 here);
+//  * its shared-memory tree pairs slot t with t + s for s = 128, 64, ..., 1 and
+//    takes the upper slot only when strictly greater, so among equal maxima
+//    the slot whose bit-reversed 8-bit number is smallest wins (bit 0 of the
+//    slot decides first, then bit 1, ...), and inside a slot the lowest i.
+// Key: orderable(value) << 32 | (255 - brev8(i & 255)) << 24 | (2^24 - 1 - (i >> 8)).
+// -0.0 is folded into +0.0 (the reference's `>` treats them as equal).
+__host__ __device__ __forceinline__ uint32_t brev8(uint32_t x) {
+  x = ((x & 0xF0u) >> 4) | ((x & 0x0Fu) << 4);
+  x = ((x & 0xCCu) >> 2) | ((x & 0x33u) << 2);
+  x = ((x & 0xAAu) >> 1) | ((x & 0x55u) << 1);
+  return x;
 }
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  if (!(v > -1e30f)) return 0ull;
+  uint32_t u = v == 0.0f ? 0u : __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  const uint32_t i = static_cast<uint32_t>(idx);
+  const uint32_t lo = ((255u - brev8(i & 255u)) << 24) | (0xFFFFFFu - (i >> 8));
+  return (static_cast<unsigned long long>(u) << 32) | lo;
+}
+// Index of a key; key 0 (nothing eligible) is index 0, as in the reference.
 __host__ __device__ __forceinline__ int argmax_key_index(unsigned long long k) {
-  return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+  if (k == 0ull) return 0;
+  const uint32_t lo = static_cast<uint32_t>(k & 0xFFFFFFFFull);
+  const uint32_t slot = brev8(255u - (lo >> 24));
+  const uint32_t hi = 0xFFFFFFu - (lo & 0xFFFFFFu);
+  return static_cast<int>(hi * 256u + slot);
 }
 
 // ---- programmatic dependent launch ---------------------------------------

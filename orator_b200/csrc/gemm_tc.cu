@@ -12,9 +12,11 @@
 //   * warp 1 / one lane: MMA issuer — 4 x tcgen05.mma (K = 16 each) per stage
 //     into a TMEM accumulator of BN fp32 columns, tcgen05.commit releases the
 //     stage;
-//   * all 4 warps: epilogue — tcgen05.ld of their 32 TMEM lanes (= 32 weight
-//     rows), then fp32 store, residual add (atomic when split over K) or
-//     SwiGLU on [64 gate | 64 up] tiles with the bf16 cast of the reference.
+//   * 4 epilogue warps: tcgen05.ld of their 32 TMEM lanes (= 32 weight
+//     rows), then fp32 store, residual add, SwiGLU on [64 gate | 64 up] tiles
+//     with the bf16 cast of the reference, or bias + GELU / ReLU (Linear);
+//     with split K they write fp32 partials that a reduction kernel sums in
+//     split order (deterministic).
 // Replaces Bf16WmmaKernel2 (include/model/gemm.cuh:394-459) and the
 // F32ToBf16 / AddResidual / SwiGLU launches around it.
 // No TMA multicast anywhere: every CTA loads its own tiles.
@@ -113,9 +115,9 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   TcSmem<BN, STAGES>& sm = *reinterpret_cast<TcSmem<BN, STAGES>*>(
       (reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mt = g.N / 128, nt = (g.T + BN - 1) / BN;
+  const int mt = (g.N + 127) / 128, nt = (g.T + BN - 1) / BN;
   const int items = mt * nt * splits;
-  const int kper = g.K / splits, KT = kper / kBK;
+  const int kper = g.K / splits, KT = (kper + kBK - 1) / kBK;
   constexpr int kTmemCols = 2 * (BN < 32 ? 32 : BN);  // two accumulators
   constexpr int kAccCols = kTmemCols / 2;
   int* err = g.err;
@@ -261,6 +263,20 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
                 g.out_bf16[(long long)t * g.ldo + (m0 >> 1) + rloc] =
                     f2bf((gt / (1.0f + expf(-gt))) * up);
               }
+            }
+          }
+        } else if (g.epi == kEpiLinear) {
+          if (row < g.N) {
+            const float bv = g.bias ? g.bias[row] : 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int t = n0 + c0 + i;
+              float y = v[i] + bv;
+              if (g.act == 1)
+                y = 0.5f * y * (1.0f + erff(y * 0.70710678118654752440f));
+              else if (g.act == 2)
+                y = fmaxf(y, 0.0f);
+              if (c0 + i < BN && t < g.T) g.out_f32[(long long)t * g.ldo + row] = y;
             }
           }
         } else {
@@ -417,7 +433,7 @@ void launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& g, in
     cudaDeviceGetAttribute(&sms_of[dev & 63], cudaDevAttrMultiProcessorCount, dev);
   });
   const int sms = sms_of[dev & 63] > 0 ? sms_of[dev & 63] : 148;
-  const int items = (g.N / 128) * ((g.T + BN - 1) / BN) * splits;
+  const int items = ((g.N + 127) / 128) * ((g.T + BN - 1) / BN) * splits;
   const int grid = items < sms ? items : sms;
   launch_pdl(tc_gemm_kernel<BN, STAGES>, dim3(grid), dim3(kTcThreadsP), smem, s, mw, mx, g,
              splits);

@@ -27,7 +27,8 @@ struct StepState {
 };
 
 enum ActMode : int { kActNorm = 0, kActEmbedNorm = 1, kActBf16 = 2 };
-enum EpiMode : int { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2, kEpiLogits = 3 };
+enum EpiMode : int { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2, kEpiLogits = 3,
+                     kEpiLinear = 4 };
 
 struct GemvArgs {
   const uint16_t* W;  // [rows, K] bf16 row-major
@@ -123,8 +124,11 @@ void launch_rmsnorm_bf16(const float* x, const float* w, uint16_t* out, int rows
 
 // tcgen05 GEMM (gemm_tc.cu): out[t, n] (op)= sum_k X[t, k] W[n, k].
 struct TcArgs {
-  int N, K, T;         // weight rows (multiple of 128), depth (multiple of 64 * splits), tokens
-  int epi;             // kEpiStore / kEpiResid / kEpiSwiglu
+  // weight rows, depth, tokens. N is a multiple of 128 and K of 64 * splits
+  // except under kEpiLinear (splits 1, any N, K a multiple of 8: the tensor
+  // maps zero-fill the ragged tiles and the epilogue masks rows >= N).
+  int N, K, T;
+  int epi;             // kEpiStore / kEpiResid / kEpiSwiglu / kEpiLinear
   float* out_f32;      // [T, ldo]
   uint16_t* out_bf16;  // SwiGLU output [T, ldo]
   int ldo;
@@ -135,6 +139,9 @@ struct TcArgs {
   const float* norm_w;
   uint16_t* norm_out;
   float eps;
+  // kEpiLinear: out = act(acc + bias[n]); act 0 none, 1 GELU (erf), 2 ReLU.
+  const float* bias;
+  int act;
 };
 // X: [T, K] bf16 row-major (device), W: [N, K] bf16. splits divides K / 64.
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
@@ -144,6 +151,19 @@ bool tc_available();
 // Argmax over fp32 logits with up to two banned ids into st (finalize sets st->tok).
 void launch_argmax(const float* logits, int n, int ban0, int ban1, StepState* st, int* out_dev,
                    cudaStream_t s);
+
+// Free operators of the reference API (ops.cu).
+void op_rms_norm(const float* x, const float* w, float* out, int rows, int dim, float eps,
+                 cudaStream_t s);
+void op_rope(float* x, const int* pos, int n_tokens, int n_heads, int head_dim, float theta,
+             bool rotate_half, cudaStream_t s);
+void op_swiglu(const float* g, const float* u, float* o, long long n, cudaStream_t s);
+void op_argmax_banned(const float* x, int n, int ban0, int ban1, int* out, cudaStream_t s);
+cudaError_t op_gqa_attention(const float* q, const float* k, const float* v, float* out, int T,
+                             int Hq, int Hkv, int D, float scale, bool causal, cudaStream_t s);
+// Linear without tensor maps (K not a multiple of 8): one warp per output.
+void op_linear_simt(const uint16_t* X, const uint16_t* W, const float* bias, float* out, int M,
+                    int K, int N, int act, cudaStream_t s);
 
 void launch_rope_table(float* cos, float* sin, int max_pos, float theta, cudaStream_t s);
 void launch_synth_bf16(uint16_t* dst, long long n, int seed, int tid, double std, float mean,

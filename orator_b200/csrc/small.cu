@@ -41,7 +41,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bf16_kernel(const float* x, const
 }
 
 // Multi-CTA banned argmax (replaces the single-block ArgmaxBannedKernel,
-// asr_ops.cu:300-325). Exact ties resolve to the lowest index.
+// asr_ops.cu:300-325); exact ties resolve as that kernel does (argmax_key).
 __global__ void __launch_bounds__(256) argmax_kernel(const float* x, int n, int ban0, int ban1,
                                                      StepState* st, int* out_dev) {
   pdl_trigger();
