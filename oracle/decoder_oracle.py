@@ -88,6 +88,7 @@ def argmax_banned(logits: np.ndarray, ban0: int = -1, ban1: int = -1) -> int:
     slot t with t + s (s = 128 .. 1) and takes t + s only when strictly
     greater. Restated step by step, so no closed form is assumed here."""
     x = np.asarray(logits, dtype=np.float32).copy()
+    x[np.isnan(x)] = -np.inf  # `v > best` is false for NaN: it never wins, like -inf
     n = x.shape[0]
     for b in (ban0, ban1):
         if 0 <= b < n:

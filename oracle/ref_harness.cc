@@ -129,6 +129,9 @@ int ref_op_rmsnorm(const float* x, const float* w, float* out, int rows, int dim
 int ref_op_rope_half(float* x, const int* pos, int n, int heads, int dim, float theta) {
   REF_OP(ops::RopeHalf(x, pos, n, heads, dim, theta))
 }
+int ref_op_rope_interleaved(float* x, const int* pos, int n, int heads, int dim, float theta) {
+  REF_OP(ops::RopeInterleaved(x, pos, n, heads, dim, theta))
+}
 int ref_op_swiglu(const float* g, const float* u, float* out, int n) {
   REF_OP(ops::SwiGLU(g, u, out, n))
 }

@@ -47,3 +47,45 @@ class RefDecoder:
         if self.h:
             self.L.ref_destroy(self.h)
             self.h = None
+
+
+class RefOps:
+    """The reference's own free operators (asr_ops / asr_gemm), unmodified,
+    on device pointers (ints); each call synchronizes the device."""
+
+    def __init__(self):
+        self.L = C.CDLL(LIB)
+        self.L.ref_last_error.restype = C.c_char_p
+
+    def _ok(self, rc):
+        if rc != 0:
+            raise RuntimeError(self.L.ref_last_error().decode())
+
+    def rms_norm(self, x, w, out, rows, dim, eps):
+        self._ok(self.L.ref_op_rmsnorm(C.c_void_p(x), C.c_void_p(w), C.c_void_p(out), rows, dim,
+                                       C.c_float(eps)))
+
+    def rope_half(self, x, pos, n, heads, dim, theta):
+        self._ok(self.L.ref_op_rope_half(C.c_void_p(x), C.c_void_p(pos), n, heads, dim,
+                                         C.c_float(theta)))
+
+    def rope_interleaved(self, x, pos, n, heads, dim, theta):
+        self._ok(self.L.ref_op_rope_interleaved(C.c_void_p(x), C.c_void_p(pos), n, heads, dim,
+                                                C.c_float(theta)))
+
+    def swiglu(self, g, u, out, n):
+        self._ok(self.L.ref_op_swiglu(C.c_void_p(g), C.c_void_p(u), C.c_void_p(out), n))
+
+    def gqa(self, q, k, v, out, T, hq, hkv, dh, scale, causal):
+        self._ok(self.L.ref_op_gqa(C.c_void_p(q), C.c_void_p(k), C.c_void_p(v), C.c_void_p(out),
+                                   T, hq, hkv, dh, C.c_float(scale), int(causal)))
+
+    def argmax_banned(self, x, n, ban0, ban1, out):
+        self._ok(self.L.ref_op_argmax_banned(C.c_void_p(x), n, ban0, ban1, C.c_void_p(out)))
+
+    def f32_to_bf16(self, x, out, n):
+        self._ok(self.L.ref_op_f32_to_bf16(C.c_void_p(x), C.c_void_p(out), C.c_long(n)))
+
+    def linear(self, x, w, bias, out, M, K, N, act):
+        self._ok(self.L.ref_op_linear(C.c_void_p(x), C.c_void_p(w), C.c_void_p(bias or 0),
+                                      C.c_void_p(out), M, K, N, act))

@@ -195,3 +195,40 @@ def test_cpp_stream_pool_matches_python(tmp_path, cuda):
     assert [pool.ckpt[a], pool.ckpt[b]] == [ck[0], ck[2]]
     bd.close()
     d.close()
+
+
+OPS_PROGRAM = r"""
+#include <cstdio>
+#include <stdexcept>
+#include "orator_b200/asr_text_decoder.h"
+#include "orator_b200/asr_ops.h"
+namespace ops = orator::model::asr_ops;
+namespace gm = orator::model::asr_gemm;
+int main() {
+  int fails = 0;
+  // empty sizes are no-ops, as in the reference
+  ops::RmsNorm(nullptr, nullptr, nullptr, 0, 2048, 1e-6f);
+  gm::Linear(nullptr, nullptr, nullptr, nullptr, 0, 8, 8, 0);
+  // argument errors surface as std::runtime_error (not GpuError)
+  try {
+    ops::GqaAttention(reinterpret_cast<const float*>(16), reinterpret_cast<const float*>(16),
+                      reinterpret_cast<const float*>(16), reinterpret_cast<float*>(16),
+                      2, 3, 2, 8, 1.0f, true);
+    ++fails;
+  } catch (const orator::model::GpuError&) {
+    ++fails;
+  } catch (const std::runtime_error&) {
+  }
+  std::printf("%s\n", fails ? "FAIL" : "OK");
+  return fails;
+}
+"""
+
+
+def test_cpp_ops_header(tmp_path):
+    """The asr_ops / asr_gemm shim compiles beside the decoder header with
+    -Wall -Wextra -Werror, and argument errors throw std::runtime_error."""
+    _need_build()
+    exe = _compile(tmp_path, OPS_PROGRAM, "ops_api")
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip() == "OK", r.stdout + r.stderr

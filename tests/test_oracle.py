@@ -78,6 +78,40 @@ def test_argmax_tie_rule():
     assert D.argmax_banned(z) == 0
 
 
+def _key_rule(x, ban0=-1, ban1=-1):
+    """Closed form of the reference tie rule that the CUDA kernels pack into
+    one 64-bit key (orator_b200/csrc/common.cuh argmax_key): among values
+    > -1e30, the largest value, then the slot i % 256 with the smallest
+    8-bit bit reversal, then the smallest i; nothing eligible -> 0."""
+    best = None
+    for i, v in enumerate(np.asarray(x, np.float32)):
+        if i in (ban0, ban1) or not (v > np.float32(-1e30)):
+            continue
+        s = i & 255
+        rev = int(f"{s:08b}"[::-1], 2)
+        key = (float(v), -rev, -(i >> 8))
+        if best is None or key > best[0]:
+            best = (key, i)
+    return 0 if best is None else best[1]
+
+
+def test_argmax_key_closed_form_equals_tree():
+    rng = np.random.default_rng(11)
+    for trial in range(300):
+        n = int(rng.integers(1, 3000))
+        x = rng.integers(-3, 4, n).astype(np.float32)  # many exact ties
+        if trial % 5 == 0:
+            x[rng.integers(0, n, max(1, n // 7))] = np.nan
+        if trial % 7 == 0:
+            x[:] = -1e31
+            x[rng.integers(0, n)] = np.float32(-1e30)
+        if trial % 11 == 0:
+            x = np.where(x == 0, np.float32(-0.0), x).astype(np.float32)
+        b0 = int(rng.integers(-1, n)) if trial % 3 else -1
+        b1 = int(rng.integers(-1, n)) if trial % 4 else -1
+        assert _key_rule(x, b0, b1) == D.argmax_banned(x, b0, b1), trial
+
+
 class _FakeDecoder(D.OracleDecoder):
     """Scripted logits: exercises DecodeGreedy's control loop only."""
 
