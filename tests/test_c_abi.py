@@ -37,12 +37,17 @@ int main(void) {
   CHECK(orx_layer32_create(&c, &l) == ORX_EINVAL && l == NULL);
   CHECK(orx_decoder_create(NULL, &d) == ORX_EINVAL);
   CHECK(orx_batch_create(NULL, 1, 1, 1, 1, &b) == ORX_EINVAL && b == NULL);
-  /* LinearPre: empty input is a no-op, unsupported shapes are rejected */
+  /* free operators: empty input is a no-op; bad arguments are rejected
+     before any device work */
   CHECK(orx_linear_pre(NULL, NULL, NULL, NULL, 0, 64, 128, 0, NULL) == ORX_OK);
-  CHECK(orx_linear_pre((const uint16_t*)16, (const uint16_t*)16, NULL, (float*)16, 4, 100, 128,
-                       0, NULL) == ORX_EINVAL);
-  CHECK(orx_linear_pre((const uint16_t*)16, (const uint16_t*)16, (const float*)16, (float*)16, 4,
-                       64, 128, 0, NULL) == ORX_EINVAL);
+  CHECK(orx_linear_pre((const uint16_t*)16, (const uint16_t*)16, NULL, (float*)16, 4, 64, 128,
+                       3, NULL) == ORX_EINVAL);
+  CHECK(orx_linear(NULL, (const uint16_t*)16, NULL, (float*)16, 4, 64, 128, 0, NULL) == ORX_EINVAL);
+  CHECK(orx_rms_norm(NULL, NULL, NULL, 0, 2048, 1e-6f, NULL) == ORX_OK);
+  CHECK(orx_gqa_attention((const float*)16, (const float*)16, (const float*)16, (float*)16, 2, 3,
+                          2, 8, 1.0f, 1, NULL) == ORX_EINVAL);
+  CHECK(orx_rope_half((float*)16, (const int*)16, 1, 1, 7, 1e6f, NULL) == ORX_EINVAL);
+  CHECK(orx_argmax_banned(NULL, 10, -1, -1, (int*)16, NULL) == ORX_EINVAL);
   /* null handles */
   CHECK(orx_decoder_reset_cache(NULL) == ORX_EINVAL);
   CHECK(orx_batch_step(NULL, NULL, 0, NULL, NULL) == ORX_EINVAL);
