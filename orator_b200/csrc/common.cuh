@@ -179,6 +179,17 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
   return v;
 }
+// Sums two per-lane values over the warp at once: lanes 0-15 end with the
+// sum of `a`, lanes 16-31 with the sum of `b`. Lane 0's addition tree is the
+// one warp_sum uses (xor 16, 8, 4, 2, 1).
+__device__ __forceinline__ float reduce_pair(float a, float b, int lane) {
+  const bool hi = (lane & 16) != 0;
+  float keep = hi ? b : a;
+  keep += __shfl_xor_sync(0xffffffffu, hi ? a : b, 16);
+#pragma unroll
+  for (int m = 8; m > 0; m >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, m);
+  return keep;
+}
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int m = 16; m > 0; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));

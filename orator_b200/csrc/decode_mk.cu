@@ -30,7 +30,7 @@ namespace {
 
 constexpr int kW = 8;                  // warps per CTA
 constexpr int kT = kW * 32;
-constexpr int kD = 4;                  // ring slots per warp
+constexpr int kDMax = 4;               // ring slots per warp (capacity)
 constexpr int kChunkE = 2048;          // bf16 per chunk
 constexpr int kChunkB = kChunkE * 2;   // 4 KiB
 constexpr int kP = 8;                  // pages per attention split (one per warp)
@@ -45,18 +45,21 @@ constexpr unsigned long long kBarrierNs = 1000ull * 1000 * 1000;
 enum Phase : int { kPhQkv = 0, kPhO = 1, kPhGu = 2, kPhDown = 3, kPhLm = 4 };
 
 struct MkSmem {
-  alignas(128) uint8_t ring[kW * kD][kChunkB];   // 128 KiB weight rings
+  alignas(128) uint8_t ring[kW * kDMax][kChunkB];   // 128 KiB weight rings
   alignas(128) uint8_t pages[kP][kPgB];          // 66 KiB attention staging
   alignas(16) uint16_t xs[kInter];               // activation of the phase
-  uint64_t full[kW * kD];
+  uint64_t full[kW * kDMax];
   float red[kW];
   unsigned long long best[kW];
   float qs[2][kHeadDim];
   float sm_m[kW][2], sm_l[kW][2];
   float sm_acc[kW][2][kHeadDim];
   int ptab[kMkMaxSplit * kP];                    // the page table, read once per launch
+  MkLayerW lw[kMkMaxLayers];                     // per-layer weight pointers (no global loads in issue)
   float xown[kMkOwnRows];  // this CTA's rows of the residual x (master copy)
 };
+
+static_assert(sizeof(MkSmem) + 128 <= 227 * 1024, "persistent decode kernel exceeds shared memory");
 
 // Units of a phase held by CTA `b` of `G` and the warp's count of chunks.
 struct PhaseGeom {
@@ -118,6 +121,7 @@ __device__ __forceinline__ void cp_async16_mk(uint32_t dst, const void* src) {
 
 __device__ __forceinline__ float ldcg_f(const float* p) { return __ldcg(p); }
 
+template <int kD>
 __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
   extern __shared__ uint8_t mk_raw[];
   MkSmem& sm = *reinterpret_cast<MkSmem*>((reinterpret_cast<uintptr_t>(mk_raw) + 127) &
@@ -129,7 +133,7 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
   auto ready = [&]() {  // this CTA's inputs of the coming phase are in place
     if (a.trace_cta && tid == 0) a.trace_cta[((bar_k + 1) * G + b) * 2] = global_ns();
   };
-  auto barrier = [&]() {
+  auto barrier_raw = [&]() {
     ++bar_k;
     if (a.trace && b == 0 && tid == 0) a.trace[2 * bar_k] = global_ns();   // arrive
     if (a.trace_cta && tid == 0) a.trace_cta[(bar_k * G + b) * 2 + 1] = global_ns();
@@ -152,48 +156,64 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
   const long long total = per_token * a.steps;
   uint64_t* full = &sm.full[warp * kD];
 
-  // Issue cursor (lane 0): walks (token, layer, phase, unit, row, chunk) in
-  // consumption order without divisions.
+  // Chunk cursor (lane 0): walks (token, layer, phase, unit, row, chunk) in
+  // consumption order without divisions; it feeds the ring.
   auto nu_of = [&](int ph) {
     return ph == 0 ? nph[0] : ph == 1 ? nph[1] : ph == 2 ? nph[2] / 2 : ph == 3 ? nph[3] / 3 : nph[4];
   };
-  int cu_l = 0, cu_ph = 0, cu_k = 0, cu_r = 0, cu_c = 0;
-  auto cursor_settle = [&]() {  // skip phases in which this warp has no units
-    while (true) {
-      if (cu_k < nu_of(cu_ph)) return;
-      cu_k = 0;
-      if (cu_ph == kPhLm) { cu_ph = 0; cu_l = 0; }
-      else if (cu_ph == kPhDown) { cu_ph = (cu_l + 1 < a.L) ? 0 : kPhLm; cu_l = (cu_l + 1 < a.L) ? cu_l + 1 : cu_l; }
-      else ++cu_ph;
-    }
+  struct Cur {
+    int l, ph, k, r, c;
+    const uint16_t* W;  // weight matrix of (l, ph)
+    const uint16_t* p;  // the chunk the next issue copies
   };
-  auto issue = [&](long long seq) {  // lane 0 only; seq selects the ring slot
-    const int ph = cu_ph;
-    const int K = (ph == kPhDown) ? kInter : kHidden;
-    const int unit = (ph == 0 ? u0ph[0] : ph == 1 ? u0ph[1] : ph == 2 ? u0ph[2] : ph == 3 ? u0ph[3] : u0ph[4]) +
-                     warp + cu_k * kW;
+  auto row_ptr = [&](const Cur& q) {
+    const int K = (q.ph == kPhDown) ? kInter : kHidden;
+    const int unit = (q.ph == 0 ? u0ph[0] : q.ph == 1 ? u0ph[1] : q.ph == 2 ? u0ph[2]
+                      : q.ph == 3 ? u0ph[3] : u0ph[4]) + warp + q.k * kW;
     long long row = unit;
-    if (ph == kPhGu) row = (long long)(unit >> 6) * 128 + (unit & 63) + cu_r * 64;
-    const MkLayerW& Lw = a.layers[cu_l];
-    const uint16_t* W = ph == kPhQkv ? Lw.qkv : ph == kPhO ? Lw.o : ph == kPhGu ? Lw.gu
-                      : ph == kPhDown ? Lw.down : a.embed;
+    if (q.ph == kPhGu) row = (long long)(unit >> 6) * 128 + (unit & 63) + q.r * 64;
+    return q.W + row * K;
+  };
+  auto settle = [&](Cur& q) {  // skip phases in which this warp has no units
+    while (true) {
+      if (q.k < nu_of(q.ph)) break;
+      q.k = 0;
+      if (q.ph == kPhLm) { q.ph = 0; q.l = 0; }
+      else if (q.ph == kPhDown) { q.ph = (q.l + 1 < a.L) ? 0 : kPhLm; q.l = (q.l + 1 < a.L) ? q.l + 1 : q.l; }
+      else ++q.ph;
+    }
+    const MkLayerW& Lw = sm.lw[q.l];
+    q.W = q.ph == kPhQkv ? Lw.qkv : q.ph == kPhO ? Lw.o : q.ph == kPhGu ? Lw.gu
+        : q.ph == kPhDown ? Lw.down : a.embed;
+    q.p = row_ptr(q);
+  };
+  auto advance = [&](Cur& q) {
+    const int cpr = (q.ph == kPhDown) ? kInter / kChunkE : 1, rpu = (q.ph == kPhGu) ? 2 : 1;
+    if (++q.c < cpr) {
+      q.p += kChunkE;
+      return;
+    }
+    q.c = 0;
+    if (++q.r < rpu) {
+      q.p = row_ptr(q);
+      return;
+    }
+    q.r = 0;
+    ++q.k;
+    if (q.k < nu_of(q.ph)) q.p = row_ptr(q);
+    else settle(q);
+  };
+  Cur cur = {0, 0, 0, 0, 0, nullptr, nullptr};
+  auto issue = [&](long long seq) {  // lane 0 only; seq selects the ring slot
     const int slot = static_cast<int>(seq % kD);
     mbar_arrive_expect_tx(&full[slot], kChunkB);
-    bulk_g2s(sm.ring[warp * kD + slot], W + row * K + (long long)cu_c * kChunkE, kChunkB,
-             &full[slot]);
-    // advance
-    const int cpr = K / kChunkE, rpu = (ph == kPhGu) ? 2 : 1;
-    if (++cu_c == cpr) {
-      cu_c = 0;
-      if (++cu_r == rpu) {
-        cu_r = 0;
-        ++cu_k;
-        cursor_settle();
-      }
-    }
+    bulk_g2s(sm.ring[warp * kD + slot], cur.p, kChunkB, &full[slot]);
+    advance(cur);
   };
-  cursor_settle();
-
+  for (int i = tid; i < a.L * static_cast<int>(sizeof(MkLayerW) / 8); i += kT)
+    reinterpret_cast<unsigned long long*>(sm.lw)[i] = reinterpret_cast<const unsigned long long*>(a.layers)[i];
+  __syncthreads();
+  settle(cur);
   if (lane == 0) {
     for (int i = 0; i < kD; ++i) mbar_init(&full[i], 1);
     fence_mbar_init();
@@ -201,14 +221,30 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
   }
   __syncwarp();
   long long seq = 0;  // next chunk this warp consumes
+  auto barrier = [&]() { barrier_raw(); };
 
   // Consume one phase: per unit of this warp, rpu rows of cpr chunks each.
+  // A slot is refilled right after the warp's FMAs have consumed the values
+  // it loaded from it (so the bulk copy cannot overwrite unread data and no
+  // proxy fence is needed). Row sums are reduced two at a time: lanes 0-15
+  // finish row A and lanes 16-31 row B in one 5-step butterfly (the same
+  // addition tree as a full-warp reduction, so the sums are unchanged), and
+  // lanes 0 and 16 run the two epilogues side by side. In the gate/up phase
+  // the pair is (gate, up) of one unit.
   auto run_phase = [&](int ph, auto&& epi) {
     const PhaseGeom g = geom(ph, a.vocab);
     const int nu = nph[ph] / g.cpu();
+    float held = 0.f;      // partial of a row waiting for its partner (rpu == 1)
+    int held_unit = -1;
+    // With one chunk per row (K = 2048) every row meets the same activation
+    // slice: keep it in registers for the whole phase.
+    const bool one = g.cpr() == 1;
+    uint4 xr[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xr[j] = reinterpret_cast<const uint4*>(sm.xs)[j * 32 + lane];
     for (int k = 0; k < nu; ++k) {
       const int unit = u0ph[ph] + warp + k * kW;
-      float accs[2] = {0.f, 0.f};
+      float part[2] = {0.f, 0.f};
       for (int r = 0; r < g.rpu; ++r) {
         float acc4[4] = {0.f, 0.f, 0.f, 0.f};
         for (int c = 0; c < g.cpr(); ++c) {
@@ -219,26 +255,39 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
           uint4 wv[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) wv[j] = wp[j * 32 + lane];
-          __syncwarp();
-          if (lane == 0 && seq + kD < total) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(seq + kD);
-          }
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const uint4 w = wv[j];
-            const uint4 xv = xp[j * 32 + lane];
+            const uint4 xv = one ? xr[j] : xp[j * 32 + lane];
             float& acc = acc4[j & 3];
             acc = fma2_bf16(w.x, xv.x, acc);
             acc = fma2_bf16(w.y, xv.y, acc);
             acc = fma2_bf16(w.z, xv.z, acc);
             acc = fma2_bf16(w.w, xv.w, acc);
           }
+          __syncwarp();
+          if (lane == 0 && seq + kD < total) issue(seq + kD);
           ++seq;
         }
-        accs[r] = warp_sum((acc4[0] + acc4[1]) + (acc4[2] + acc4[3]));
+        part[r] = (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
       }
-      if (lane == 0) epi(unit, accs[0], accs[1]);
+      if (g.rpu == 2) {
+        const float s = reduce_pair(part[0], part[1], lane);  // lane 0: gate, lane 16: up
+        const float up = __shfl_sync(0xffffffffu, s, 16);
+        if (lane == 0) epi(unit, s, up);
+      } else if (held_unit >= 0) {
+        const float s = reduce_pair(held, part[0], lane);
+        if (lane == 0) epi(held_unit, s, 0.f);
+        if (lane == 16) epi(unit, s, 0.f);
+        held_unit = -1;
+      } else {
+        held = part[0];
+        held_unit = unit;
+      }
+    }
+    if (held_unit >= 0) {
+      const float s = warp_sum(held);
+      if (lane == 0) epi(held_unit, s, 0.f);
     }
   };
 
@@ -329,7 +378,7 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
     const int items = kKvHeads * nsplit;
 
     for (int l = 0; l < a.L; ++l) {
-      const MkLayerW& Lw = a.layers[l];
+      const MkLayerW& Lw = sm.lw[l];
       uint16_t* kvl = a.kv + (long long)l * a.kv_layer_stride;
       // ---------------- qkv ----------------
       {
@@ -579,7 +628,7 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
           a.x[u] = xn;
         });
       }
-      load_w8(l + 1 < a.L ? a.layers[l + 1].in_ln : a.final_norm, wn);
+      load_w8(l + 1 < a.L ? sm.lw[l + 1].in_ln : a.final_norm, wn);
       barrier();
     }
 
@@ -600,7 +649,10 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
           best = k > best ? k : best;
         }
       });
-      if (lane == 0) sm.best[warp] = best;
+      {
+        const unsigned long long ob = __shfl_sync(0xffffffffu, best, 16);
+        if (lane == 0) sm.best[warp] = ob > best ? ob : best;
+      }
       __syncthreads();
       if (tid == 0) {
         unsigned long long bb = 0;
@@ -627,7 +679,11 @@ size_t decode_mk_smem() { return sizeof(MkSmem) + 128; }
 void launch_decode_mk_config() {
   static std::atomic<unsigned long long> done{0};
   once_per_device(done, [] {
-    cudaFuncSetAttribute(decode_mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(decode_mk_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(decode_mk_smem()));
+    cudaFuncSetAttribute(decode_mk_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(decode_mk_smem()));
+    cudaFuncSetAttribute(decode_mk_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(decode_mk_smem()));
   });
 }
@@ -637,7 +693,14 @@ cudaError_t launch_decode_mk(const MkArgs& a, int grid, cudaStream_t s) {
   const size_t smem = decode_mk_smem();
   MkArgs copy = a;
   void* params[] = {&copy};
-  return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(decode_mk_kernel), dim3(grid),
+  static const int depth = [] {
+    const char* e = std::getenv("ORX_MK_D");
+    return e ? std::atoi(e) : 4;
+  }();
+  const void* fn = depth == 2 ? reinterpret_cast<const void*>(decode_mk_kernel<2>)
+                 : depth == 3 ? reinterpret_cast<const void*>(decode_mk_kernel<3>)
+                              : reinterpret_cast<const void*>(decode_mk_kernel<4>);
+  return cudaLaunchCooperativeKernel(fn, dim3(grid),
                                      dim3(kT), params, smem, s);
 }
 
@@ -646,7 +709,7 @@ int decode_mk_max_grid() {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   launch_decode_mk_config();
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_mk_kernel, kT, decode_mk_smem());
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_mk_kernel<4>, kT, decode_mk_smem());
   return (per >= 1 && sms * kMkOwnRows >= kHidden) ? sms : 0;
 }
 

@@ -98,6 +98,7 @@ Decoder::Decoder(Model* m, bool own) : model(m), own_model_(own) {
   // stays within its attention split table
   const char* nomk = std::getenv("ORX_NO_MK");
   use_mk_ = !(nomk && nomk[0] == '1') && max_pages_ <= kMkMaxSplit * 8 &&
+            c.num_layers <= kMkMaxLayers &&
             decode_mk_max_grid() > 0;
   cudaGetLastError();
   if (use_mk_) {

@@ -178,6 +178,7 @@ void launch_embed_rows(const uint16_t* table, const int* ids, float* out, int ro
 // Persistent cooperative decode kernel (decode_mk.cu).
 constexpr int kMkMaxSplit = 32;  // attention splits per kv head: 32 x 8 pages = 4096 positions
 constexpr int kMkPart = 2 * 132;
+constexpr int kMkMaxLayers = 48;  // layers the persistent kernel keeps pointers for
 constexpr int kMkOwnRows = 16;   // rows of x per CTA: needs a grid of at least 128 CTAs
 struct MkLayerW {
   const uint16_t *qkv, *o, *gu, *down;

@@ -57,10 +57,14 @@ class SessionRouter:
         return best
 
     def grow(self, sid: int, n: int = 1):
-        """Session `sid` appended n tokens (new pages are taken as needed)."""
+        """Session `sid` appended n tokens (new pages are taken as needed);
+        raises RuntimeError, changing nothing, when its rank lacks the pages."""
         r = self.where[sid]
         old = self.lens[sid]
-        self.ranks[r].free_pages -= self._pages(old + n) - self._pages(old)
+        extra = self._pages(old + n) - self._pages(old)
+        if extra > self.ranks[r].free_pages:
+            raise RuntimeError(f"rank {r} has no free page for session {sid}")
+        self.ranks[r].free_pages -= extra
         self.ranks[r].kv_tokens += n
         self.lens[sid] = old + n
 
@@ -81,12 +85,21 @@ class SessionRouter:
     def loads(self) -> list[int]:
         return [ld.kv_tokens for ld in self.ranks]
 
-    def gather_loads(self, rank: int, kv_tokens: int, free_pages: int, group=None):
-        """Replace the modelled (kv_tokens, free_pages) of every rank by the
-        values the ranks report (collective over `group`; host only)."""
+    def gather_loads(self, rank: int, kv_tokens: int, free_pages: int, lens=None, group=None):
+        """Replace the modelled state of every rank by what the ranks report
+        (collective over `group`; host only): (kv_tokens, free_pages) and, in
+        `lens`, the measured cache length of each of the reporting rank's
+        sessions (sid -> tokens). Reported lengths replace the modelled ones,
+        so a later `release` returns what the rank actually held; sessions a
+        rank does not report keep their modelled length."""
         import torch.distributed as dist
         got = [None] * self.world
-        dist.all_gather_object(got, (rank, int(kv_tokens), int(free_pages)), group=group)
-        for r, kv, fp in got:
+        dist.all_gather_object(got, (rank, int(kv_tokens), int(free_pages),
+                                     {int(k): int(v) for k, v in (lens or {}).items()}),
+                               group=group)
+        for r, kv, fp, ln in got:
             self.ranks[r].kv_tokens = kv
             self.ranks[r].free_pages = fp
+            for sid, n in ln.items():
+                if self.where.get(sid) == r:
+                    self.lens[sid] = n

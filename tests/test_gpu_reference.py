@@ -85,6 +85,7 @@ def test_loader_matches_synthetic_init(trio, cuda):
     ours.ResetCache()
     ours.Prefill(x)
     other.Prefill(x)
-    # split-K accumulation is atomic, so the summation order may differ run to run
-    assert np.abs(ours.CopyLogits() - other.CopyLogits()).max() < 1e-2
+    # two decoders on the same weights and rows: split-K partials are summed in
+    # split order, so the logits agree exactly
+    assert np.array_equal(ours.CopyLogits(), other.CopyLogits())
     other.close()

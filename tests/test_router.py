@@ -40,6 +40,45 @@ def test_grow_takes_pages():
     assert r.ranks[0].free_pages == 4 and r.loads() == [0]
 
 
+def test_grow_without_pages_raises_and_keeps_state():
+    r = SessionRouter(world=1, pages_per_rank=2, page=16)
+    r.place(1, 32)                 # both pages
+    with pytest.raises(RuntimeError):
+        r.grow(1)
+    assert r.ranks[0].free_pages == 0 and r.lens[1] == 32 and r.loads() == [32]
+
+
+def _release_worker(rank, world, port, q):
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=30))
+    r = SessionRouter(world, pages_per_rank=100, page=16)
+    a, b = r.place(10, 64), r.place(11, 64)       # one session per rank
+    # each rank's session really holds 20 tokens (it was truncated): report it
+    mine = 10 if rank == a else 11
+    r.gather_loads(rank, kv_tokens=20, free_pages=100 - 2, lens={mine: 20})
+    r.release(10)
+    r.release(11)
+    q.put((rank, r.loads(), [ld.free_pages for ld in r.ranks], a, b))
+    dist.destroy_process_group()
+
+
+def test_gather_loads_then_release_is_consistent():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_release_worker, args=(i, 2, port, q)) for i in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=120) for _ in ps]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, loads, free, a, b in res:
+        assert (a, b) == (0, 1)
+        assert loads == [0, 0]          # the reported 20 tokens come back, not the modelled 64
+        assert free == [100, 100]
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
