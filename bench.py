@@ -159,6 +159,62 @@ def cpu_oracle_rate(sample_tokens: int, warm: int = 1, reps: int = 1):
     return sample_tokens / statistics.median(times), threads, times
 
 
+def reference_gpu_rate(prompt, reps: int = 3):
+    """The reference's own CUDA decoder on this GPU, for the same workload:
+    the unmodified AsrTextDecoder compiled from its sources into
+    oracle/_ref/libref_asr.so (oracle/build_ref.sh), loaded from a checkpoint
+    with the same seeded weights, prefilled with the same 400 rows, then
+    DecodeGreedy(400, 128 tokens, no EOS, batch 128) through its CUDA-graph
+    loop (its fastest path), timed with CUDA events around the call."""
+    import ctypes as C
+    import shutil
+    lib_path = os.path.join(ROOT, "oracle", "_ref", "libref_asr.so")
+    if not os.path.exists(lib_path):
+        return {"unavailable": "oracle/_ref/libref_asr.so not built (oracle/build_ref.sh)"}
+    import torch
+    from oracle import st_writer, synth
+    from orator_b200 import synth_f32
+
+    def gen(seed, tid, shape, is_norm):
+        n = int(np.prod(shape))
+        buf = torch.empty(n, dtype=torch.float32, device="cuda")
+        synth_f32(buf.data_ptr(), n, seed, tid, synth.NORM_STD if is_norm else synth.MATRIX_STD,
+                  1.0 if is_norm else 0.0, True)
+        return (buf.view(torch.int32) >> 16).to(torch.int16).cpu().numpy().view(np.uint16).reshape(shape)
+
+    L = C.CDLL(lib_path)
+    L.ref_create_graphs.restype = C.c_void_p
+    L.ref_create_graphs.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int]
+    L.ref_last_error.restype = C.c_char_p
+    d = tempfile.mkdtemp(prefix="ref_ckpt_")
+    try:
+        st_writer.write_synthetic_model(d, SEED, LAYERS, VOCAB, shards=4, gen=gen)
+        h = L.ref_create_graphs(d.encode(), LAYERS, VOCAB, 2048)
+        if not h:
+            return {"unavailable": "reference decoder failed to load: " + L.ref_last_error().decode()}
+        h = C.c_void_p(h)
+        x = np.ascontiguousarray(prompt, np.float32)
+        assert L.ref_prefill_at(h, x.ctypes.data_as(C.c_void_p), PROMPT_ROWS, 0) == 0
+        ms, n = C.c_float(), C.c_int()
+        times = []
+        for r in range(reps + 1):
+            L.ref_truncate(h, PROMPT_ROWS)
+            rc = L.ref_time_greedy(h, PROMPT_ROWS, NEW_TOKENS, NEW_TOKENS, C.byref(ms), C.byref(n))
+            if rc != 0 or n.value != NEW_TOKENS:
+                return {"unavailable": f"reference DecodeGreedy failed (rc {rc}, {n.value} tokens)"}
+            if r:
+                times.append(ms.value)
+        L.ref_destroy(h)
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    t = statistics.median(times)
+    return {"value": NEW_TOKENS / (t * 1e-3), "unit": "tokens/s", "ms_per_step": t,
+            "workload": WORKLOAD2,
+            "note": "unmodified reference AsrTextDecoder (oracle/_ref) on this GPU, same weights "
+                    "and prompt, DecodeGreedy with its CUDA-graph loop, median of "
+                    f"{reps} after 1 warm-up"}
+
+
 def run_reference(args):
     rank, _, world = dist_env()
     if rank != 0:
@@ -447,6 +503,8 @@ def run_ours(args):
     e2e_ms = f0.elapsed_time(f1)
 
     prof = dec.profile_kernels(iters=20)
+    ref_gpu = (reference_gpu_rate(prompt) if world == 1 and not args.no_reference_gpu
+               else None)
     prefill = measure_prefill(dec, torch, prompt, s)
     ragged = None if args.no_ragged else run_ragged(dec, torch, world, dist, rank, steps=args.ragged_steps)
     ragged_strong = (run_ragged(dec, torch, world, dist, rank, strong=True, steps=args.ragged_steps)
@@ -498,6 +556,10 @@ def run_ours(args):
         "prefill": prefill,
         "clocks": clocks,
     }
+    if ref_gpu is not None:
+        if "value" in ref_gpu:
+            ref_gpu["ours_over_reference"] = value / ref_gpu["value"]
+        line["reference_gpu"] = ref_gpu
     if ragged is not None:
         line["ragged"] = ragged
     if ragged_strong is not None:
@@ -523,6 +585,8 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ragged", action="store_true", help="skip the config-3 ragged batch run")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own CUDA decoder (oracle/_ref)")
     ap.add_argument("--no-config1", action="store_true", help="skip the config-1 fp32 layer run")
     ap.add_argument("--ragged-steps", type=int, default=256,
                     help="decode steps of the config-3 runs (256 = the config; fewer for profiling)")

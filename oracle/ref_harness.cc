@@ -32,14 +32,14 @@ extern "C" {
 
 const char* ref_last_error() { return g_err.c_str(); }
 
-void* ref_create(const char* model_dir, int num_layers, int vocab, int max_seq) {
+static void* create(const char* model_dir, int num_layers, int vocab, int max_seq, bool graphs) {
   try {
     auto* h = new RefHandle;
     orator::model::AsrTextConfig c;
     c.num_layers = num_layers;
     c.vocab_size = vocab;
     c.max_seq_len = max_seq;
-    c.cuda_graph_enabled = false;
+    c.cuda_graph_enabled = graphs;
     h->w = std::make_unique<orator::io::ShardedSafeTensors>(model_dir);
     h->dec = std::make_unique<orator::model::AsrTextDecoder>(c);
     h->dec->LoadWeights(*h->w);
@@ -48,6 +48,41 @@ void* ref_create(const char* model_dir, int num_layers, int vocab, int max_seq) 
   } catch (const std::exception& e) {
     g_err = e.what();
     return nullptr;
+  }
+}
+
+void* ref_create(const char* model_dir, int num_layers, int vocab, int max_seq) {
+  return create(model_dir, num_layers, vocab, max_seq, false);
+}
+
+// As ref_create, with the reference's CUDA-graph decode loop enabled (its
+// default AsrTextConfig, the fastest path of DecodeGreedy).
+void* ref_create_graphs(const char* model_dir, int num_layers, int vocab, int max_seq) {
+  return create(model_dir, num_layers, vocab, max_seq, true);
+}
+
+// Times one DecodeGreedy(start_pos, max_new, no EOS, no ban, batch) call:
+// *ms = elapsed time between CUDA events on the legacy stream around the
+// call (DecodeGreedy synchronizes before returning), *n_out = tokens made.
+int ref_time_greedy(void* p, int start_pos, int max_new, int batch, float* ms, int* n_out) {
+  try {
+    auto* h = static_cast<RefHandle*>(p);
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaDeviceSynchronize();
+    cudaEventRecord(a, 0);
+    auto v = h->dec->DecodeGreedy(start_pos, max_new, -1, -1, 0, batch);
+    cudaEventRecord(b, 0);
+    cudaEventSynchronize(b);
+    cudaEventElapsedTime(ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    *n_out = static_cast<int>(v.size());
+    return cudaGetLastError() == cudaSuccess ? 0 : 1;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return 1;
   }
 }
 

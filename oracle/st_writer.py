@@ -34,7 +34,9 @@ def write_shard(path: str, tensors: list[tuple[str, np.ndarray]]):
 
 
 def write_synthetic_model(out_dir: str, seed: int, num_layers: int, vocab: int,
-                          shards: int = 2) -> str:
+                          shards: int = 2, gen=None) -> str:
+    """``gen(seed, tid, shape, is_norm)`` may supply each tensor's bf16 bit
+    array (e.g. from the bit-exact GPU generator); by default numpy makes it."""
     os.makedirs(out_dir, exist_ok=True)
     items = list(synth.model_tensors(seed, num_layers, vocab))
     groups = [items[i::shards] for i in range(shards)]
@@ -43,8 +45,12 @@ def write_synthetic_model(out_dir: str, seed: int, num_layers: int, vocab: int,
         fname = f"model-{s + 1:05d}-of-{shards:05d}.safetensors"
         tens = []
         for name, tid, shape, is_norm in g:
-            v = synth.make_tensor(seed, tid, shape, is_norm, bf16=False)
-            tens.append((name, synth.f32_to_bf16_bits(v).reshape(shape)))
+            if gen is not None:
+                bits = gen(seed, tid, shape, is_norm)
+            else:
+                v = synth.make_tensor(seed, tid, shape, is_norm, bf16=False)
+                bits = synth.f32_to_bf16_bits(v).reshape(shape)
+            tens.append((name, bits))
             wmap[name] = fname
         write_shard(os.path.join(out_dir, fname), tens)
     with open(os.path.join(out_dir, "model.safetensors.index.json"), "w") as f:

@@ -14,16 +14,19 @@ def available() -> bool:
 
 
 class RefDecoder:
-    def __init__(self, model_dir: str, num_layers: int, vocab: int, max_seq: int = 2048):
+    def __init__(self, model_dir: str, num_layers: int, vocab: int, max_seq: int = 2048,
+                 graphs: bool = False):
         L = C.CDLL(LIB)
-        L.ref_create.restype = C.c_void_p
-        L.ref_create.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int]
+        for f in ("ref_create", "ref_create_graphs"):
+            getattr(L, f).restype = C.c_void_p
+            getattr(L, f).argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int]
         L.ref_last_error.restype = C.c_char_p
         for f in ["ref_prefill_at", "ref_copy_logits", "ref_decode_step_token", "ref_argmax",
                   "ref_destroy", "ref_truncate", "ref_cache_len", "ref_decode_greedy"]:
             getattr(L, f).argtypes = None
         self.L, self.vocab = L, vocab
-        h = L.ref_create(model_dir.encode(), num_layers, vocab, max_seq)
+        h = (L.ref_create_graphs if graphs else L.ref_create)(model_dir.encode(), num_layers,
+                                                               vocab, max_seq)
         if not h:
             raise RuntimeError(L.ref_last_error().decode())
         self.h = C.c_void_p(h)
