@@ -161,49 +161,62 @@ __global__ void __launch_bounds__(kT, 1) decode_mk_kernel(MkArgs a) {
   auto nu_of = [&](int ph) {
     return ph == 0 ? nph[0] : ph == 1 ? nph[1] : ph == 2 ? nph[2] / 2 : ph == 3 ? nph[3] / 3 : nph[4];
   };
+  // Per phase the warp's rows are unit u0 + warp + 8k: row pointers advance
+  // by a fixed stride (gate/up: +8 rows, +64 more when the unit crosses a
+  // 64-unit block, since gate and up rows are interleaved in 128-row tiles).
   struct Cur {
-    int l, ph, k, r, c;
-    const uint16_t* W;  // weight matrix of (l, ph)
-    const uint16_t* p;  // the chunk the next issue copies
+    int l, ph, k, r, c, nu, unit;
+    const uint16_t* rowp;  // row r = 0 of the current unit
+    const uint16_t* p;     // the chunk the next issue copies
   };
-  auto row_ptr = [&](const Cur& q) {
-    const int K = (q.ph == kPhDown) ? kInter : kHidden;
-    const int unit = (q.ph == 0 ? u0ph[0] : q.ph == 1 ? u0ph[1] : q.ph == 2 ? u0ph[2]
-                      : q.ph == 3 ? u0ph[3] : u0ph[4]) + warp + q.k * kW;
-    long long row = unit;
-    if (q.ph == kPhGu) row = (long long)(unit >> 6) * 128 + (unit & 63) + q.r * 64;
-    return q.W + row * K;
-  };
-  auto settle = [&](Cur& q) {  // skip phases in which this warp has no units
+  auto settle = [&](Cur& q) {  // enter phase q.ph at its first unit (skipping empty phases)
     while (true) {
-      if (q.k < nu_of(q.ph)) break;
+      q.nu = nu_of(q.ph);
+      if (q.k < q.nu) break;
       q.k = 0;
       if (q.ph == kPhLm) { q.ph = 0; q.l = 0; }
       else if (q.ph == kPhDown) { q.ph = (q.l + 1 < a.L) ? 0 : kPhLm; q.l = (q.l + 1 < a.L) ? q.l + 1 : q.l; }
       else ++q.ph;
     }
     const MkLayerW& Lw = sm.lw[q.l];
-    q.W = q.ph == kPhQkv ? Lw.qkv : q.ph == kPhO ? Lw.o : q.ph == kPhGu ? Lw.gu
-        : q.ph == kPhDown ? Lw.down : a.embed;
-    q.p = row_ptr(q);
+    const uint16_t* W = q.ph == kPhQkv ? Lw.qkv : q.ph == kPhO ? Lw.o : q.ph == kPhGu ? Lw.gu
+                      : q.ph == kPhDown ? Lw.down : a.embed;
+    const int K = (q.ph == kPhDown) ? kInter : kHidden;
+    q.unit = (q.ph == 0 ? u0ph[0] : q.ph == 1 ? u0ph[1] : q.ph == 2 ? u0ph[2]
+              : q.ph == 3 ? u0ph[3] : u0ph[4]) + warp;
+    const long long row = q.ph == kPhGu ? (long long)(q.unit >> 6) * 128 + (q.unit & 63) : q.unit;
+    q.rowp = W + row * K;
+    q.p = q.rowp;
   };
   auto advance = [&](Cur& q) {
-    const int cpr = (q.ph == kPhDown) ? kInter / kChunkE : 1, rpu = (q.ph == kPhGu) ? 2 : 1;
-    if (++q.c < cpr) {
-      q.p += kChunkE;
-      return;
-    }
-    q.c = 0;
-    if (++q.r < rpu) {
-      q.p = row_ptr(q);
+    if (q.ph == kPhDown) {  // three chunks per row
+      if (++q.c < kInter / kChunkE) {
+        q.p += kChunkE;
+        return;
+      }
+      q.c = 0;
+    } else if (q.ph == kPhGu && q.r == 0) {  // gate row -> up row of the same unit
+      q.r = 1;
+      q.p = q.rowp + 64 * kHidden;
       return;
     }
     q.r = 0;
-    ++q.k;
-    if (q.k < nu_of(q.ph)) q.p = row_ptr(q);
-    else settle(q);
+    if (++q.k == q.nu) {
+      q.k = 0;
+      if (q.ph == kPhLm) { q.ph = 0; q.l = 0; }
+      else if (q.ph == kPhDown) { q.ph = (q.l + 1 < a.L) ? 0 : kPhLm; q.l = (q.l + 1 < a.L) ? q.l + 1 : q.l; }
+      else ++q.ph;
+      settle(q);
+      return;
+    }
+    const int K = (q.ph == kPhDown) ? kInter : kHidden;
+    int step = kW;
+    if (q.ph == kPhGu && (q.unit & 63) >= 64 - kW) step += 64;
+    q.unit += kW;
+    q.rowp += (long long)step * K;
+    q.p = q.rowp;
   };
-  Cur cur = {0, 0, 0, 0, 0, nullptr, nullptr};
+  Cur cur = {0, 0, 0, 0, 0, 0, 0, nullptr, nullptr};
   auto issue = [&](long long seq) {  // lane 0 only; seq selects the ring slot
     const int slot = static_cast<int>(seq % kD);
     mbar_arrive_expect_tx(&full[slot], kChunkB);
