@@ -19,7 +19,8 @@ mkdir -p "$OUT/obj"
 NVCC="${NVCC:-nvcc}"
 GEN="-gencode arch=compute_100a,code=sm_100a"
 objs=()
-for f in src/model/asr_text_decoder.cu src/model/asr_gemm.cu src/model/asr_ops.cu; do
+for f in src/model/asr_text_decoder.cu src/model/asr_gemm.cu src/model/asr_ops.cu \
+         src/pipeline/gpu_vad.cu; do
   o="$OUT/obj/$(basename "$f").o"
   "$NVCC" -std=c++20 -O3 $GEN -Xcompiler -fPIC -I"$R/include" -c "$R/$f" -o "$o"
   objs+=("$o")
@@ -33,4 +34,9 @@ done
 g++ -std=c++20 -O2 -fPIC -I"$R/include" -I/usr/local/cuda/include \
   -c "$HERE/ref_harness.cc" -o "$OUT/obj/ref_harness.o"
 "$NVCC" -shared $GEN -o "$OUT/libref_asr.so" "${objs[@]}" "$OUT/obj/ref_harness.o" -lcudart
-echo "built $OUT/libref_asr.so"
+# the reference's CPU speech detector (a test utility of the reference)
+g++ -std=c++20 -O2 -fPIC -shared -I"$R/include" -I"$R/test/utils" -I/usr/local/cuda/include \
+  "$R/test/utils/asr_vad_cpu.cc" "$R/src/io/safetensor.cc" "$R/src/core/tensor.cc" \
+  "$R/src/gpu/memory.cc" "$HERE/ref_vad_harness.cc" -L/usr/local/cuda/lib64 -lcudart \
+  -o "$OUT/libref_vad_cpu.so"
+echo "built $OUT/libref_asr.so $OUT/libref_vad_cpu.so"

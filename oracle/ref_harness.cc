@@ -18,6 +18,7 @@
 #include "model/asr_gemm.h"
 #include "model/asr_ops.cuh"
 #include "model/asr_text_decoder.h"
+#include "pipeline/gpu_vad.h"
 
 namespace {
 struct RefHandle {
@@ -186,6 +187,52 @@ int ref_op_linear(const float* in, const uint16_t* w, const float* bias, float* 
 int ref_op_linear_pre(const uint16_t* in, const uint16_t* w, const float* bias, float* out, int M,
                       int K, int N, int act) {
   REF_OP(gm::LinearPre(in, w, bias, out, M, K, N, act))
+}
+
+// ---- the reference's GPU speech detector (src/pipeline/gpu_vad.cu) ----
+void* ref_gpuvad_create(const char* weights_path) {
+  try {
+    orator::pipeline::GpuVad::Params p;
+    p.silero_model_path = weights_path;
+    return new orator::pipeline::GpuVad(p);
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return nullptr;
+  }
+}
+void ref_gpuvad_destroy(void* h) { delete static_cast<orator::pipeline::GpuVad*>(h); }
+// Per-window probabilities of n samples from a fresh state (DebugWindowProbs).
+int ref_gpuvad_probs(void* h, const float* pcm, int n, float* out) {
+  try {
+    auto v = static_cast<orator::pipeline::GpuVad*>(h)->DebugWindowProbs(pcm, n);
+    std::memcpy(out, v.data(), v.size() * sizeof(float));
+    return static_cast<int>(v.size());
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return -1;
+  }
+}
+void ref_gpuvad_reset(void* h) { static_cast<orator::pipeline::GpuVad*>(h)->Reset(); }
+// Push samples and drain finished speech segments: pairs (start, end) into
+// out[2 * cap]; returns the number of segments.
+int ref_gpuvad_push_drain(void* h, const float* pcm, int n, int finalize, long* out, int cap) {
+  try {
+    auto* v = static_cast<orator::pipeline::GpuVad*>(h);
+    v->Push(pcm, n);
+    std::vector<orator::core::VadSegmentResult> segs;
+    v->DrainSegments(finalize != 0, &segs);
+    int k = 0;
+    for (const auto& s : segs) {
+      if (k >= cap) break;
+      out[2 * k] = s.start_sample;
+      out[2 * k + 1] = s.end_sample;
+      ++k;
+    }
+    return k;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return -1;
+  }
 }
 
 void ref_truncate(void* p, int len) { static_cast<RefHandle*>(p)->dec->TruncateCache(len); }
