@@ -241,6 +241,29 @@ int orx_decoder_trace_ctas(orx_decoder* d, int steps, void* stream, unsigned lon
 int orx_argmax_banned_noalloc(const float* d_logits, int n, int ban0, int ban1, int* d_out,
                               void* stream);
 
+/* ---- Batched speech detector (the Silero-shaped model of the reference's
+ * GpuVad, src/pipeline/gpu_vad.cu, batched over streams instead of over one
+ * stream's windows). ---- */
+typedef struct orx_vad orx_vad;
+/* GpuVad::GpuVad (include/pipeline/gpu_vad.h:40): `streams` independent
+ * streams, LSTM state and 64-sample context zeroed, on the current device. */
+int orx_vad_create(int streams, orx_vad** out);
+void orx_vad_destroy(orx_vad* v);
+/* GpuVad::LoadWeights (gpu_vad.cu:242-271), one fp32 host tensor at a time by
+ * its checkpoint name ("stft.forward_basis_buffer", "encoder.{0..3}.reparam_conv.
+ * {weight,bias}", "decoder.rnn.{weight,bias}_{ih,hh}", "decoder.decoder.2.{weight,bias}"). */
+int orx_vad_set_tensor(orx_vad* v, const char* name, const float* data, size_t numel);
+/* Seeded synthetic weights (no reference counterpart; test and bench data). */
+int orx_vad_init_synthetic(orx_vad* v, int seed);
+/* GpuVad::Reset (gpu_vad.cu:471-483): every stream's LSTM state and context. */
+int orx_vad_reset(orx_vad* v);
+/* GpuVad::RunBatch (gpu_vad.cu:320-368) for all streams at once: pcm
+ * [streams][steps * 512] fp32 -> speech probabilities probs [streams][steps];
+ * both on the device (on_device = 1, asynchronous on `stream`) or both on the
+ * host (synchronous). State carries over to the next call. */
+int orx_vad_run(orx_vad* v, const float* pcm, int steps, float* probs, int on_device,
+                void* stream);
+
 /* Seeded synthetic fp32 data on the device, bit-exact with oracle/synth.py
  * (test and benchmark inputs; no reference counterpart). */
 int orx_synth_f32(float* d_out, long long n, int seed, int tensor_id, double std, float mean,

@@ -114,6 +114,12 @@ _SIGS = {
                                     C.c_int, C.c_int, C.c_int, C.c_float, C.c_int, C.c_void_p]),
     "orx_argmax_banned": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                     C.c_void_p]),
+    "orx_vad_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
+    "orx_vad_destroy": (None, [C.c_void_p]),
+    "orx_vad_set_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]),
+    "orx_vad_init_synthetic": (C.c_int, [C.c_void_p, C.c_int]),
+    "orx_vad_reset": (C.c_int, [C.c_void_p]),
+    "orx_vad_run": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]),
     "orx_synth_f32": (C.c_int, [C.c_void_p, C.c_longlong, C.c_int, C.c_int, C.c_double,
                                 C.c_float, C.c_int, C.c_void_p]),
 }

@@ -22,6 +22,11 @@ struct orx_layer32 {
   int cap = 0;
 };
 
+struct orx_vad {
+  orx::BatchVad* v = nullptr;
+  int device = 0;
+};
+
 struct orx_batch {
   orx::BatchDecoder* b = nullptr;
   int device = 0;
@@ -707,6 +712,68 @@ int orx_argmax_banned(const float* logits, int n, int ban0, int ban1, int* d_out
     need(d_out, "out");
     orx::op_argmax_banned(logits, n, ban0, ban1, d_out, S(stream));
     orx::check(cudaGetLastError(), "argmax");
+  });
+}
+
+int orx_vad_create(int streams, orx_vad** out) {
+  return guard([&] {
+    need(out, "out");
+    *out = nullptr;
+    auto* h = new orx_vad;
+    try {
+      cudaGetDevice(&h->device);
+      h->v = new orx::BatchVad(streams);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+void orx_vad_destroy(orx_vad* v) {
+  if (!v) return;
+  DeviceScope ds(v->device);
+  delete v->v;
+  delete v;
+}
+
+int orx_vad_set_tensor(orx_vad* v, const char* name, const float* data, size_t numel) {
+  return guard([&] {
+    need(v, "vad");
+    need(name, "name");
+    need(data, "data");
+    v->v->set_tensor(name, data, numel);
+  });
+}
+
+int orx_vad_init_synthetic(orx_vad* v, int seed) {
+  return guard([&] {
+    need(v, "vad");
+    DeviceScope ds(v->device);
+    v->v->init_synthetic(seed);
+  });
+}
+
+int orx_vad_reset(orx_vad* v) {
+  return guard([&] {
+    need(v, "vad");
+    DeviceScope ds(v->device);
+    v->v->reset();
+  });
+}
+
+int orx_vad_run(orx_vad* v, const float* pcm, int steps, float* probs, int on_device,
+                void* stream) {
+  return guard([&] {
+    need(v, "vad");
+    if (steps < 0) throw std::invalid_argument("negative step count");
+    if (steps == 0) return;
+    need(pcm, "pcm");
+    need(probs, "probs");
+    DeviceScope ds(v->device);
+    if (on_device) v->v->run_device(pcm, steps, probs, S(stream));
+    else v->v->run_host(pcm, steps, probs, S(stream));
   });
 }
 

@@ -265,6 +265,29 @@ class BatchDecoder {
   GraphCache<cudaGraphExec_t, cudaError_t (*)(cudaGraphExec_t)> graphs_{cudaGraphExecDestroy};
 };
 
+// Batched Silero-shaped speech detector (vad.cu): `streams` independent
+// streams advance one 512-sample window per step; LSTM state and the 64-sample
+// context are carried per stream across calls.
+class BatchVad {
+ public:
+  explicit BatchVad(int streams);
+  ~BatchVad();
+  BatchVad(const BatchVad&) = delete;
+  BatchVad& operator=(const BatchVad&) = delete;
+  int streams() const;
+  void set_tensor(const std::string& name, const float* data, size_t n);  // host fp32
+  void init_synthetic(int seed);
+  void reset();
+  // pcm [streams][steps * 512] -> probs [streams][steps] (device / host).
+  void run_device(const float* d_pcm, int steps, float* d_probs, cudaStream_t s);
+  void run_host(const float* pcm, int steps, float* probs, cudaStream_t s);
+
+ private:
+  void upload();
+  struct Impl;
+  Impl* p_;
+};
+
 // fp32 single decoder layer (layer32.cu): fp32 weights, activations and KV.
 struct Layer32;
 Layer32* layer32_create(int max_seq_len, float eps, float theta);

@@ -1,0 +1,532 @@
+// Batched Silero-shaped speech detector: thousands of independent streams,
+// one window (64 context + 512 new samples) per stream per step.
+//
+// The reference detector (src/pipeline/gpu_vad.cu) serves one stream at a
+// time: it batches the windows of that stream through six kernels and scans
+// the LSTM in a single 128-thread block. Here the stream is the batch axis:
+//  * vad_frontend_kernel: the whole conv front end of a chunk of steps for
+//    every stream at once (windows are independent of the LSTM state): a CTA
+//    takes 32 windows, stages their reflect-padded input in shared memory,
+//    computes the 4-frame STFT magnitude against the 258 x 256 basis (staged
+//    in 32-bin slices), then the four conv1d + ReLU blocks, and writes the
+//    128-wide LSTM input of each window;
+//  * vad_lstm_kernel: a CTA owns 32 streams and scans all steps of the chunk
+//    (streams never interact, so no grid-wide sync): gates = [x | h] x
+//    [W_ih | W_hh]^T + b with the weights pre-transposed to [256][512] so a
+//    warp's loads are coalesced, the cell update, and the head
+//    sigmoid(b + relu(h) . w).
+// All arithmetic is fp32 with fmaf, as the reference (different summation
+// order only).
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "engine.h"
+
+namespace orx {
+namespace {
+
+constexpr int kCtx = 64, kWin = 512, kIn = 576, kPad = 640;
+constexpr int kNfft = 256, kHop = 128, kBins = 129, kFrames = 4, kH = 128;
+constexpr int kFeWin = 32;   // windows per front-end CTA
+constexpr int kBinTile = 32; // STFT bins per basis slice
+
+struct VadW {
+  const float* basis;  // [258][256]
+  const float* w0; const float* b0;  // [128][129][3]
+  const float* w1; const float* b1;  // [64][128][3]
+  const float* w2; const float* b2;  // [64][64][3]
+  const float* w3; const float* b3;  // [128][64][3]
+  const float* wt;     // [256][512]: rows 0-127 W_ih^T, 128-255 W_hh^T
+  const float* bias;   // [512] = b_ih + b_hh
+  const float* head;   // [128]
+  float head_b;
+};
+
+// Row strides padded so that the 32 lanes of a warp (32 windows, or 8 bin
+// groups) hit 32 different banks.
+constexpr int kXs = kPad + 4;         // padded input row
+constexpr int kBs = kNfft + 1;        // basis row
+constexpr int kMs = kBins * kFrames + 1;  // magnitude row [ci * 4 + t]
+constexpr int kE0s = 128 * 4 + 1;     // enc0 row [c * 4 + t]
+constexpr int kE1s = 64 * 2 + 1;      // enc1 row [c * 2 + t]
+constexpr int kE2s = 64 + 1;          // enc2 row
+
+struct FeSmem {
+  float x[kFeWin][kXs];               // 80.5 KiB padded inputs
+  union {
+    float basis[2 * kBinTile][kBs];   // 64.3 KiB: re rows, then im rows, of a bin slice
+    float e0[kFeWin][kE0s];           // 64.1 KiB
+  };
+  union {
+    float mag[kFeWin][kMs];           // 64.6 KiB
+    struct {
+      float e1[kFeWin][kE1s];
+      float e2[kFeWin][kE2s];
+    };
+  };
+};
+
+// pcm: [S][steps * 512]; ctx: [S][64] (the context before step 0).
+// Window (s, k) = global window id s * steps + k; out: [steps][S][128].
+__global__ void __launch_bounds__(256, 1) vad_frontend_kernel(const float* __restrict__ pcm,
+                                                              const float* __restrict__ ctx,
+                                                              int S, int steps, VadW w,
+                                                              float* __restrict__ out) {
+  extern __shared__ uint8_t fe_raw[];
+  FeSmem& sm = *reinterpret_cast<FeSmem*>((reinterpret_cast<uintptr_t>(fe_raw) + 15) & ~uintptr_t(15));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long nwin = (long long)S * steps;
+  const long long w0 = (long long)blockIdx.x * kFeWin;
+  const int nw = static_cast<int>(nwin - w0 < kFeWin ? nwin - w0 : kFeWin);
+  const long long row = (long long)steps * kWin;
+
+  // ---- padded inputs: [context | window] then 64 reflected samples ----
+  for (int i = tid; i < kFeWin * kPad; i += 256) {
+    const int wi = i / kPad, j = i % kPad;
+    float v = 0.f;
+    if (wi < nw) {
+      const long long g = w0 + wi;
+      const int s = static_cast<int>(g / steps), k = static_cast<int>(g % steps);
+      const int jj = j < kIn ? j : 2 * kIn - 2 - j;  // reflect right: out[576+i] = in[574-i]
+      const long long pos = (long long)k * kWin - kCtx + jj;
+      v = pos >= 0 ? pcm[s * row + pos] : ctx[(long long)s * kCtx + kCtx + pos];
+    }
+    sm.x[wi][j] = v;
+  }
+
+  // ---- STFT magnitude: thread = one window (4 frames) x 4 bins of a slice ----
+  {
+    const int wsel = tid >> 3;
+    const int bsel = (tid & 7) * 4;
+    for (int f0 = 0; f0 < kBins; f0 += kBinTile) {
+      const int nb = kBins - f0 < kBinTile ? kBins - f0 : kBinTile;
+      __syncthreads();  // previous slice consumed (and inputs written)
+      for (int i = tid; i < 2 * kBinTile * kNfft; i += 256) {
+        const int r = i / kNfft, k = i % kNfft;
+        const int fr = r % kBinTile;
+        const int f = r < kBinTile ? f0 + fr : kBins + f0 + fr;
+        sm.basis[r][k] = fr < nb ? __ldg(w.basis + (long long)f * kNfft + k) : 0.f;
+      }
+      __syncthreads();
+      float re[4][4], im[4][4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) re[t][q] = im[t][q] = 0.f;
+      const float* xw = sm.x[wsel];
+#pragma unroll 4
+      for (int k = 0; k < kNfft; ++k) {
+        float xv[4], br[4], bi[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) xv[t] = xw[t * kHop + k];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          br[q] = sm.basis[bsel + q][k];
+          bi[q] = sm.basis[kBinTile + bsel + q][k];
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            re[t][q] = fmaf(xv[t], br[q], re[t][q]);
+            im[t][q] = fmaf(xv[t], bi[q], im[t][q]);
+          }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (bsel + q < nb)
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            sm.mag[wsel][(f0 + bsel + q) * 4 + t] =
+                sqrtf(re[t][q] * re[t][q] + im[t][q] * im[t][q]);
+    }
+  }
+  __syncthreads();
+
+  // The conv blocks: lane = window, warp = a group of output channels, so a
+  // warp's weight loads are uniform (broadcast) and read once per CTA.
+  // ---- enc0: 129 -> 128, 4 frames, k3 s1 p1, ReLU ----
+  {
+    const int cg = warp * 16;
+    float acc[16][4];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const float b = __ldg(w.b0 + cg + c);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) acc[c][t] = b;
+    }
+    const float* mw = sm.mag[lane];
+    for (int ci = 0; ci < kBins; ++ci) {
+      const float in[6] = {0.f, mw[ci * 4], mw[ci * 4 + 1], mw[ci * 4 + 2], mw[ci * 4 + 3], 0.f};
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float* wr = w.w0 + ((long long)(cg + c) * kBins + ci) * 3;
+        const float k0 = __ldg(wr), k1 = __ldg(wr + 1), k2 = __ldg(wr + 2);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float a2 = acc[c][t];
+          a2 = fmaf(in[t], k0, a2);
+          a2 = fmaf(in[t + 1], k1, a2);
+          a2 = fmaf(in[t + 2], k2, a2);
+          acc[c][t] = a2;
+        }
+      }
+    }
+    __syncthreads();  // e0 reuses the basis slice
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+#pragma unroll
+      for (int t = 0; t < 4; ++t) sm.e0[lane][(cg + c) * 4 + t] = fmaxf(acc[c][t], 0.f);
+  }
+  __syncthreads();
+  // ---- enc1: 128 -> 64, 4 -> 2, k3 s2 p1 (out t reads 2t-1, 2t, 2t+1) ----
+  {
+    const int cg = warp * 8;
+    float acc[8][2];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c][0] = acc[c][1] = __ldg(w.b1 + cg + c);
+    const float* ew = sm.e0[lane];
+    for (int ci = 0; ci < 128; ++ci) {
+      const float i0 = ew[ci * 4], i1 = ew[ci * 4 + 1], i2 = ew[ci * 4 + 2], i3 = ew[ci * 4 + 3];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float* wr = w.w1 + ((long long)(cg + c) * 128 + ci) * 3;
+        const float k0 = __ldg(wr), k1 = __ldg(wr + 1), k2 = __ldg(wr + 2);
+        acc[c][0] = fmaf(i1, k2, fmaf(i0, k1, acc[c][0]));             // positions -1 (zero), 0, 1
+        acc[c][1] = fmaf(i3, k2, fmaf(i2, k1, fmaf(i1, k0, acc[c][1])));  // positions 1, 2, 3
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      sm.e1[lane][(cg + c) * 2] = fmaxf(acc[c][0], 0.f);
+      sm.e1[lane][(cg + c) * 2 + 1] = fmaxf(acc[c][1], 0.f);
+    }
+  }
+  __syncthreads();
+  // ---- enc2: 64 -> 64, 2 -> 1, k3 s2 p1 (reads positions -1, 0, 1) ----
+  {
+    const int cg = warp * 8;
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = __ldg(w.b2 + cg + c);
+    const float* ew = sm.e1[lane];
+    for (int ci = 0; ci < 64; ++ci) {
+      const float a0 = ew[ci * 2], a1 = ew[ci * 2 + 1];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float* wr = w.w2 + ((long long)(cg + c) * 64 + ci) * 3;
+        acc[c] = fmaf(a1, __ldg(wr + 2), fmaf(a0, __ldg(wr + 1), acc[c]));
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) sm.e2[lane][cg + c] = fmaxf(acc[c], 0.f);
+  }
+  __syncthreads();
+  // ---- enc3: 64 -> 128, 1 -> 1, k3 s1 p1 (only the centre tap sees data) ----
+  {
+    const int cg = warp * 16;
+    float acc[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) acc[c] = __ldg(w.b3 + cg + c);
+    const float* ew = sm.e2[lane];
+    for (int ci = 0; ci < 64; ++ci) {
+      const float a = ew[ci];
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        acc[c] = fmaf(a, __ldg(w.w3 + ((long long)(cg + c) * 64 + ci) * 3 + 1), acc[c]);
+    }
+    if (lane < nw) {
+      const long long g = w0 + lane;
+      const int s = static_cast<int>(g / steps), k = static_cast<int>(g % steps);
+      float* o = out + ((long long)k * S + s) * kH + cg;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) o[c] = fmaxf(acc[c], 0.f);
+    }
+  }
+}
+
+// The next chunk's context: the last 64 samples of each stream's chunk.
+__global__ void vad_ctx_kernel(const float* pcm, int S, int steps, float* ctx) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)S * kCtx) return;
+  const long long s = i / kCtx, j = i % kCtx;
+  ctx[i] = pcm[s * steps * kWin + (long long)steps * kWin - kCtx + j];
+}
+
+constexpr int kLstmStreams = 32;
+
+// h, c: [S][128] carried state; xin: [steps][S][128]; probs: [S][steps].
+__global__ void __launch_bounds__(256, 1) vad_lstm_kernel(const float* __restrict__ xin, int S,
+                                                          int steps, VadW w, float* __restrict__ h,
+                                                          float* __restrict__ c,
+                                                          float* __restrict__ probs) {
+  __shared__ float xh[kLstmStreams][2 * kH];  // [x | h] per stream
+  __shared__ float red[kLstmStreams][kH / 2 + 1];
+  const int tid = threadIdx.x;
+  const int s0 = blockIdx.x * kLstmStreams;
+  const int ns = S - s0 < kLstmStreams ? S - s0 : kLstmStreams;
+  // thread: 8 streams x 2 hidden units x 4 gates
+  const int sg = (tid >> 6) * 8;      // streams sg .. sg+7
+  const int j0 = (tid & 63) * 2;      // hidden units j0, j0+1
+  float cst[8][2];
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+      cst[a][u] = (sg + a < ns) ? c[(long long)(s0 + sg + a) * kH + j0 + u] : 0.f;
+  for (int i = tid; i < kLstmStreams * kH; i += 256) {
+    const int a = i / kH, j = i % kH;
+    xh[a][kH + j] = a < ns ? h[(long long)(s0 + a) * kH + j] : 0.f;
+  }
+  float bias[4][2];
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+#pragma unroll
+    for (int u = 0; u < 2; ++u) bias[g][u] = __ldg(w.bias + g * kH + j0 + u);
+  const float hw0 = __ldg(w.head + j0), hw1 = __ldg(w.head + j0 + 1);
+
+  for (int k = 0; k < steps; ++k) {
+    for (int i = tid; i < kLstmStreams * kH; i += 256) {
+      const int a = i / kH, j = i % kH;
+      xh[a][j] = a < ns ? __ldg(xin + ((long long)k * S + s0 + a) * kH + j) : 0.f;
+    }
+    __syncthreads();
+    float acc[8][4][2];
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        acc[a][g][0] = bias[g][0];
+        acc[a][g][1] = bias[g][1];
+      }
+    for (int kk = 0; kk < 2 * kH; ++kk) {
+      const float* wr = w.wt + (long long)kk * 4 * kH + j0;
+      float2 wv[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) wv[g] = __ldg(reinterpret_cast<const float2*>(wr + g * kH));
+#pragma unroll
+      for (int a = 0; a < 8; ++a) {
+        const float v = xh[sg + a][kk];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          acc[a][g][0] = fmaf(v, wv[g].x, acc[a][g][0]);
+          acc[a][g][1] = fmaf(v, wv[g].y, acc[a][g][1]);
+        }
+      }
+    }
+    __syncthreads();  // every thread has read h of this step
+    float part[8];
+#pragma unroll
+    for (int a = 0; a < 8; ++a) {
+      float hs[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float gi = 1.0f / (1.0f + expf(-acc[a][0][u]));
+        const float gf = 1.0f / (1.0f + expf(-acc[a][1][u]));
+        const float gg = tanhf(acc[a][2][u]);
+        const float go = 1.0f / (1.0f + expf(-acc[a][3][u]));
+        cst[a][u] = gf * cst[a][u] + gi * gg;
+        hs[u] = go * tanhf(cst[a][u]);
+        xh[sg + a][kH + j0 + u] = hs[u];
+      }
+      part[a] = fmaxf(hs[0], 0.f) * hw0 + fmaxf(hs[1], 0.f) * hw1;
+    }
+#pragma unroll
+    for (int a = 0; a < 8; ++a) red[sg + a][tid & 63] = part[a];
+    __syncthreads();
+    if (tid < ns) {
+      float d = w.head_b;
+      for (int q = 0; q < kH / 2; ++q) d += red[tid][q];
+      probs[(long long)(s0 + tid) * steps + k] = 1.0f / (1.0f + expf(-d));
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < kLstmStreams * kH; i += 256) {
+    const int a = i / kH, j = i % kH;
+    if (a < ns) h[(long long)(s0 + a) * kH + j] = xh[a][kH + j];
+  }
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+      if (sg + a < ns) c[(long long)(s0 + sg + a) * kH + j0 + u] = cst[a][u];
+}
+
+}  // namespace
+
+struct BatchVad::Impl {
+  int streams = 0;
+  std::vector<float> host[15];
+  bool have[15] = {};
+  float* d_w = nullptr;          // all weights, packed
+  size_t off[20] = {};
+  float *d_h = nullptr, *d_c = nullptr, *d_ctx = nullptr, *d_xin = nullptr;
+  float *d_pcm = nullptr, *d_probs = nullptr;
+  long long xin_cap = 0, pcm_cap = 0, probs_cap = 0;
+  bool uploaded = false;
+  VadW w{};
+};
+
+namespace {
+const char* kVadNames[15] = {
+    "stft.forward_basis_buffer", "encoder.0.reparam_conv.weight", "encoder.0.reparam_conv.bias",
+    "encoder.1.reparam_conv.weight", "encoder.1.reparam_conv.bias",
+    "encoder.2.reparam_conv.weight", "encoder.2.reparam_conv.bias",
+    "encoder.3.reparam_conv.weight", "encoder.3.reparam_conv.bias", "decoder.rnn.weight_ih",
+    "decoder.rnn.weight_hh", "decoder.rnn.bias_ih", "decoder.rnn.bias_hh",
+    "decoder.decoder.2.weight", "decoder.decoder.2.bias"};
+const size_t kVadSizes[15] = {258 * 256, 128 * 129 * 3, 128, 64 * 128 * 3, 64, 64 * 64 * 3, 64,
+                              128 * 64 * 3, 128, 512 * 128, 512 * 128, 512, 512, 128, 1};
+}  // namespace
+
+BatchVad::BatchVad(int streams) : p_(new Impl) {
+  if (streams <= 0) throw std::invalid_argument("streams must be positive");
+  p_->streams = streams;
+  p_->d_h = dalloc<float>((size_t)streams * kH);
+  p_->d_c = dalloc<float>((size_t)streams * kH);
+  p_->d_ctx = dalloc<float>((size_t)streams * kCtx);
+  reset();
+}
+
+BatchVad::~BatchVad() {
+  for (void* q : {(void*)p_->d_w, (void*)p_->d_h, (void*)p_->d_c, (void*)p_->d_ctx,
+                  (void*)p_->d_xin, (void*)p_->d_pcm, (void*)p_->d_probs})
+    if (q) cudaFree(q);
+  delete p_;
+}
+
+int BatchVad::streams() const { return p_->streams; }
+
+void BatchVad::set_tensor(const std::string& name, const float* data, size_t n) {
+  for (int i = 0; i < 15; ++i)
+    if (name == kVadNames[i]) {
+      if (n != kVadSizes[i]) throw std::invalid_argument("wrong element count for " + name);
+      p_->host[i].assign(data, data + n);
+      p_->have[i] = true;
+      p_->uploaded = false;
+      return;
+    }
+  throw std::invalid_argument("unknown detector tensor " + name);
+}
+
+void BatchVad::reset() {
+  ORX_CHECK(cudaMemset(p_->d_h, 0, sizeof(float) * p_->streams * kH));
+  ORX_CHECK(cudaMemset(p_->d_c, 0, sizeof(float) * p_->streams * kH));
+  ORX_CHECK(cudaMemset(p_->d_ctx, 0, sizeof(float) * p_->streams * kCtx));
+}
+
+// Packs the weights in the kernels' layouts: the LSTM matrices transposed to
+// [256][512] ([W_ih | W_hh]^T), the two LSTM biases summed.
+void BatchVad::upload() {
+  for (int i = 0; i < 15; ++i)
+    if (!p_->have[i]) throw std::invalid_argument(std::string("missing detector tensor ") + kVadNames[i]);
+  std::vector<float> pk;
+  auto put = [&](int slot, const float* src, size_t n) {
+    p_->off[slot] = pk.size();
+    pk.insert(pk.end(), src, src + n);
+    while (pk.size() % 4) pk.push_back(0.f);  // 16-byte alignment of every tensor
+  };
+  for (int i = 0; i < 9; ++i) put(i, p_->host[i].data(), p_->host[i].size());
+  std::vector<float> wt((size_t)2 * kH * 4 * kH);
+  for (int r = 0; r < 4 * kH; ++r)
+    for (int k = 0; k < kH; ++k) {
+      wt[(size_t)k * 4 * kH + r] = p_->host[9][(size_t)r * kH + k];
+      wt[(size_t)(kH + k) * 4 * kH + r] = p_->host[10][(size_t)r * kH + k];
+    }
+  put(9, wt.data(), wt.size());
+  std::vector<float> b(4 * kH);
+  for (int r = 0; r < 4 * kH; ++r) b[r] = p_->host[11][r] + p_->host[12][r];
+  put(10, b.data(), b.size());
+  put(11, p_->host[13].data(), kH);
+  if (p_->d_w) cudaFree(p_->d_w);
+  p_->d_w = dalloc<float>(pk.size());
+  ORX_CHECK(cudaMemcpy(p_->d_w, pk.data(), pk.size() * 4, cudaMemcpyHostToDevice));
+  const float* d = p_->d_w;
+  VadW& w = p_->w;
+  w.basis = d + p_->off[0];
+  w.w0 = d + p_->off[1]; w.b0 = d + p_->off[2];
+  w.w1 = d + p_->off[3]; w.b1 = d + p_->off[4];
+  w.w2 = d + p_->off[5]; w.b2 = d + p_->off[6];
+  w.w3 = d + p_->off[7]; w.b3 = d + p_->off[8];
+  w.wt = d + p_->off[9];
+  w.bias = d + p_->off[10];
+  w.head = d + p_->off[11];
+  w.head_b = p_->host[14][0];
+  p_->uploaded = true;
+}
+
+void BatchVad::run_device(const float* d_pcm, int steps, float* d_probs, cudaStream_t s) {
+  if (steps <= 0) return;
+  if (!p_->uploaded) upload();
+  const int S = p_->streams;
+  const long long need = (long long)steps * S * kH;
+  if (need > p_->xin_cap) {
+    ORX_CHECK(cudaStreamSynchronize(s));
+    if (p_->d_xin) cudaFree(p_->d_xin);
+    p_->d_xin = dalloc<float>(need);
+    p_->xin_cap = need;
+  }
+  static std::atomic<unsigned long long> configured{0};
+  const size_t smem = sizeof(FeSmem) + 16;
+  once_per_device(configured, [&] {
+    cudaFuncSetAttribute(vad_frontend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+  });
+  const long long nwin = (long long)S * steps;
+  vad_frontend_kernel<<<static_cast<unsigned>((nwin + kFeWin - 1) / kFeWin), 256, smem, s>>>(
+      d_pcm, p_->d_ctx, S, steps, p_->w, p_->d_xin);
+  vad_lstm_kernel<<<(S + kLstmStreams - 1) / kLstmStreams, 256, 0, s>>>(
+      p_->d_xin, S, steps, p_->w, p_->d_h, p_->d_c, d_probs);
+  vad_ctx_kernel<<<(S * kCtx + 255) / 256, 256, 0, s>>>(d_pcm, S, steps, p_->d_ctx);
+  ORX_CHECK(cudaGetLastError());
+}
+
+void BatchVad::run_host(const float* pcm, int steps, float* probs, cudaStream_t s) {
+  if (steps <= 0) return;
+  const int S = p_->streams;
+  const long long np = (long long)S * steps * kWin, nq = (long long)S * steps;
+  if (np > p_->pcm_cap) {
+    ORX_CHECK(cudaStreamSynchronize(s));
+    if (p_->d_pcm) cudaFree(p_->d_pcm);
+    p_->d_pcm = dalloc<float>(np);
+    p_->pcm_cap = np;
+  }
+  if (nq > p_->probs_cap) {
+    ORX_CHECK(cudaStreamSynchronize(s));
+    if (p_->d_probs) cudaFree(p_->d_probs);
+    p_->d_probs = dalloc<float>(nq);
+    p_->probs_cap = nq;
+  }
+  ORX_CHECK(cudaMemcpyAsync(p_->d_pcm, pcm, np * 4, cudaMemcpyHostToDevice, s));
+  run_device(p_->d_pcm, steps, p_->d_probs, s);
+  ORX_CHECK(cudaMemcpyAsync(probs, p_->d_probs, nq * 4, cudaMemcpyDeviceToHost, s));
+  ORX_CHECK(cudaStreamSynchronize(s));
+}
+
+void BatchVad::init_synthetic(int seed) {
+  // N(0, gain^2 / fan_in) per tensor from the counter-hash generator (tensor
+  // ids 70000 + i), head bias 0.3: the same recipe as the CPU restatement.
+  const int fan[15] = {256, 387, 387, 384, 384, 192, 192, 192, 192, 128, 128, 128, 128, 128, 128};
+  for (int i = 0; i < 15; ++i) {
+    const std::string nm = kVadNames[i];
+    const double gain = nm.rfind("decoder.decoder", 0) == 0 ? 8.0
+                      : nm.rfind("decoder.rnn", 0) == 0 ? 2.0
+                      : nm.rfind("encoder", 0) == 0 ? 1.5 : 1.0;
+    const size_t n = kVadSizes[i];
+    float* tmp = dalloc<float>(n);
+    launch_synth_f32(tmp, static_cast<long long>(n), seed, 70000 + i, gain / std::sqrt((double)fan[i]),
+                     0.f, 0, nullptr);
+    std::vector<float> h(n);
+    ORX_CHECK(cudaMemcpy(h.data(), tmp, n * 4, cudaMemcpyDeviceToHost));
+    cudaFree(tmp);
+    if (i == 14) h[0] = 0.3f;
+    set_tensor(nm, h.data(), n);
+  }
+}
+
+}  // namespace orx
