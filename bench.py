@@ -412,6 +412,116 @@ def run_config1(torch, hbm, cpu: bool):
     return out
 
 
+VAD_MACS_PER_WINDOW = (4 * 258 * 256           # STFT (4 frames x 258 filters x 256)
+                       + 128 * 4 * 129 * 3       # enc0
+                       + 64 * 2 * 128 * 3        # enc1
+                       + 64 * 64 * 2             # enc2 (two taps see data)
+                       + 128 * 64                # enc3 (centre tap)
+                       + 512 * 256 + 128)        # LSTM gates + head
+
+
+def run_config5(torch, cpu: bool, ref_gpu: bool, reps: int = 3):
+    """Config 5: the Silero-shaped detector (seed 4) over 4096 streams x 100
+    steps of 512 (+64 context) samples, PCM U[-1, 1) on the device; one step
+    of the bench = the whole 409,600-window job (front end of every window,
+    then each stream's LSTM scan over its 100 steps). Device time with CUDA
+    events; e2e through the C ABI from pinned host PCM to host probabilities."""
+    from orator_b200.vad import BatchVad
+    S, steps = 4096, 100
+    g = torch.Generator(device="cuda").manual_seed(4)
+    pcm = torch.rand(S, steps * 512, device="cuda", generator=g) * 2 - 1
+    probs = torch.empty(S, steps, device="cuda")
+    v = BatchVad(S)
+    v.init_synthetic(4)
+    s = torch.cuda.current_stream()
+    for _ in range(2):
+        v.reset()
+        v.run_device(pcm.data_ptr(), steps, probs.data_ptr(), s)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(reps):
+        v.reset()
+        torch.cuda.synchronize()
+        e0.record(s)
+        v.run_device(pcm.data_ptr(), steps, probs.data_ptr(), s)
+        e1.record(s)
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ms = statistics.median(ts)
+    windows = S * steps
+    flops = 2.0 * VAD_MACS_PER_WINDOW * windows
+    peak = 148 * 128 * 2 * 1.965e9 / 1e12  # fp32 FMA issue rate, nominal (no measured fp32 peak)
+    host = torch.empty(S, steps * 512, pin_memory=True)
+    host.copy_(pcm)
+    hp = host.numpy()
+    v.reset()
+    v.run(hp)
+    t0 = time.perf_counter()
+    v.reset()
+    v.run(hp)
+    e2e_s = time.perf_counter() - t0
+    out = {"workload": "config5: Silero-shaped detector, 4096 streams x 100 steps (512 + 64 samples), "
+                       "fp32, seed 4, LSTM state carried across steps",
+           "value": windows / (ms * 1e-3), "unit": "windows/s", "ms_per_step": ms,
+           "tflops": flops / (ms * 1e-3) / 1e12, "roofline": {
+               "bound": "fp32 FMA (SIMT)", "achieved": flops / (ms * 1e-3) / 1e12,
+               "peak": peak, "peak_kind": "nominal 148 SM x 128 FMA/clk x 1.965 GHz",
+               "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / peak},
+           "e2e": {"value": windows / e2e_s, "unit": "windows/s",
+                   "h2d_bytes_per_step": S * steps * 512 * 4, "d2h_bytes_per_step": S * steps * 4}}
+    v.close()
+    if cpu:
+        from oracle import vad_oracle as V
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        Sc, kc = 256, 10
+        o = V.BatchVadOracle(V.synthetic_weights(4), Sc)
+        x = pcm[:Sc, :kc * 512].cpu().numpy()
+        t0 = time.perf_counter()
+        o.run(x, kc)
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": Sc * kc / dt, "unit": "windows/s", "cores": threads,
+                               "kind": "port", "sample": f"{Sc} streams x {kc} steps (numpy restatement)"}
+    if ref_gpu:
+        out["reference_gpu"] = vad_reference_gpu_rate(pcm)
+    return out
+
+
+def vad_reference_gpu_rate(pcm, streams: int = 16):
+    """The reference's own GpuVad (oracle/_ref) on this GPU: one stream at a
+    time, as it is built, for a sample of streams x all 100 steps (its
+    DebugWindowProbs: one batched pass over the stream's windows)."""
+    import ctypes as C
+    import shutil
+    lib_path = os.path.join(ROOT, "oracle", "_ref", "libref_asr.so")
+    if not os.path.exists(lib_path):
+        return {"unavailable": "oracle/_ref/libref_asr.so not built (oracle/build_ref.sh)"}
+    from oracle import vad_oracle as V
+    L = C.CDLL(lib_path)
+    L.ref_gpuvad_create.restype = C.c_void_p
+    L.ref_gpuvad_create.argtypes = [C.c_char_p]
+    d = tempfile.mkdtemp(prefix="ref_vad_")
+    try:
+        path = V.write_safetensors(os.path.join(d, "vad.safetensors"), V.synthetic_weights(4))
+        h = C.c_void_p(L.ref_gpuvad_create(path.encode()))
+        x = pcm[:streams].cpu().numpy()
+        steps = x.shape[1] // 512
+        out = np.zeros(steps, np.float32)
+        L.ref_gpuvad_probs(h, x[0].ctypes.data_as(C.c_void_p), C.c_int(x.shape[1]),
+                           out.ctypes.data_as(C.c_void_p))  # warm-up
+        t0 = time.perf_counter()
+        for s in range(streams):
+            L.ref_gpuvad_probs(h, x[s].ctypes.data_as(C.c_void_p), C.c_int(x.shape[1]),
+                               out.ctypes.data_as(C.c_void_p))
+        dt = time.perf_counter() - t0
+        L.ref_gpuvad_destroy(h)
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    return {"value": streams * steps / dt, "unit": "windows/s",
+            "sample": f"{streams} streams x {steps} steps, one stream per call (wall clock, "
+                      "each call synchronizes)"}
+
+
 def measure_prefill(dec, torch, prompt, s, reps=5):
     """Config 2's 400-row prefill from device-resident rows (tcgen05 GEMMs,
     flash prefill attention, last-row lm_head), device time per prefill, and
@@ -566,6 +676,9 @@ def run_ours(args):
         line["ragged_strong"] = ragged_strong
     if not args.no_config1:
         line["config1"] = run_config1(torch, hbm, cpu=world == 1 and not args.no_cpu_baseline)
+    if world == 1 and not args.no_config5:
+        line["config5"] = run_config5(torch, cpu=not args.no_cpu_baseline,
+                                      ref_gpu=not args.no_reference_gpu)
     if world == 1 and not args.no_cpu_baseline:
         rate, threads, _ = cpu_oracle_rate(args.cpu_sample)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -588,6 +701,7 @@ def main():
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own CUDA decoder (oracle/_ref)")
     ap.add_argument("--no-config1", action="store_true", help="skip the config-1 fp32 layer run")
+    ap.add_argument("--no-config5", action="store_true", help="skip the config-5 detector run")
     ap.add_argument("--ragged-steps", type=int, default=256,
                     help="decode steps of the config-3 runs (256 = the config; fewer for profiling)")
     ap.add_argument("--tokens", type=int, default=128,
