@@ -487,6 +487,154 @@ def run_config5(torch, cpu: bool, ref_gpu: bool, reps: int = 3):
     return out
 
 
+TOWER_FRAMES = 1000  # 10 s utterances (100 mel frames per second)
+
+
+def tower_flops(frames_list, layers: int = 24) -> float:
+    """Algorithmic FLOPs of one tower pass over the utterances (2 per MAC):
+    the three convolutions at the reference's padded chunk widths, conv_out,
+    the encoder layers (q, k, v, out, fc1, fc2 and full attention inside each
+    utterance) and proj1 / proj2; kept rows only past conv_out."""
+    co = lambda x: 0 if x <= 0 else (x - 1) // 2 + 1
+    ol = lambda n: co(co(co(n % 100))) + (n // 100) * 13
+    f = 0.0
+    for n in frames_list:
+        ch = (n + 99) // 100
+        mcl = min(n, 100)
+        w1, w2, w3 = co(mcl), co(co(mcl)), co(co(co(mcl)))
+        f += ch * 2.0 * (64 * w1 * 480 * 9 + 32 * w2 * 480 * 4320 + 16 * w3 * 480 * 4320)
+        f += ch * w3 * 2.0 * 7680 * 1024
+        r = ol(n)
+        f += layers * (2.0 * r * (4 * 1024 * 1024 + 2 * 1024 * 4096) + 4.0 * r * r * 1024)
+        f += 2.0 * r * (1024 * 1024 + 1024 * 2048)
+    return f
+
+
+def run_tower(torch, cpu: bool, ref_gpu: bool, utts: int = 64, reps: int = 3):
+    """The audio tower (24 layers, seed 5) over `utts` 10 s utterances of
+    N(0, 1) log-mel in one batched call (attention per utterance). Device
+    time with CUDA events; e2e from pinned host mel to host rows through the
+    C ABI's batched call, copies included."""
+    from orator_b200.tower import AudioTower, output_length
+    frames = [TOWER_FRAMES] * utts
+    rows = sum(output_length(n) for n in frames)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    mel = torch.randn(utts * 128 * TOWER_FRAMES, device="cuda", generator=g)
+    out = torch.empty(rows, 2048, device="cuda")
+    t = AudioTower(24)
+    t.init_synthetic(5)
+    s = torch.cuda.current_stream()
+    for _ in range(3):
+        t.forward_batch(mel.data_ptr(), frames, out.data_ptr(), s)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        e0.record(s)
+        t.forward_batch(mel.data_ptr(), frames, out.data_ptr(), s)
+        e1.record(s)
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ms = statistics.median(ts)
+    flops = tower_flops(frames)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, kind = float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        peak, kind = 1590.0, "fallback"
+    tf = flops / (ms * 1e-3) / 1e12
+    audio_s = utts * TOWER_FRAMES / 100.0
+    hm = torch.empty(mel.numel(), pin_memory=True)
+    hm.copy_(mel)
+    ho = torch.empty(rows, 2048, pin_memory=True)
+    e2e = []
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        mel.copy_(hm, non_blocking=True)
+        t.forward_batch(mel.data_ptr(), frames, out.data_ptr(), s)
+        ho.copy_(out, non_blocking=True)
+        torch.cuda.synchronize()
+        e2e.append(time.perf_counter() - t0)
+    e2e_s = statistics.median(e2e)
+    res = {"workload": f"audio tower: 24 layers (d 1024, 16 heads, ffn 4096) + conv front end, "
+                       f"{utts} utterances x {TOWER_FRAMES} mel frames (10 s) in one batched call, "
+                       "bf16 GEMMs / fp32 elsewhere, seed 5",
+           "value": audio_s / (ms * 1e-3), "unit": "audio seconds/s", "ms_per_step": ms,
+           "rows_per_s": rows / (ms * 1e-3),
+           "roofline": {"bound": "tensor", "achieved": tf, "peak": peak,
+                        "peak_kind": f"{kind} cuBLAS bf16 burst", "unit": "TFLOP/s",
+                        "frac": tf / peak, "flops_per_step": flops,
+                        "note": "whole pass (all kernels) against the GEMM peak"},
+           "e2e": {"value": audio_s / e2e_s, "unit": "audio seconds/s",
+                   "h2d_bytes_per_step": mel.numel() * 4, "d2h_bytes_per_step": rows * 2048 * 4}}
+    t.close()
+    if cpu or ref_gpu:
+        from oracle import tower_oracle as TO
+        from orator_b200 import synth_f32
+
+        def gpu_normal(seed, tid, n, std, mean):
+            buf = torch.empty(n, dtype=torch.float32, device="cuda")
+            synth_f32(buf.data_ptr(), n, seed, tid, std, mean, False)
+            return buf.cpu().numpy()
+        w = TO.synthetic_weights(24, normal=gpu_normal)
+        sample = mel[:128 * TOWER_FRAMES].view(128, TOWER_FRAMES).cpu().numpy()
+        if cpu:
+            threads = os.cpu_count() or 1
+            torch.set_num_threads(threads)
+            o = TO.TowerOracle(w, 24)
+            k = 2
+            t0 = time.perf_counter()
+            for _ in range(k):
+                o.forward(sample)
+            dt = time.perf_counter() - t0
+            res["cpu_baseline"] = {"value": k * TOWER_FRAMES / 100.0 / dt, "unit": "audio seconds/s",
+                                   "cores": threads, "kind": "port",
+                                   "sample": f"{k} x one 10 s utterance (torch fp32 restatement)"}
+        if ref_gpu:
+            res["reference_gpu"] = tower_reference_gpu_rate(w, sample)
+            if "value" in res["reference_gpu"]:
+                res["reference_gpu"]["ours_over_reference"] = res["value"] / res["reference_gpu"]["value"]
+    return res
+
+
+def tower_reference_gpu_rate(weights, mel, utts: int = 8):
+    """The reference's own AsrAudioTower (oracle/_ref) on this GPU through its
+    public host-to-host Forward, one 10 s utterance per call as it is built."""
+    lib_path = os.path.join(ROOT, "oracle", "_ref", "libref_asr.so")
+    if not os.path.exists(lib_path):
+        return {"unavailable": "oracle/_ref/libref_asr.so not built (oracle/build_ref.sh)"}
+    import ctypes as C
+    import shutil
+    from oracle import tower_oracle as TO
+    d = tempfile.mkdtemp(prefix="ref_tower_")
+    try:
+        TO.write_checkpoint(d, weights, 24)
+        L = C.CDLL(lib_path)
+        L.ref_tower_create.restype = C.c_void_p
+        L.ref_tower_create.argtypes = [C.c_char_p, C.c_int, C.c_int]
+        L.ref_tower_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+        L.ref_tower_destroy.argtypes = [C.c_void_p]
+        h = C.c_void_p(L.ref_tower_create(d.encode(), 24, 0))
+        if not h:
+            return {"unavailable": "reference tower failed to load"}
+        n = mel.shape[1]
+        x = np.ascontiguousarray(mel, np.float32)
+        out = np.empty((TO.output_length(n), 2048), np.float32)
+        for _ in range(2):
+            L.ref_tower_forward(h, x.ctypes.data_as(C.c_void_p), C.c_int(n), out.ctypes.data_as(C.c_void_p))
+        t0 = time.perf_counter()
+        for _ in range(utts):
+            L.ref_tower_forward(h, x.ctypes.data_as(C.c_void_p), C.c_int(n), out.ctypes.data_as(C.c_void_p))
+        dt = time.perf_counter() - t0
+        L.ref_tower_destroy(h)
+        return {"value": utts * n / 100.0 / dt, "unit": "audio seconds/s",
+                "sample": f"{utts} calls of AsrAudioTower::Forward on one 10 s utterance "
+                          "(host mel in, host rows out)"}
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+
+
 def vad_reference_gpu_rate(pcm, streams: int = 16):
     """The reference's own GpuVad (oracle/_ref) on this GPU: one stream at a
     time, as it is built, for a sample of streams x all 100 steps (its
@@ -679,6 +827,9 @@ def run_ours(args):
     if world == 1 and not args.no_config5:
         line["config5"] = run_config5(torch, cpu=not args.no_cpu_baseline,
                                       ref_gpu=not args.no_reference_gpu)
+    if world == 1 and not args.no_tower:
+        line["tower"] = run_tower(torch, cpu=not args.no_cpu_baseline,
+                                  ref_gpu=not args.no_reference_gpu)
     if world == 1 and not args.no_cpu_baseline:
         rate, threads, _ = cpu_oracle_rate(args.cpu_sample)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -702,6 +853,9 @@ def main():
                     help="skip timing the reference's own CUDA decoder (oracle/_ref)")
     ap.add_argument("--no-config1", action="store_true", help="skip the config-1 fp32 layer run")
     ap.add_argument("--no-config5", action="store_true", help="skip the config-5 detector run")
+    ap.add_argument("--no-tower", action="store_true", help="skip the audio tower run")
+    ap.add_argument("--tower-only", type=int, default=0, metavar="UTTS",
+                    help="run only the audio tower leg over UTTS utterances (profiling)")
     ap.add_argument("--ragged-steps", type=int, default=256,
                     help="decode steps of the config-3 runs (256 = the config; fewer for profiling)")
     ap.add_argument("--tokens", type=int, default=128,
@@ -711,6 +865,10 @@ def main():
     NEW_TOKENS = args.tokens
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.tower_only:
+        import torch
+        print(json.dumps(run_tower(torch, cpu=False, ref_gpu=False, utts=args.tower_only)), flush=True)
         return
     try:
         run_ours(args)

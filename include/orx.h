@@ -264,6 +264,41 @@ int orx_vad_reset(orx_vad* v);
 int orx_vad_run(orx_vad* v, const float* pcm, int steps, float* probs, int on_device,
                 void* stream);
 
+/* ---- Audio tower (the Qwen3-ASR encoder that produces the decoder's audio
+ * rows; AsrAudioTower, include/model/asr_audio_tower.h:52-128), batched over
+ * utterances. ---- */
+typedef struct orx_tower orx_tower;
+/* AsrAudioTower::AsrAudioTower (asr_audio_tower.h:54) with
+ * AsrAudioConfig::encoder_layers = `layers` and windowed_attention =
+ * `windowed` (other fields at their defaults: 128 mel bins, d_model 1024,
+ * 16 heads, ffn 4096, downsample 480, output 2048, 100-frame chunks). */
+int orx_tower_create(int layers, int windowed, orx_tower** out);
+void orx_tower_destroy(orx_tower* t);
+/* One host tensor by checkpoint name (thinker.audio_tower.*); dtype 0 = fp32,
+ * 1 = bf16 bits. Matrices are held in bf16, vectors in fp32 (as
+ * AsrAudioTower::LoadWeights, asr_audio_tower.cu:318-361). */
+int orx_tower_set_tensor(orx_tower* t, const char* name, const void* data, int dtype,
+                         size_t numel);
+/* AsrAudioTower::LoadWeights(ShardedSafeTensors) from a model directory. */
+int orx_tower_load_safetensors(orx_tower* t, const char* dir);
+/* Seeded synthetic weights (no reference counterpart; test and bench data). */
+int orx_tower_init_synthetic(orx_tower* t, int seed);
+int orx_tower_weights_complete(const orx_tower* t, int* complete);
+/* AsrAudioTower::OutputLength (asr_audio_tower.cu:279-283). */
+int orx_tower_output_length(int n_frames);
+/* AsrAudioTower::Forward (asr_audio_tower.h:77-78): mel [128, n_frames] fp32
+ * (host) -> out [OutputLength(n_frames), 2048] fp32 (host); *out_tokens gets
+ * the row count. Synchronous on `stream`. */
+int orx_tower_forward(orx_tower* t, const float* mel, int n_frames, float* out, int* out_tokens,
+                      void* stream);
+/* Many utterances in one call (no reference counterpart: the batched form).
+ * d_mel: the n utterances' [128, frames[u]] blocks back to back (device);
+ * frames: host array; d_out: [sum OutputLength(frames[u]), 2048] (device),
+ * utterance u's rows after those of u - 1. Attention never crosses
+ * utterances. Asynchronous on `stream`; *out_rows gets the total rows. */
+int orx_tower_forward_batch(orx_tower* t, const float* d_mel, const int* frames, int n,
+                            float* d_out, int* out_rows, void* stream);
+
 /* Seeded synthetic fp32 data on the device, bit-exact with oracle/synth.py
  * (test and benchmark inputs; no reference counterpart). */
 int orx_synth_f32(float* d_out, long long n, int seed, int tensor_id, double std, float mean,

@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include "io/sharded_safetensor.h"
+#include "model/asr_audio_tower.h"
 #include "model/asr_gemm.h"
 #include "model/asr_ops.cuh"
 #include "model/asr_text_decoder.h"
@@ -187,6 +188,44 @@ int ref_op_linear(const float* in, const uint16_t* w, const float* bias, float* 
 int ref_op_linear_pre(const uint16_t* in, const uint16_t* w, const float* bias, float* out, int M,
                       int K, int N, int act) {
   REF_OP(gm::LinearPre(in, w, bias, out, M, K, N, act))
+}
+
+// ---- the reference's audio tower (src/model/asr_audio_tower.cu) ----
+struct RefTower {
+  std::unique_ptr<orator::io::ShardedSafeTensors> w;
+  std::unique_ptr<orator::model::AsrAudioTower> t;
+};
+void* ref_tower_create(const char* model_dir, int layers, int windowed) {
+  try {
+    auto* h = new RefTower;
+    orator::model::AsrAudioConfig c;
+    c.encoder_layers = layers;
+    c.windowed_attention = windowed != 0;
+    h->w = std::make_unique<orator::io::ShardedSafeTensors>(model_dir);
+    h->t = std::make_unique<orator::model::AsrAudioTower>(c);
+    h->t->LoadWeights(*h->w);
+    return h;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return nullptr;
+  }
+}
+void ref_tower_destroy(void* h) { delete static_cast<RefTower*>(h); }
+// mel [128, n_frames] (host) -> out [N, 2048] (host, room for
+// OutputLength(n_frames) rows); returns N, or -1.
+int ref_tower_forward(void* h, const float* mel, int n_frames, float* out) {
+  try {
+    int n = 0;
+    auto v = static_cast<RefTower*>(h)->t->Forward(mel, n_frames, &n);
+    std::memcpy(out, v.data(), v.size() * sizeof(float));
+    return n;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return -1;
+  }
+}
+int ref_tower_output_length(int n_frames) {
+  return orator::model::AsrAudioTower::OutputLength(n_frames);
 }
 
 // ---- the reference's GPU speech detector (src/pipeline/gpu_vad.cu) ----

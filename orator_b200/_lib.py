@@ -120,6 +120,17 @@ _SIGS = {
     "orx_vad_init_synthetic": (C.c_int, [C.c_void_p, C.c_int]),
     "orx_vad_reset": (C.c_int, [C.c_void_p]),
     "orx_vad_run": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]),
+    "orx_tower_create": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "orx_tower_destroy": (None, [C.c_void_p]),
+    "orx_tower_set_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_int, C.c_size_t]),
+    "orx_tower_load_safetensors": (C.c_int, [C.c_void_p, C.c_char_p]),
+    "orx_tower_init_synthetic": (C.c_int, [C.c_void_p, C.c_int]),
+    "orx_tower_weights_complete": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "orx_tower_output_length": (C.c_int, [C.c_int]),
+    "orx_tower_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                    C.POINTER(C.c_int), C.c_void_p]),
+    "orx_tower_forward_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                          C.c_void_p, C.POINTER(C.c_int), C.c_void_p]),
     "orx_synth_f32": (C.c_int, [C.c_void_p, C.c_longlong, C.c_int, C.c_int, C.c_double,
                                 C.c_float, C.c_int, C.c_void_p]),
 }

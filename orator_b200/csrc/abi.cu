@@ -27,6 +27,11 @@ struct orx_vad {
   int device = 0;
 };
 
+struct orx_tower {
+  orx::AudioTower* t = nullptr;
+  int device = 0;
+};
+
 struct orx_batch {
   orx::BatchDecoder* b = nullptr;
   int device = 0;
@@ -784,6 +789,114 @@ int orx_synth_f32(float* d_out, long long n, int seed, int tid, double std, floa
     if (n <= 0) return;
     orx::launch_synth_f32(d_out, n, seed, tid, std, mean, round_bf16, S(stream));
     orx::check(cudaGetLastError(), "synth");
+  });
+}
+
+int orx_tower_create(int layers, int windowed, orx_tower** out) {
+  return guard([&] {
+    need(out, "out");
+    *out = nullptr;
+    auto* h = new orx_tower;
+    try {
+      orx::check(cudaGetDevice(&h->device), "cudaGetDevice");
+      h->t = new orx::AudioTower(layers, windowed != 0);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+void orx_tower_destroy(orx_tower* t) {
+  if (!t) return;
+  DeviceScope ds(t->device);
+  delete t->t;
+  delete t;
+}
+
+int orx_tower_set_tensor(orx_tower* t, const char* name, const void* data, int dtype,
+                         size_t numel) {
+  return guard([&] {
+    need(t, "tower");
+    need(name, "name");
+    need(data, "data");
+    DeviceScope ds(t->device);
+    t->t->set_tensor(name, data, dtype, numel);
+  });
+}
+
+int orx_tower_load_safetensors(orx_tower* t, const char* dir) {
+  return guard([&] {
+    need(t, "tower");
+    need(dir, "model_dir");
+    DeviceScope ds(t->device);
+    orx::ShardedCheckpoint ck(dir);
+    for (const auto& kv : ck.tensors()) {
+      if (kv.first.rfind("thinker.audio_tower.", 0) != 0) continue;
+      const auto& v = kv.second;
+      int dtype;
+      size_t es;
+      if (v.dtype == "BF16") { dtype = 1; es = 2; }
+      else if (v.dtype == "F32") { dtype = 0; es = 4; }
+      else throw std::invalid_argument("unsupported dtype " + v.dtype + " for " + kv.first);
+      // layers beyond the configured count are not part of this tower
+      try {
+        t->t->set_tensor(kv.first, v.data, dtype, v.nbytes / es);
+      } catch (const std::invalid_argument& e) {
+        if (std::string(e.what()).rfind("unknown audio tower tensor", 0) != 0) throw;
+      }
+    }
+    if (!t->t->complete()) throw std::invalid_argument("checkpoint is missing audio tower tensors");
+  });
+}
+
+int orx_tower_init_synthetic(orx_tower* t, int seed) {
+  return guard([&] {
+    need(t, "tower");
+    DeviceScope ds(t->device);
+    t->t->init_synthetic(seed);
+  });
+}
+
+int orx_tower_weights_complete(const orx_tower* t, int* complete) {
+  return guard([&] {
+    need(t, "tower");
+    need(complete, "complete");
+    *complete = t->t->complete() ? 1 : 0;
+  });
+}
+
+int orx_tower_output_length(int n_frames) { return orx::AudioTower::output_length(n_frames); }
+
+int orx_tower_forward(orx_tower* t, const float* mel, int n_frames, float* out, int* out_tokens,
+                      void* stream) {
+  return guard([&] {
+    need(t, "tower");
+    if (n_frames < 0) throw std::invalid_argument("n_frames must be >= 0");
+    if (out_tokens) *out_tokens = 0;
+    if (n_frames == 0) return;
+    need(mel, "mel");
+    need(out, "out");
+    DeviceScope ds(t->device);
+    const int n = t->t->forward_host(mel, n_frames, out, S(stream));
+    if (out_tokens) *out_tokens = n;
+  });
+}
+
+int orx_tower_forward_batch(orx_tower* t, const float* d_mel, const int* frames, int n,
+                            float* d_out, int* out_rows, void* stream) {
+  return guard([&] {
+    need(t, "tower");
+    if (n < 0) throw std::invalid_argument("negative utterance count");
+    if (out_rows) *out_rows = 0;
+    if (n == 0) return;
+    need(frames, "frames");
+    need(d_mel, "mel");
+    need(d_out, "out");
+    DeviceScope ds(t->device);
+    const int rows = t->t->forward_device(d_mel, frames, n, d_out, S(stream));
+    if (out_rows) *out_rows = rows;
   });
 }
 

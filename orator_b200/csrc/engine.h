@@ -288,6 +288,33 @@ class BatchVad {
   Impl* p_;
 };
 
+// Qwen3-ASR audio tower (tower.cu), batched over utterances: mel
+// [128, frames] of each utterance -> [OutputLength(frames), 2048] rows.
+class AudioTower {
+ public:
+  AudioTower(int layers, bool windowed);
+  ~AudioTower();
+  AudioTower(const AudioTower&) = delete;
+  AudioTower& operator=(const AudioTower&) = delete;
+  int layers() const;
+  // By checkpoint name (thinker.audio_tower.*); dtype 0 fp32, 1 bf16 bits (host).
+  void set_tensor(const std::string& name, const void* data, int dtype, size_t numel);
+  void init_synthetic(int seed);
+  bool complete() const;
+  // d_mel: the utterances' [128, frames[u]] blocks back to back (device);
+  // d_out: [sum of OutputLength(frames[u]), 2048] (device). Returns the rows.
+  int forward_device(const float* d_mel, const int* frames, int n_utt, float* d_out,
+                     cudaStream_t s);
+  // One utterance from / to host memory (AsrAudioTower::Forward).
+  int forward_host(const float* mel, int n_frames, float* out, cudaStream_t s);
+  int device_error() const;
+  static int output_length(int frames);
+
+ private:
+  struct Impl;
+  Impl* p_;
+};
+
 // fp32 single decoder layer (layer32.cu): fp32 weights, activations and KV.
 struct Layer32;
 Layer32* layer32_create(int max_seq_len, float eps, float theta);

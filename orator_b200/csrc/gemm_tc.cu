@@ -276,7 +276,12 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
                 y = 0.5f * y * (1.0f + erff(y * 0.70710678118654752440f));
               else if (g.act == 2)
                 y = fmaxf(y, 0.0f);
-              if (c0 + i < BN && t < g.T) g.out_f32[(long long)t * g.ldo + row] = y;
+              if (c0 + i < BN && t < g.T) {
+                const long long o = (long long)t * g.ldo + row;
+                if (g.out_bf16) g.out_bf16[o] = f2bf(y);
+                else if (g.resid) g.out_f32[o] += y;
+                else g.out_f32[o] = y;
+              }
             }
           }
         } else {
@@ -459,7 +464,13 @@ bool make_tmap_2d(void* map, const void* base, long long rows, int cols, int box
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
                     cudaStream_t s) {
   if (g.T <= 0) return;
-  const int bn = g.T <= 16 ? 16 : g.T <= 32 ? 32 : g.T <= 64 ? 64 : g.T <= 128 ? 128 : 256;
+  int bn = g.T <= 16 ? 16 : g.T <= 32 ? 32 : g.T <= 64 ? 64 : g.T <= 128 ? 128 : 256;
+  if (g.epi == kEpiLinear && splits == 1) {
+    // No split-K here: narrower token tiles until the tiles cover most SMs
+    // (the weight tile is then re-read from L2 by more CTAs).
+    const int mt = (g.N + 127) / 128;
+    while (bn > 32 && mt * ((g.T + bn - 1) / bn) < 111) bn >>= 1;
+  }
   CUtensorMap mw, mx;
   if (!make_map(&mw, W, g.N, g.K, 128) || !make_map(&mx, X, g.T, g.K, bn)) {
     fprintf(stderr, "orx: tensor map encoding failed\n");

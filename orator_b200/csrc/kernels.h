@@ -139,9 +139,12 @@ struct TcArgs {
   const float* norm_w;
   uint16_t* norm_out;
   float eps;
-  // kEpiLinear: out = act(acc + bias[n]); act 0 none, 1 GELU (erf), 2 ReLU.
+  // kEpiLinear: y = act(acc + bias[n]); act 0 none, 1 GELU (erf), 2 ReLU.
+  // The row goes to out_bf16 (rounded) when it is set, else it is stored
+  // into out_f32, or added to it when `resid` is set.
   const float* bias;
   int act;
+  int resid;
 };
 // X: [T, K] bf16 row-major (device), W: [N, K] bf16. splits divides K / 64.
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,

@@ -1,0 +1,722 @@
+// Qwen3-ASR audio tower (the encoder that produces the decoder's audio rows)
+// on B200, batched over utterances.
+//
+// Replaces AsrAudioTower (include/model/asr_audio_tower.h:52-128,
+// src/model/asr_audio_tower.cu:362-631). Same arithmetic contract: every
+// projection rounds its fp32 input to bf16 and multiplies bf16 weights with
+// fp32 accumulation, then adds the fp32 bias and applies exact GELU; the
+// convolutions see bf16-rounded inputs; LayerNorm (eps 1e-5), softmax and
+// the residual stream stay fp32.
+//
+// Layout, chosen for the tcgen05 GEMM (gemm_tc.cu) rather than the
+// reference's NCHW + rearrange passes:
+// * every chunk is a full 100-frame tile. The reference pads an utterance's
+//   chunks to its longest one (100 frames, or the whole utterance when it is
+//   shorter), so each conv input is zero past that padded width: the chunk
+//   carries the widths (w1, w2) of its utterance and the im2col reads zeros
+//   beyond them, which reproduces the rows the reference keeps;
+// * conv1 (K = 9) is a direct kernel; its output is channel-last bf16
+//   [chunk][64][50][480], so conv2 / conv3 im2col rows are nine contiguous
+//   960-byte runs (weights permuted to (kh, kw, ci) columns once at load);
+// * conv2 / conv3 are tcgen05 GEMMs with the bias + GELU + bf16 rounding in
+//   the epilogue, writing channel-last rows directly; conv3's rows are
+//   ordered (chunk, t, f), so its output IS the conv_out input
+//   [chunk * 13][16 * 480] (conv_out weight columns permuted to (f, co));
+// * q / k / v are one GEMM over concatenated weights; out_proj and fc2 add
+//   into the fp32 residual in their epilogue; fc1 / proj1 write bf16 GELU
+//   rows that the next GEMM reads as is.
+// Many utterances go through one call: their chunks share the conv and
+// projection GEMMs, and attention stays inside each utterance (or inside
+// each 104-row window of it when windowed attention is on).
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "engine.h"
+#include "kernels.h"
+
+namespace orx {
+namespace {
+
+constexpr int kF = 128, kD = 1024, kHeads = 16, kDh = 64, kFfn = 4096, kDs = 480, kOut = 2048;
+constexpr int kWin = 100;                 // mel frames per chunk
+constexpr int kH1 = 64, kW1 = 50;         // conv1 output (freq, time)
+constexpr int kH2 = 32, kW2 = 25;         // conv2 output
+constexpr int kH3 = 16, kWc = 13;         // conv3 output
+constexpr int kTaps = 9 * kDs;            // im2col depth of conv2 / conv3
+constexpr int kCf = kH3 * kDs;            // conv_out depth (7680)
+constexpr int kVec = kDs / 8;             // 16-byte vectors per 480-channel run
+constexpr int kSlab = 64;                 // chunks per pass of the conv front end
+constexpr int kWindowRows = 104;          // windowed attention: 13 rows x 8 chunks
+constexpr float kEps = 1e-5f;
+
+__device__ __forceinline__ float gelu(float y) {
+  return 0.5f * y * (1.0f + erff(y * 0.70710678118654752440f));
+}
+
+struct ChunkInfo {
+  long long mel_off;  // first float of the utterance's [128, frames] mel
+  int frames;         // the utterance's frame count (row stride of its mel)
+  int t0;             // first frame of the chunk
+  int len;            // frames in the chunk (1..100)
+  int w1, w2;         // conv1 / conv2 output widths of the utterance's padded chunk
+  int pad;
+};
+
+// conv1 (1 -> 480, 3x3, stride 2, pad 1) + bias + GELU, one CTA per
+// (chunk, output frequency row); output channel-last bf16.
+__global__ void __launch_bounds__(256) tower_conv1_kernel(const float* __restrict__ mel,
+                                                          const ChunkInfo* __restrict__ chunks,
+                                                          const float* __restrict__ w,
+                                                          const float* __restrict__ b,
+                                                          uint16_t* __restrict__ out) {
+  __shared__ float xs[3][kWin + 2];
+  __shared__ float ws[kDs * 9];
+  __shared__ float bs[kDs];
+  const int c = blockIdx.x / kH1, ho = blockIdx.x - c * kH1;
+  const ChunkInfo ci = chunks[c];
+  for (int i = threadIdx.x; i < kDs * 9; i += blockDim.x) ws[i] = w[i];
+  for (int i = threadIdx.x; i < kDs; i += blockDim.x) bs[i] = b[i];
+  for (int i = threadIdx.x; i < 3 * (kWin + 2); i += blockDim.x) {
+    const int kh = i / (kWin + 2), wi = i - kh * (kWin + 2) - 1;
+    const int hi = 2 * ho - 1 + kh;
+    float v = 0.f;
+    if (hi >= 0 && hi < kF && wi >= 0 && wi < ci.len)
+      v = bf2f(f2bf(mel[ci.mel_off + static_cast<long long>(hi) * ci.frames + ci.t0 + wi]));
+    xs[kh][wi + 1] = v;
+  }
+  __syncthreads();
+  uint16_t* o = out + static_cast<long long>(blockIdx.x) * kW1 * kDs;
+  for (int idx = threadIdx.x; idx < kW1 * kDs; idx += blockDim.x) {
+    const int wo = idx / kDs, co = idx - wo * kDs;
+    const float* wr = ws + co * 9;
+    float acc = 0.f;
+#pragma unroll
+    for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+      for (int kw = 0; kw < 3; ++kw) acc = fmaf(xs[kh][2 * wo + kw], wr[kh * 3 + kw], acc);
+    o[idx] = f2bf(gelu(acc + bs[co]));
+  }
+}
+
+// im2col of a stride-2 pad-1 3x3 conv over channel-last bf16 input
+// [chunk][Hi][Wi][480]: row r holds taps (kh, kw) x 480 channels. Rows run
+// (chunk, ho, wo) (wo_major == 0, conv2, input width w1) or (chunk, wo, ho)
+// (wo_major == 1, conv3, input width w2). One thread per 16-byte vector.
+__global__ void __launch_bounds__(256) tower_im2col_kernel(const uint4* __restrict__ src,
+                                                           uint4* __restrict__ col,
+                                                           const ChunkInfo* __restrict__ chunks,
+                                                           long long rows, int Hi, int Wi, int Ho,
+                                                           int Wo, int wo_major) {
+  const long long total = rows * (9 * kVec);
+  const int per_chunk = Ho * Wo;
+  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < total;
+       v += (long long)gridDim.x * blockDim.x) {
+    const long long r = v / (9 * kVec);
+    const int q = static_cast<int>(v - r * (9 * kVec));
+    const int tap = q / kVec, cv = q - tap * kVec;
+    const int kh = tap / 3, kw = tap - kh * 3;
+    const long long c = r / per_chunk;
+    const int rem = static_cast<int>(r - c * per_chunk);
+    const int ho = wo_major ? rem % Ho : rem / Wo;
+    const int wo = wo_major ? rem / Ho : rem % Wo;
+    const int hi = 2 * ho - 1 + kh, wi = 2 * wo - 1 + kw;
+    const int wv = wo_major ? chunks[c].w2 : chunks[c].w1;  // the utterance's padded width
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (hi >= 0 && hi < Hi && wi >= 0 && wi < Wi && wi < wv)
+      val = src[((c * Hi + hi) * Wi + wi) * kVec + cv];
+    col[v] = val;
+  }
+}
+
+// hid[r] = h[src_row[r]] + pe[src_row[r] % 13]: drops each chunk's padded
+// rows and adds the sinusoidal position of the row inside its chunk.
+__global__ void __launch_bounds__(256) tower_gather_pe_kernel(const float4* __restrict__ h,
+                                                              const int* __restrict__ src_row,
+                                                              const float4* __restrict__ pe,
+                                                              float4* __restrict__ hid, int n) {
+  const long long total = static_cast<long long>(n) * (kD / 4);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int r = static_cast<int>(i / (kD / 4)), c4 = static_cast<int>(i % (kD / 4));
+    const int s = src_row[r];
+    const float4 a = h[static_cast<long long>(s) * (kD / 4) + c4];
+    const float4 p = pe[(s % kWc) * (kD / 4) + c4];
+    hid[i] = make_float4(a.x + p.x, a.y + p.y, a.z + p.z, a.w + p.w);
+  }
+}
+
+// LayerNorm of 1024-wide fp32 rows to bf16, one warp per row (two-pass mean
+// and variance in registers).
+__global__ void __launch_bounds__(256) tower_layernorm_kernel(const float* __restrict__ x,
+                                                              const float* __restrict__ g,
+                                                              const float* __restrict__ b,
+                                                              uint16_t* __restrict__ out, int n) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  if (r >= n) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(r) * kD);
+  float4 v[8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[i] = xr[lane + 32 * i];
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  const float mean = warp_sum(s) / kD;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    ss += (a * a + bb * bb) + (c * c + d * d);
+  }
+  const float inv = rsqrtf(warp_sum(ss) / kD + kEps);
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  uint2* o = reinterpret_cast<uint2*>(out + static_cast<long long>(r) * kD);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int j = lane + 32 * i;
+    const float4 gg = g4[j], bv = b4[j];
+    const float y0 = (v[i].x - mean) * inv * gg.x + bv.x;
+    const float y1 = (v[i].y - mean) * inv * gg.y + bv.y;
+    const float y2 = (v[i].z - mean) * inv * gg.z + bv.z;
+    const float y3 = (v[i].w - mean) * inv * gg.w + bv.w;
+    o[j] = make_uint2(pack_bf16(y0, y1), pack_bf16(y2, y3));
+  }
+}
+
+// Bidirectional attention inside segments. qkv [n][3072] fp32 (q | k | v,
+// 16 heads of 64 each); out [n][1024] bf16. A CTA serves one head and up to
+// 16 consecutive query rows of one segment (a warp per row); keys stream
+// through shared memory in tiles of 32 shared by all 16 warps. Lane j scores
+// key j of the tile; lanes own output dims lane and lane + 32.
+struct AttnTile {
+  int row0, nrows, seg0, seg1;
+};
+constexpr int kAttnRows = 16, kAttnKeys = 32;
+
+__global__ void __launch_bounds__(kAttnRows * 32) tower_attn_kernel(
+    const float* __restrict__ qkv, const AttnTile* __restrict__ tiles, uint16_t* __restrict__ out,
+    float scale) {
+  __shared__ float sq[kAttnRows][kDh];
+  __shared__ float sk[kAttnKeys][kDh + 1];
+  __shared__ float sv[kAttnKeys][kDh];
+  const AttnTile t = tiles[blockIdx.x];
+  const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool active = warp < t.nrows;
+  const int row = t.row0 + warp;
+  if (active) {
+    const float* qr = qkv + static_cast<long long>(row) * (3 * kD) + h * kDh;
+    sq[warp][lane] = qr[lane];
+    sq[warp][lane + 32] = qr[lane + 32];
+  }
+  float m = -1e30f, l = 0.f, a0 = 0.f, a1 = 0.f;
+  for (int j0 = t.seg0; j0 < t.seg1; j0 += kAttnKeys) {
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < kAttnKeys * kDh; idx += blockDim.x) {
+      const int jj = idx / kDh, d = idx - jj * kDh, j = j0 + jj;
+      const bool ok = j < t.seg1;
+      const float* base = qkv + static_cast<long long>(j) * (3 * kD) + h * kDh + d;
+      sk[jj][d] = ok ? base[kD] : 0.f;
+      sv[jj][d] = ok ? base[2 * kD] : 0.f;
+    }
+    __syncthreads();
+    if (!active) continue;
+    float s = 0.f;
+#pragma unroll 16
+    for (int d = 0; d < kDh; ++d) s = fmaf(sq[warp][d], sk[lane][d], s);
+    const bool valid = j0 + lane < t.seg1;
+    s = valid ? s * scale : -INFINITY;
+    const float mn = fmaxf(m, warp_max(s));
+    const float corr = expf(m - mn);
+    const float p = valid ? expf(s - mn) : 0.f;
+    l = l * corr + warp_sum(p);
+    a0 *= corr;
+    a1 *= corr;
+    const int nj = min(kAttnKeys, t.seg1 - j0);
+    for (int jj = 0; jj < nj; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, p, jj);
+      a0 = fmaf(pj, sv[jj][lane], a0);
+      a1 = fmaf(pj, sv[jj][lane + 32], a1);
+    }
+    m = mn;
+  }
+  if (!active) return;
+  const float invl = l > 0.f ? 1.0f / l : 0.f;
+  uint16_t* o = out + static_cast<long long>(row) * kD + h * kDh;
+  o[lane] = f2bf(a0 * invl);
+  o[lane + 32] = f2bf(a1 * invl);
+}
+
+// Weight re-layouts applied once at load (host side).
+void permute_conv(const uint16_t* src, uint16_t* dst) {  // [co][ci][9] -> [co][9][ci]
+  for (int co = 0; co < kDs; ++co)
+    for (int ci = 0; ci < kDs; ++ci)
+      for (int tap = 0; tap < 9; ++tap)
+        dst[(static_cast<size_t>(co) * 9 + tap) * kDs + ci] =
+            src[(static_cast<size_t>(co) * kDs + ci) * 9 + tap];
+}
+void permute_conv_out(const uint16_t* src, uint16_t* dst) {  // [d][co*16+f] -> [d][f*480+co]
+  for (int d = 0; d < kD; ++d)
+    for (int co = 0; co < kDs; ++co)
+      for (int f = 0; f < kH3; ++f)
+        dst[static_cast<size_t>(d) * kCf + f * kDs + co] =
+            src[static_cast<size_t>(d) * kCf + co * kH3 + f];
+}
+
+uint16_t host_f2bf(float f) {  // round to nearest even (finite values)
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>(u >> 16);
+}
+float host_bf2f(uint16_t b) {
+  const uint32_t u = static_cast<uint32_t>(b) << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+int grid_for_n(long long n) {
+  const long long b = (n + 255) / 256;
+  return static_cast<int>(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
+}
+
+}  // namespace
+
+int AudioTower::output_length(int frames) {
+  auto co = [](int x) { return x <= 0 ? 0 : (x - 1) / 2 + 1; };
+  return co(co(co(frames % 100))) + (frames / 100) * 13;
+}
+
+struct AudioTower::Impl {
+  enum Kind { kVecF32, kMatBf16, kConvPerm, kConvOutPerm, kConv1 };
+  struct Entry {
+    std::string name;
+    Kind kind;
+    void* dst;
+    size_t numel;
+    size_t fan_in;  // synthetic init scale (0 for vectors)
+    int norm_gain;  // LayerNorm gain: synthetic mean 1
+  };
+  int layers = 0;
+  bool windowed = false;
+  int* err = nullptr;
+  // weights
+  float *conv1_w = nullptr, *conv1_b = nullptr, *conv2_b = nullptr, *conv3_b = nullptr;
+  uint16_t *conv2_w = nullptr, *conv3_w = nullptr, *conv_out_w = nullptr;
+  float *ln_post_g = nullptr, *ln_post_b = nullptr, *proj1_b = nullptr, *proj2_b = nullptr;
+  uint16_t *proj1_w = nullptr, *proj2_w = nullptr;
+  struct Layer {
+    float *ln1_g, *ln1_b, *qkv_b, *o_b, *ln2_g, *ln2_b, *fc1_b, *fc2_b;
+    uint16_t *qkv_w, *o_w, *fc1_w, *fc2_w;
+  };
+  std::vector<Layer> L;
+  std::vector<Entry> entries;
+  std::vector<bool> have;
+  float* pe = nullptr;  // [13][1024]
+  // scratch (grown on demand)
+  uint16_t *c1 = nullptr, *col = nullptr, *c2 = nullptr, *feat = nullptr;
+  float* h = nullptr;
+  long long h_rows = 0;
+  bool slab_alloc = false;
+  float *hid = nullptr, *qkv = nullptr;
+  uint16_t *xn = nullptr, *att = nullptr, *ff = nullptr;
+  long long n_cap = 0;
+  float* d_mel = nullptr;
+  long long mel_cap = 0;
+  float* d_out = nullptr;
+  long long out_cap = 0;
+  // metadata staging
+  char* meta_h = nullptr;
+  char* meta_d = nullptr;
+  size_t meta_cap = 0;
+  cudaEvent_t meta_done = nullptr;
+
+  void alloc_weights() {
+    auto F = [](size_t n) { return dalloc<float>(n); };
+    auto B = [](size_t n) { return dalloc<uint16_t>(n); };
+    conv1_w = F(kDs * 9);
+    conv1_b = F(kDs);
+    conv2_w = B(static_cast<size_t>(kDs) * kTaps);
+    conv2_b = F(kDs);
+    conv3_w = B(static_cast<size_t>(kDs) * kTaps);
+    conv3_b = F(kDs);
+    conv_out_w = B(static_cast<size_t>(kD) * kCf);
+    ln_post_g = F(kD);
+    ln_post_b = F(kD);
+    proj1_w = B(static_cast<size_t>(kD) * kD);
+    proj1_b = F(kD);
+    proj2_w = B(static_cast<size_t>(kOut) * kD);
+    proj2_b = F(kOut);
+    L.resize(layers);
+    for (auto& l : L) {
+      l.ln1_g = F(kD);
+      l.ln1_b = F(kD);
+      l.qkv_w = B(3ull * kD * kD);
+      l.qkv_b = F(3 * kD);
+      l.o_w = B(static_cast<size_t>(kD) * kD);
+      l.o_b = F(kD);
+      l.ln2_g = F(kD);
+      l.ln2_b = F(kD);
+      l.fc1_w = B(static_cast<size_t>(kFfn) * kD);
+      l.fc1_b = F(kFfn);
+      l.fc2_w = B(static_cast<size_t>(kD) * kFfn);
+      l.fc2_b = F(kD);
+    }
+  }
+
+  // Checkpoint order (the synthetic generator's tensor ids follow it).
+  void build_entries() {
+    const std::string A = "thinker.audio_tower.";
+    auto add = [&](const std::string& n, Kind k, void* d, size_t numel, size_t fan, int g = 0) {
+      entries.push_back({A + n, k, d, numel, fan, g});
+    };
+    add("conv2d1.weight", kConv1, conv1_w, kDs * 9, 9);
+    add("conv2d1.bias", kVecF32, conv1_b, kDs, 0);
+    add("conv2d2.weight", kConvPerm, conv2_w, static_cast<size_t>(kDs) * kTaps, kTaps);
+    add("conv2d2.bias", kVecF32, conv2_b, kDs, 0);
+    add("conv2d3.weight", kConvPerm, conv3_w, static_cast<size_t>(kDs) * kTaps, kTaps);
+    add("conv2d3.bias", kVecF32, conv3_b, kDs, 0);
+    add("conv_out.weight", kConvOutPerm, conv_out_w, static_cast<size_t>(kD) * kCf, kCf);
+    add("ln_post.weight", kVecF32, ln_post_g, kD, 0, 1);
+    add("ln_post.bias", kVecF32, ln_post_b, kD, 0);
+    add("proj1.weight", kMatBf16, proj1_w, static_cast<size_t>(kD) * kD, kD);
+    add("proj1.bias", kVecF32, proj1_b, kD, 0);
+    add("proj2.weight", kMatBf16, proj2_w, static_cast<size_t>(kOut) * kD, kD);
+    add("proj2.bias", kVecF32, proj2_b, kOut, 0);
+    for (int i = 0; i < layers; ++i) {
+      const std::string p = "layers." + std::to_string(i) + ".";
+      Layer& l = L[i];
+      add(p + "self_attn_layer_norm.weight", kVecF32, l.ln1_g, kD, 0, 1);
+      add(p + "self_attn_layer_norm.bias", kVecF32, l.ln1_b, kD, 0);
+      const size_t mm = static_cast<size_t>(kD) * kD;
+      add(p + "self_attn.q_proj.weight", kMatBf16, l.qkv_w, mm, kD);
+      add(p + "self_attn.q_proj.bias", kVecF32, l.qkv_b, kD, 0);
+      add(p + "self_attn.k_proj.weight", kMatBf16, l.qkv_w + mm, mm, kD);
+      add(p + "self_attn.k_proj.bias", kVecF32, l.qkv_b + kD, kD, 0);
+      add(p + "self_attn.v_proj.weight", kMatBf16, l.qkv_w + 2 * mm, mm, kD);
+      add(p + "self_attn.v_proj.bias", kVecF32, l.qkv_b + 2 * kD, kD, 0);
+      add(p + "self_attn.out_proj.weight", kMatBf16, l.o_w, mm, kD);
+      add(p + "self_attn.out_proj.bias", kVecF32, l.o_b, kD, 0);
+      add(p + "final_layer_norm.weight", kVecF32, l.ln2_g, kD, 0, 1);
+      add(p + "final_layer_norm.bias", kVecF32, l.ln2_b, kD, 0);
+      add(p + "fc1.weight", kMatBf16, l.fc1_w, static_cast<size_t>(kFfn) * kD, kD);
+      add(p + "fc1.bias", kVecF32, l.fc1_b, kFfn, 0);
+      add(p + "fc2.weight", kMatBf16, l.fc2_w, static_cast<size_t>(kD) * kFfn, kFfn);
+      add(p + "fc2.bias", kVecF32, l.fc2_b, kD, 0);
+    }
+    have.assign(entries.size(), false);
+  }
+
+  void ensure_rows(long long n) {
+    if (n <= n_cap) return;
+    ORX_CHECK(cudaDeviceSynchronize());
+    for (void* p : {(void*)hid, (void*)qkv, (void*)xn, (void*)att, (void*)ff})
+      if (p) cudaFree(p);
+    n_cap = n + 256;
+    hid = dalloc<float>(n_cap * kD);
+    qkv = dalloc<float>(n_cap * 3 * kD);
+    xn = dalloc<uint16_t>(n_cap * kD);
+    att = dalloc<uint16_t>(n_cap * kD);
+    ff = dalloc<uint16_t>(n_cap * kFfn);
+  }
+  void ensure_front(long long chunks) {
+    if (!slab_alloc) {
+      c1 = dalloc<uint16_t>(static_cast<size_t>(kSlab) * kH1 * kW1 * kDs);
+      col = dalloc<uint16_t>(static_cast<size_t>(kSlab) * kH2 * kW2 * kTaps);
+      c2 = dalloc<uint16_t>(static_cast<size_t>(kSlab) * kH2 * kW2 * kDs);
+      feat = dalloc<uint16_t>(static_cast<size_t>(kSlab) * kWc * kCf);
+      slab_alloc = true;
+    }
+    if (chunks * kWc > h_rows) {
+      ORX_CHECK(cudaDeviceSynchronize());
+      if (h) cudaFree(h);
+      h_rows = chunks * kWc + 13 * 64;
+      h = dalloc<float>(h_rows * kD);
+    }
+  }
+
+  void gemm(const uint16_t* X, const uint16_t* W, int T, int K, int N, const float* bias, int act,
+            float* out_f32, uint16_t* out_bf16, int resid, cudaStream_t s) {
+    TcArgs g = {};
+    g.N = N;
+    g.K = K;
+    g.T = T;
+    g.epi = kEpiLinear;
+    g.out_f32 = out_f32;
+    g.out_bf16 = out_bf16;
+    g.ldo = N;
+    g.err = err;
+    g.bias = bias;
+    g.act = act;
+    g.resid = resid;
+    launch_gemm_tc(X, W, g, 1, s);
+    check(cudaGetLastError(), "tower gemm");
+  }
+};
+
+AudioTower::AudioTower(int layers, bool windowed) : p_(new Impl) {
+  if (layers < 0 || layers > 64) throw std::invalid_argument("encoder_layers must be in [0, 64]");
+  p_->layers = layers;
+  p_->windowed = windowed;
+  p_->err = dalloc<int>(1);
+  ORX_CHECK(cudaMemset(p_->err, 0, sizeof(int)));
+  p_->alloc_weights();
+  p_->build_entries();
+  // Whisper sinusoidal position code, rows 0..12 (asr_audio_tower.cu:285-300).
+  std::vector<float> pe(static_cast<size_t>(kWc) * kD);
+  const double inc = std::log(10000.0) / (kD / 2 - 1);
+  for (int t = 0; t < kWc; ++t)
+    for (int i = 0; i < kD / 2; ++i) {
+      const double a = t * std::exp(-inc * i);
+      pe[static_cast<size_t>(t) * kD + i] = static_cast<float>(std::sin(a));
+      pe[static_cast<size_t>(t) * kD + kD / 2 + i] = static_cast<float>(std::cos(a));
+    }
+  p_->pe = dalloc<float>(pe.size());
+  ORX_CHECK(cudaMemcpy(p_->pe, pe.data(), pe.size() * 4, cudaMemcpyHostToDevice));
+  ORX_CHECK(cudaEventCreateWithFlags(&p_->meta_done, cudaEventDisableTiming));
+}
+
+AudioTower::~AudioTower() {
+  cudaDeviceSynchronize();
+  Impl& p = *p_;
+  std::vector<void*> mine = {p.conv1_w, p.conv1_b, p.conv2_w, p.conv2_b, p.conv3_w, p.conv3_b,
+                             p.conv_out_w, p.ln_post_g, p.ln_post_b, p.proj1_w, p.proj1_b,
+                             p.proj2_w, p.proj2_b, p.pe, p.err, p.c1, p.col, p.c2, p.feat, p.h,
+                             p.hid, p.qkv, p.xn, p.att, p.ff, p.d_mel, p.d_out, p.meta_d};
+  for (auto& l : p.L)
+    for (void* q : {(void*)l.ln1_g, (void*)l.ln1_b, (void*)l.qkv_b, (void*)l.o_b, (void*)l.ln2_g,
+                    (void*)l.ln2_b, (void*)l.fc1_b, (void*)l.fc2_b, (void*)l.qkv_w, (void*)l.o_w,
+                    (void*)l.fc1_w, (void*)l.fc2_w})
+      mine.push_back(q);
+  for (void* q : mine)
+    if (q) cudaFree(q);
+  if (p.meta_h) cudaFreeHost(p.meta_h);
+  if (p.meta_done) cudaEventDestroy(p.meta_done);
+  delete p_;
+}
+
+int AudioTower::layers() const { return p_->layers; }
+
+bool AudioTower::complete() const {
+  for (bool b : p_->have)
+    if (!b) return false;
+  return true;
+}
+
+void AudioTower::set_tensor(const std::string& name, const void* data, int dtype, size_t numel) {
+  Impl& p = *p_;
+  if (dtype != 0 && dtype != 1) throw std::invalid_argument("dtype must be 0 (fp32) or 1 (bf16)");
+  for (size_t i = 0; i < p.entries.size(); ++i) {
+    const auto& e = p.entries[i];
+    if (e.name != name) continue;
+    if (numel != e.numel)
+      throw std::invalid_argument("tensor " + name + " has " + std::to_string(numel) +
+                                  " elements, expected " + std::to_string(e.numel));
+    const float* f = static_cast<const float*>(data);
+    const uint16_t* b = static_cast<const uint16_t*>(data);
+    if (e.kind == Impl::kVecF32 || e.kind == Impl::kConv1) {
+      // vectors keep fp32 (bf16 files are widened); the conv1 kernel is held
+      // as bf16 values, as the reference's bf16 im2col GEMM reads it
+      std::vector<float> v(numel);
+      for (size_t j = 0; j < numel; ++j) {
+        v[j] = dtype == 1 ? host_bf2f(b[j]) : f[j];
+        if (e.kind == Impl::kConv1) v[j] = host_bf2f(host_f2bf(v[j]));
+      }
+      ORX_CHECK(cudaMemcpy(e.dst, v.data(), numel * 4, cudaMemcpyHostToDevice));
+    } else {
+      std::vector<uint16_t> v(numel), w;
+      for (size_t j = 0; j < numel; ++j) v[j] = dtype == 1 ? b[j] : host_f2bf(f[j]);
+      if (e.kind == Impl::kConvPerm) {
+        w.resize(numel);
+        permute_conv(v.data(), w.data());
+        v.swap(w);
+      } else if (e.kind == Impl::kConvOutPerm) {
+        w.resize(numel);
+        permute_conv_out(v.data(), w.data());
+        v.swap(w);
+      }
+      ORX_CHECK(cudaMemcpy(e.dst, v.data(), numel * 2, cudaMemcpyHostToDevice));
+    }
+    p.have[i] = true;
+    return;
+  }
+  throw std::invalid_argument("unknown audio tower tensor " + name);
+}
+
+void AudioTower::init_synthetic(int seed) {
+  Impl& p = *p_;
+  // ids 80000 + i in checkpoint order; matrices N(0, 1/fan_in), vectors
+  // N(0, 0.02^2) (+1 for LayerNorm gains), all rounded to bf16.
+  float* tmp = nullptr;
+  for (size_t i = 0; i < p.entries.size(); ++i) {
+    const auto& e = p.entries[i];
+    const int tid = 80000 + static_cast<int>(i);
+    const double sd = e.fan_in ? 1.0 / std::sqrt(static_cast<double>(e.fan_in)) : 0.02;
+    const float mean = e.norm_gain ? 1.0f : 0.0f;
+    const long long n = static_cast<long long>(e.numel);
+    if (e.kind == Impl::kVecF32 || e.kind == Impl::kConv1) {
+      launch_synth_f32(static_cast<float*>(e.dst), n, seed, tid, sd, mean, 1, 0);
+    } else if (e.kind == Impl::kMatBf16) {
+      launch_synth_bf16(static_cast<uint16_t*>(e.dst), n, seed, tid, sd, mean, 0);
+    } else {
+      if (!tmp) tmp = dalloc<float>(static_cast<size_t>(kD) * kCf);
+      launch_synth_f32(tmp, n, seed, tid, sd, mean, 1, 0);
+      std::vector<float> h(e.numel);
+      ORX_CHECK(cudaMemcpy(h.data(), tmp, e.numel * 4, cudaMemcpyDeviceToHost));
+      set_tensor(e.name, h.data(), 0, e.numel);
+    }
+    ORX_CHECK(cudaGetLastError());
+    p.have[i] = true;
+  }
+  ORX_CHECK(cudaDeviceSynchronize());
+  if (tmp) cudaFree(tmp);
+}
+
+int AudioTower::device_error() const {
+  int e = 0;
+  ORX_CHECK(cudaMemcpy(&e, p_->err, sizeof(int), cudaMemcpyDeviceToHost));
+  return e;
+}
+
+int AudioTower::forward_device(const float* d_mel, const int* frames, int n_utt, float* d_out,
+                               cudaStream_t s) {
+  Impl& p = *p_;
+  if (!complete()) throw std::invalid_argument("audio tower weights are incomplete");
+  if (!tc_available()) throw CudaError("tcgen05 GEMM unavailable (tensor-map encoder missing)");
+  if (n_utt < 0) throw std::invalid_argument("utterance count must be >= 0");
+  // ---- host plan: chunks, kept rows, attention segments and tiles ----
+  std::vector<ChunkInfo> chunks;
+  std::vector<int> src_row;
+  std::vector<AttnTile> tiles;
+  long long mel_off = 0;
+  for (int u = 0; u < n_utt; ++u) {
+    const int fr = frames[u];
+    if (fr < 0) throw std::invalid_argument("frame count must be >= 0");
+    const int row_begin = static_cast<int>(src_row.size());
+    auto co = [](int x) { return x <= 0 ? 0 : (x - 1) / 2 + 1; };
+    const int max_cl = fr < kWin ? fr : kWin;
+    for (int t0 = 0; t0 < fr; t0 += kWin) {
+      const int len = fr - t0 < kWin ? fr - t0 : kWin;
+      const int c = static_cast<int>(chunks.size());
+      chunks.push_back({mel_off, fr, t0, len, co(max_cl), co(co(max_cl)), 0});
+      const int keep = output_length(len);
+      for (int t = 0; t < keep; ++t) src_row.push_back(c * kWc + t);
+    }
+    const int row_end = static_cast<int>(src_row.size());
+    const int win = p.windowed ? kWindowRows : (row_end - row_begin);
+    for (int s0 = row_begin; s0 < row_end; s0 += win > 0 ? win : 1) {
+      const int s1 = s0 + win < row_end ? s0 + win : row_end;
+      for (int r = s0; r < s1; r += kAttnRows)
+        tiles.push_back({r, s1 - r < kAttnRows ? s1 - r : kAttnRows, s0, s1});
+    }
+    mel_off += static_cast<long long>(kF) * fr;
+  }
+  const int C = static_cast<int>(chunks.size());
+  const int N = static_cast<int>(src_row.size());
+  if (N == 0) return 0;
+  // ---- metadata upload through one pinned staging buffer ----
+  auto al = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  const size_t o_chunks = 0, o_rows = al(C * sizeof(ChunkInfo)),
+               o_tiles = o_rows + al(N * sizeof(int)),
+               total = o_tiles + al(tiles.size() * sizeof(AttnTile));
+  ORX_CHECK(cudaEventSynchronize(p.meta_done));  // previous call's copy has left the buffer
+  if (total > p.meta_cap) {
+    ORX_CHECK(cudaDeviceSynchronize());
+    if (p.meta_h) cudaFreeHost(p.meta_h);
+    if (p.meta_d) cudaFree(p.meta_d);
+    p.meta_cap = total * 2;
+    ORX_CHECK(cudaMallocHost(&p.meta_h, p.meta_cap));
+    p.meta_d = dalloc<char>(p.meta_cap);
+  }
+  std::memcpy(p.meta_h + o_chunks, chunks.data(), C * sizeof(ChunkInfo));
+  std::memcpy(p.meta_h + o_rows, src_row.data(), N * sizeof(int));
+  std::memcpy(p.meta_h + o_tiles, tiles.data(), tiles.size() * sizeof(AttnTile));
+  ORX_CHECK(cudaMemcpyAsync(p.meta_d, p.meta_h, total, cudaMemcpyHostToDevice, s));
+  ORX_CHECK(cudaEventRecord(p.meta_done, s));
+  const ChunkInfo* d_chunks = reinterpret_cast<const ChunkInfo*>(p.meta_d + o_chunks);
+  const int* d_src = reinterpret_cast<const int*>(p.meta_d + o_rows);
+  const AttnTile* d_tiles = reinterpret_cast<const AttnTile*>(p.meta_d + o_tiles);
+  p.ensure_front(C);
+  p.ensure_rows(N);
+
+  // ---- conv front end, kSlab chunks at a time ----
+  for (int c0 = 0; c0 < C; c0 += kSlab) {
+    const int nc = C - c0 < kSlab ? C - c0 : kSlab;
+    tower_conv1_kernel<<<nc * kH1, 256, 0, s>>>(d_mel, d_chunks + c0, p.conv1_w, p.conv1_b, p.c1);
+    check(cudaGetLastError(), "tower conv1");
+    const long long r2 = static_cast<long long>(nc) * kH2 * kW2;
+    tower_im2col_kernel<<<grid_for_n(r2 * 9 * kVec), 256, 0, s>>>(
+        reinterpret_cast<const uint4*>(p.c1), reinterpret_cast<uint4*>(p.col), d_chunks + c0, r2, kH1, kW1, kH2,
+        kW2, 0);
+    check(cudaGetLastError(), "tower im2col");
+    p.gemm(p.col, p.conv2_w, static_cast<int>(r2), kTaps, kDs, p.conv2_b, 1, nullptr, p.c2, 0, s);
+    const long long r3 = static_cast<long long>(nc) * kH3 * kWc;
+    tower_im2col_kernel<<<grid_for_n(r3 * 9 * kVec), 256, 0, s>>>(
+        reinterpret_cast<const uint4*>(p.c2), reinterpret_cast<uint4*>(p.col), d_chunks + c0, r3, kH2, kW2, kH3,
+        kWc, 1);
+    check(cudaGetLastError(), "tower im2col");
+    p.gemm(p.col, p.conv3_w, static_cast<int>(r3), kTaps, kDs, p.conv3_b, 1, nullptr, p.feat, 0, s);
+    p.gemm(p.feat, p.conv_out_w, nc * kWc, kCf, kD, nullptr, 0,
+           p.h + static_cast<long long>(c0) * kWc * kD, nullptr, 0, s);
+  }
+  tower_gather_pe_kernel<<<grid_for_n(static_cast<long long>(N) * (kD / 4)), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(p.h), d_src, reinterpret_cast<const float4*>(p.pe),
+      reinterpret_cast<float4*>(p.hid), N);
+  check(cudaGetLastError(), "tower gather");
+
+  // ---- encoder layers ----
+  const int ln_grid = (N + 7) / 8;
+  const float scale = 1.0f / std::sqrt(static_cast<float>(kDh));
+  for (int li = 0; li < p.layers; ++li) {
+    const Impl::Layer& l = p.L[li];
+    tower_layernorm_kernel<<<ln_grid, 256, 0, s>>>(p.hid, l.ln1_g, l.ln1_b, p.xn, N);
+    p.gemm(p.xn, l.qkv_w, N, kD, 3 * kD, l.qkv_b, 0, p.qkv, nullptr, 0, s);
+    tower_attn_kernel<<<dim3(static_cast<unsigned>(tiles.size()), kHeads), kAttnRows * 32, 0, s>>>(
+        p.qkv, d_tiles, p.att, scale);
+    check(cudaGetLastError(), "tower attention");
+    p.gemm(p.att, l.o_w, N, kD, kD, l.o_b, 0, p.hid, nullptr, 1, s);
+    tower_layernorm_kernel<<<ln_grid, 256, 0, s>>>(p.hid, l.ln2_g, l.ln2_b, p.xn, N);
+    p.gemm(p.xn, l.fc1_w, N, kD, kFfn, l.fc1_b, 1, nullptr, p.ff, 0, s);
+    p.gemm(p.ff, l.fc2_w, N, kFfn, kD, l.fc2_b, 0, p.hid, nullptr, 1, s);
+  }
+  // ---- ln_post -> proj1 (GELU) -> proj2 ----
+  tower_layernorm_kernel<<<ln_grid, 256, 0, s>>>(p.hid, p.ln_post_g, p.ln_post_b, p.xn, N);
+  p.gemm(p.xn, p.proj1_w, N, kD, kD, p.proj1_b, 1, nullptr, p.att, 0, s);
+  p.gemm(p.att, p.proj2_w, N, kD, kOut, p.proj2_b, 0, d_out, nullptr, 0, s);
+  return N;
+}
+
+int AudioTower::forward_host(const float* mel, int n_frames, float* out, cudaStream_t s) {
+  Impl& p = *p_;
+  if (n_frames < 0) throw std::invalid_argument("n_frames must be >= 0");
+  const int n_out = output_length(n_frames);
+  if (n_out == 0) return 0;
+  const long long in = static_cast<long long>(kF) * n_frames;
+  if (in > p.mel_cap) {
+    ORX_CHECK(cudaDeviceSynchronize());
+    if (p.d_mel) cudaFree(p.d_mel);
+    p.mel_cap = in;
+    p.d_mel = dalloc<float>(in);
+  }
+  if (static_cast<long long>(n_out) * kOut > p.out_cap) {
+    ORX_CHECK(cudaDeviceSynchronize());
+    if (p.d_out) cudaFree(p.d_out);
+    p.out_cap = static_cast<long long>(n_out) * kOut;
+    p.d_out = dalloc<float>(p.out_cap);
+  }
+  ORX_CHECK(cudaMemcpyAsync(p.d_mel, mel, in * 4, cudaMemcpyHostToDevice, s));
+  const int n = forward_device(p.d_mel, &n_frames, 1, p.d_out, s);
+  ORX_CHECK(cudaMemcpyAsync(out, p.d_out, static_cast<size_t>(n) * kOut * 4,
+                            cudaMemcpyDeviceToHost, s));
+  ORX_CHECK(cudaStreamSynchronize(s));
+  if (device_error()) throw CudaError("audio tower: GEMM wait limit reached");
+  return n;
+}
+
+}  // namespace orx

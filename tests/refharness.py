@@ -92,3 +92,36 @@ class RefOps:
     def linear(self, x, w, bias, out, M, K, N, act):
         self._ok(self.L.ref_op_linear(C.c_void_p(x), C.c_void_p(w), C.c_void_p(bias or 0),
                                       C.c_void_p(out), M, K, N, act))
+
+
+class RefTower:
+    """The reference's AsrAudioTower (src/model/asr_audio_tower.cu), unmodified,
+    loaded from a safetensors directory; forward is its host-to-host Forward."""
+
+    def __init__(self, model_dir: str, layers: int, windowed: bool = False):
+        L = C.CDLL(LIB)
+        L.ref_tower_create.restype = C.c_void_p
+        L.ref_tower_create.argtypes = [C.c_char_p, C.c_int, C.c_int]
+        L.ref_tower_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+        L.ref_tower_destroy.argtypes = [C.c_void_p]
+        L.ref_last_error.restype = C.c_char_p
+        h = L.ref_tower_create(model_dir.encode(), layers, 1 if windowed else 0)
+        if not h:
+            raise RuntimeError(L.ref_last_error().decode())
+        self.L, self.h = L, C.c_void_p(h)
+
+    def forward(self, mel):
+        mel = np.ascontiguousarray(mel, np.float32)
+        n = mel.shape[1]
+        rows = self.L.ref_tower_output_length(C.c_int(n))
+        out = np.empty((max(rows, 1), 2048), np.float32)
+        got = self.L.ref_tower_forward(self.h, mel.ctypes.data_as(C.c_void_p), C.c_int(n),
+                                       out.ctypes.data_as(C.c_void_p))
+        if got < 0:
+            raise RuntimeError(self.L.ref_last_error().decode())
+        return out[:got]
+
+    def close(self):
+        if self.h:
+            self.L.ref_tower_destroy(self.h)
+            self.h = None
