@@ -2,10 +2,11 @@
 //
 // Replaces GqaCacheAttnKernel (src/model/asr_text_decoder.cu:88-142: one warp
 // per (token, head) walking every key of the cache). Here a CTA owns a tile of
-// up to 32 consecutive query positions of one session and one kv head (its 2
-// query heads = 64 query vectors); the session's K/V pages stream once per
-// tile through a 2-slot ring of swizzled 2-D TMA tiles and feed tensor-core
-// MMAs. Precision: q and the softmax probabilities are split into bf16 hi +
+// up to 16 consecutive query positions of one session and one kv head (its 2
+// query heads = 32 query vectors); the session's K/V pages stream once per
+// tile through an 8-slot ring of swizzled 2-D TMA tiles and feed tensor-core
+// MMAs. Four warps per query head take every fourth page each (online
+// softmax per warp) and merge their states at the end in a fixed order. Precision: q and the softmax probabilities are split into bf16 hi +
 // lo parts (hi + lo carries about 16 more bits), so QK^T and PV on bf16 MMAs
 // track the reference's fp32 dots against the bf16 cache.
 #include <cuda.h>
@@ -18,14 +19,19 @@
 namespace orx {
 namespace {
 
-constexpr int kPfWarps = 4;  // warp w: query head (w & 1), rows (w >> 1) * 16 .. +16
+constexpr int kKeyGroups = 4;                 // warps per query head, each on every 4th page
+constexpr int kPfWarps = 2 * kKeyGroups;      // warp w: query head (w & 1), key group (w >> 1)
 constexpr int kPfThreads = kPfWarps * 32;
-constexpr int kPfRows = 32;  // query positions per tile
+constexpr int kPfRows = 16;  // query positions per tile
 constexpr int kTileB = kPage * kHeadDim * 2;  // 4 KiB K or V tile
-constexpr int kSlots = 2;
+constexpr int kSlots = 2 * kKeyGroups;        // two groups of pages in flight
+constexpr int kPtStage = 1024;                // page ids staged in shared memory
+constexpr int kMergeFloats = 68;              // per lane: acc[16][4] + m0, m1, l0, l1
 constexpr int kPfSmem = kSlots * 2 * kTileB + 1024;
+static_assert((kPfWarps - 2) * 32 * kMergeFloats * 4 <= kSlots * 2 * kTileB,
+              "merge buffer reuses the ring");
 
-__global__ void __launch_bounds__(kPfThreads, 2)
+__global__ void __launch_bounds__(kPfThreads, 1)
     attn_prefill_kernel(const __grid_constant__ CUtensorMap kvmap, PrefillAttnArgs a) {
   extern __shared__ uint8_t pf_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
@@ -36,9 +42,13 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   const PrefillTile ti = a.tiles[tile];
   const int* pt = a.page_table + (long long)ti.tab * a.max_pages;
   const int npages = (ti.pos0 + ti.nrows - 1) / kPage + 1;  // keys [0, last position]
+  // The session's page ids, staged in shared memory: a global load per TMA
+  // issue would serialise one memory round trip per page on thread 0.
+  __shared__ int spt[kPtStage];
+  const bool staged = npages <= kPtStage;
   auto issue = [&](int p, int slot) {  // thread 0
     uint8_t* dst = sm + slot * 2 * kTileB;
-    const int r0 = a.kv_row0 + (pt[p] * 2 * kKvHeads + h) * kPage;
+    const int r0 = a.kv_row0 + ((staged ? spt[p] : pt[p]) * 2 * kKvHeads + h) * kPage;
     const int r1 = r0 + kKvHeads * kPage;
     mbar_arrive_expect_tx(&bar[slot], 2 * kTileB);
     tma_2d(dst, &kvmap, 0, r0, &bar[slot]);
@@ -50,14 +60,16 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     for (int i = 0; i < kSlots; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
   }
-  __syncthreads();
   pdl_trigger();
   pdl_wait();  // K/V of this prefill are stored by the previous kernel
+  if (staged)
+    for (int i = t; i < npages; i += kPfThreads) spt[i] = pt[i];
+  __syncthreads();
   if (t == 0)
     for (int p = 0; p < kSlots && p < npages; ++p) issue(p, p);
 
   // Q fragments of this warp's 16 rows: hi and lo bf16 parts.
-  const int hh = warp & 1, rbase = (warp >> 1) * 16;
+  const int hh = warp & 1, kg = warp >> 1, rbase = 0;
   const int g = lane >> 2, tig = lane & 3;
   uint32_t qh[8][4], ql[8][4];
   {
@@ -86,8 +98,10 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 #pragma unroll
   for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
-  for (int p = 0; p < npages; ++p) {
+  for (int p0 = 0; p0 < npages; p0 += kKeyGroups) {
+    const int p = p0 + kg;
     const int slot = p % kSlots;
+    if (p < npages) {
     mbar_wait(&bar[slot], (p / kSlots) & 1, a.err, 51);
     const uint8_t* base = sm + slot * 2 * kTileB;
     // S = Q K^T for 16 rows x 16 positions
@@ -165,10 +179,60 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       mma_bf16(acc[nt + 1], ph0, ph1, ph2, ph3, b2, b3);
       mma_bf16(acc[nt + 1], pl0, pl1, pl2, pl3, b2, b3);
     }
-    __syncthreads();  // every warp is done with this slot
-    if (t == 0 && p + kSlots < npages) {
+    }
+    __syncthreads();  // every warp is done with this group's slots
+    if (t == 0) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(p + kSlots, slot);
+      for (int q = p0; q < p0 + kKeyGroups; ++q)
+        if (q + kSlots < npages) issue(q + kSlots, q % kSlots);
+    }
+  }
+  // Merge the key groups of each head in group order (deterministic): groups
+  // 1..3 park their state in the (now idle) ring, group 0 combines.
+  {
+    float* mb = reinterpret_cast<float*>(sm);
+    if (kg > 0) {
+      float* dst = mb + ((size_t)(warp - 2) * 32 + lane) * kMergeFloats;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dst[i * 4 + j] = acc[i][j];
+      dst[64] = m0;
+      dst[65] = m1;
+      dst[66] = l0;
+      dst[67] = l1;
+    }
+    __syncthreads();
+    if (kg > 0) return;
+    float M0 = m0, M1 = m1;
+#pragma unroll
+    for (int k = 1; k < kKeyGroups; ++k) {
+      const float* src = mb + ((size_t)(2 * k + hh - 2) * 32 + lane) * kMergeFloats;
+      M0 = fmaxf(M0, src[64]);
+      M1 = fmaxf(M1, src[65]);
+    }
+    auto w = [](float m, float M) { return m == -INFINITY ? 0.f : expf(m - M); };
+    const float e0 = w(m0, M0), e1 = w(m1, M1);
+    l0 *= e0;
+    l1 *= e1;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      acc[i][0] *= e0; acc[i][1] *= e0;
+      acc[i][2] *= e1; acc[i][3] *= e1;
+    }
+#pragma unroll
+    for (int k = 1; k < kKeyGroups; ++k) {
+      const float* src = mb + ((size_t)(2 * k + hh - 2) * 32 + lane) * kMergeFloats;
+      const float f0 = w(src[64], M0), f1 = w(src[65], M1);
+      l0 = fmaf(src[66], f0, l0);
+      l1 = fmaf(src[67], f1, l1);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        acc[i][0] = fmaf(src[i * 4 + 0], f0, acc[i][0]);
+        acc[i][1] = fmaf(src[i * 4 + 1], f0, acc[i][1]);
+        acc[i][2] = fmaf(src[i * 4 + 2], f1, acc[i][2]);
+        acc[i][3] = fmaf(src[i * 4 + 3], f1, acc[i][3]);
+      }
     }
   }
   // normalise and store (bf16, the cast before o_proj)

@@ -11,10 +11,12 @@
 // this layer through its CPU oracle.
 //
 // One row at a time (a prompt of T rows is T successive rows, causally), five
-// launches per row: norm+qkv GEMV, q/k norm + RoPE + KV store, attention,
-// o GEMV (+residual), norm+gate/up GEMV (+SwiGLU), down GEMV (+residual).
-// The GEMVs stream fp32 weights with 16-byte non-allocating loads, eight in
-// flight per lane; at 201 MB of weights per row they are HBM-bound.
+// launches per row chained by programmatic dependent launch: norm+qkv GEMV,
+// attention (q/k norm + RoPE + KV store fused, split over positions), o GEMV
+// (+residual), norm+gate/up GEMV (+SwiGLU), down GEMV (+residual). The GEMVs
+// stream fp32 weights with 16-byte non-allocating loads, sixteen in flight per
+// lane, the first chunk issued before waiting on the previous kernel; at
+// 201 MB of weights per row they are HBM-bound.
 #include <cmath>
 #include <cstring>
 #include <stdexcept>
@@ -64,47 +66,42 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return t;
 }
 
-// Dot product of fp32 weight row w[K] with xs[K] (shared), one warp.
-__device__ __forceinline__ float row_dot(const float* w, const float* xs, int K) {
-  const float4* w4 = reinterpret_cast<const float4*>(w);
-  const float4* x4 = reinterpret_cast<const float4*>(xs);
-  const int lane = threadIdx.x & 31;
-  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-  const int n4 = K / 4;
-  int i = lane;
-  for (; i + 32 * 7 < n4; i += 32 * 8) {
-    float4 wv[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) wv[j] = ld_stream(w4 + i + 32 * j);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 xv = x4[i + 32 * j];
-      a0 = fmaf(wv[j].x, xv.x, a0);
-      a1 = fmaf(wv[j].y, xv.y, a1);
-      a2 = fmaf(wv[j].z, xv.z, a2);
-      a3 = fmaf(wv[j].w, xv.w, a3);
-    }
-  }
-  for (; i < n4; i += 32) {
-    const float4 wv = ld_stream(w4 + i), xv = x4[i];
-    a0 = fmaf(wv.x, xv.x, a0);
-    a1 = fmaf(wv.y, xv.y, a1);
-    a2 = fmaf(wv.z, xv.z, a2);
-    a3 = fmaf(wv.w, xv.w, a3);
-  }
-  return warp_sum((a0 + a1) + (a2 + a3));
-}
-
-// out[r] (op)= W[r, :] . act, act = RMSNorm(x) when norm_w is given, else x.
-// kL32Swiglu: rows r < N/2 pair gate row r with up row r + N/2.
+// out[u] (op)= W[u, :] . act, act = RMSNorm(x) when norm_w is given, else x.
+// kL32Swiglu: unit u pairs gate row u with up row u + N/2.
+// One warp per unit; each chunk of the unit's row(s) is 16 float4 per lane in
+// flight (2048 floats of one row, or 1024 of each of the two SwiGLU rows).
+// Launched with programmatic dependent launch: the CTA releases its
+// dependents at once, streams the first chunk of its first unit (weights do
+// not depend on earlier kernels), and only then waits for the producer of x.
 template <int EPI>
-__global__ void __launch_bounds__(kThreads) l32_gemv_kernel(const float* __restrict__ W,
-                                                            const float* __restrict__ x,
-                                                            const float* __restrict__ norm_w,
-                                                            float eps, int K, int N,
-                                                            const float* resid, float* out) {
+__global__ void __launch_bounds__(kThreads, 2) l32_gemv_kernel(const float* __restrict__ W,
+                                                               const float* __restrict__ x,
+                                                               const float* __restrict__ norm_w,
+                                                               float eps, int K, int N,
+                                                               const float* resid, float* out) {
+  constexpr int R = EPI == kL32Swiglu ? 2 : 1;
+  constexpr int V = 16 / R;
+  constexpr int kChunk = V * 32 * 4;  // floats of one row per chunk
   extern __shared__ float xs[];
   __shared__ float red[kWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = EPI == kL32Swiglu ? N / 2 : N;
+  const int nchunks = K / kChunk;
+  const int stride = gridDim.x * kWarps;
+  int u = blockIdx.x * kWarps + warp;
+  float4 buf[R][V];
+  auto load = [&](int unit, int c) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float4* w4 = reinterpret_cast<const float4*>(
+          W + (size_t)(unit + r * units) * K + (size_t)c * kChunk);
+#pragma unroll
+      for (int j = 0; j < V; ++j) buf[r][j] = ld_stream(w4 + lane + 32 * j);
+    }
+  };
+  pdl_trigger();
+  if (u < units) load(u, 0);
+  pdl_wait();
   for (int i = threadIdx.x; i < K; i += kThreads) xs[i] = x[i];
   if (norm_w) {
     float ss = 0.f;
@@ -113,99 +110,191 @@ __global__ void __launch_bounds__(kThreads) l32_gemv_kernel(const float* __restr
     for (int i = threadIdx.x; i < K; i += kThreads) xs[i] = xs[i] * inv * norm_w[i];
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows = EPI == kL32Swiglu ? N / 2 : N;
-  for (int r = blockIdx.x * kWarps + warp; r < rows; r += gridDim.x * kWarps) {
-    const float acc = row_dot(W + (size_t)r * K, xs, K);
+  bool loaded = true;
+  for (; u < units; u += stride) {
+    float acc[R][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.f;
+    for (int c = 0; c < nchunks; ++c) {
+      if (!loaded) load(u, c);
+      loaded = false;
+      const float4* x4 = reinterpret_cast<const float4*>(xs + c * kChunk);
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const float4 xv = x4[lane + 32 * j];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          acc[r][0] = fmaf(buf[r][j].x, xv.x, acc[r][0]);
+          acc[r][1] = fmaf(buf[r][j].y, xv.y, acc[r][1]);
+          acc[r][2] = fmaf(buf[r][j].z, xv.z, acc[r][2]);
+          acc[r][3] = fmaf(buf[r][j].w, xv.w, acc[r][3]);
+        }
+      }
+    }
+    const float a = warp_sum((acc[0][0] + acc[0][1]) + (acc[0][2] + acc[0][3]));
     if (EPI == kL32Swiglu) {
-      const float up = row_dot(W + (size_t)(r + rows) * K, xs, K);
-      if (lane == 0) out[r] = (acc / (1.0f + expf(-acc))) * up;
+      const float up = warp_sum((acc[R - 1][0] + acc[R - 1][1]) + (acc[R - 1][2] + acc[R - 1][3]));
+      if (lane == 0) out[u] = (a / (1.0f + expf(-a))) * up;
     } else if (lane == 0) {
-      out[r] = EPI == kL32Resid ? resid[r] + acc : acc;
+      out[u] = EPI == kL32Resid ? resid[u] + a : a;
     }
   }
 }
 
-// q/k RMSNorm per head + RoPE at `pos`, then q -> qout and (k, v) -> KV row
-// `pos` ([pos][K 1024 | V 1024]). One warp per head: warps 0..15 q, 16..23 k.
-__global__ void __launch_bounds__(768) l32_qk_kernel(const float* qkv, const float* qn,
-                                                     const float* kn, const float* rc,
-                                                     const float* rs, int pos, float eps,
-                                                     float* qout, float* kv) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool isq = warp < kQHeads;
-  const int h = isq ? warp : warp - kQHeads;
-  const float* src = qkv + (isq ? h * kHeadDim : kQDim + h * kHeadDim);
-  const float* w = isq ? qn : kn;
-  float v[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) v[i] = src[lane + 32 * i];
-  const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
-  const float inv = rsqrtf(ss / kHeadDim + eps);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) v[i] = v[i] * inv * w[lane + 32 * i];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int j = lane + 32 * i;
-    const float c = rc[pos * 64 + j], s = rs[pos * 64 + j];
-    const float lo = v[i], hi = v[i + 2];
-    v[i] = lo * c - hi * s;
-    v[i + 2] = hi * c + lo * s;
-  }
-  float* dst = isq ? qout + h * kHeadDim : kv + (size_t)pos * 2 * kKvDim + h * kHeadDim;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = v[i];
-  if (!isq) {
-    float* vd = kv + (size_t)pos * 2 * kKvDim + kKvDim + h * kHeadDim;
-    const float* vs = qkv + kQDim + kKvDim + h * kHeadDim;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) vd[lane + 32 * i] = vs[lane + 32 * i];
-  }
-}
+// Decode attention of one row at position `pos`, split over positions:
+// grid (splits of kAttnChunk positions, kv heads). Each CTA normalises and
+// ropes the q rows of its kv head's two query heads and the new k row
+// (q/k RMSNorm per head, rotate-half RoPE), takes the new v row, stages its
+// positions' K / V rows in shared memory (the new row in place of position
+// `pos`; the CTA holding `pos` also stores it into the cache), and writes a
+// partial softmax (max, sum, weighted V) per query head. The last CTA of the
+// kv head merges the partials in split order (deterministic).
+constexpr int kAttnChunk = 64;
 
-// One block per q head over positions [0, S): scores in shared memory,
-// softmax with expf, out = (sum_j p_j v_j) * (1 / sum_j p_j).
-__global__ void __launch_bounds__(kThreads) l32_attn_kernel(const float* q, const float* kv, int S,
+__global__ void __launch_bounds__(kThreads) l32_attn_kernel(const float* __restrict__ qkv,
+                                                            const float* __restrict__ qn,
+                                                            const float* __restrict__ kn,
+                                                            const float* __restrict__ rc,
+                                                            const float* __restrict__ rs, int pos,
+                                                            float eps, float* kv, float* part,
+                                                            int part_stride, int* counters,
                                                             float* out) {
-  extern __shared__ float sc[];
-  __shared__ float qs[kHeadDim];
-  __shared__ float red[kWarps];
-  __shared__ float acc2[kHeadDim];
-  const int h = blockIdx.x, g = h / (kQHeads / kKvHeads);
+  extern __shared__ float sm[];
+  float* ks = sm;                                  // [kAttnChunk][128]
+  float* vs = ks + kAttnChunk * kHeadDim;          // [kAttnChunk][128]
+  __shared__ float qs[kGroup][kHeadDim];
+  __shared__ float knew[kHeadDim], vnew[kHeadDim];
+  __shared__ float sc[kGroup][kAttnChunk];
+  __shared__ int last;
+  const int split = blockIdx.x, g = blockIdx.y, splits = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x < kHeadDim) qs[threadIdx.x] = q[h * kHeadDim + threadIdx.x];
+  const int S = pos + 1;
+  const int s0 = split * kAttnChunk, n = min(kAttnChunk, S - s0);
+  pdl_trigger();
+  pdl_wait();
+  if (warp <= kGroup) {  // q rows of the group (warps 0, 1) and the new k row (warp 2)
+    const bool isq = warp < kGroup;
+    const float* src = isq ? qkv + (g * kGroup + warp) * kHeadDim : qkv + kQDim + g * kHeadDim;
+    const float* w = isq ? qn : kn;
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = src[lane + 32 * i];
+    const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+    const float inv = rsqrtf(ss / kHeadDim + eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = v[i] * inv * w[lane + 32 * i];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int j = lane + 32 * i;
+      const float c = rc[pos * 64 + j], s = rs[pos * 64 + j];
+      const float lo = v[i], hi = v[i + 2];
+      v[i] = lo * c - hi * s;
+      v[i + 2] = hi * c + lo * s;
+    }
+    float* dst = isq ? qs[warp] : knew;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = v[i];
+  } else if (warp == kGroup + 1) {
+    const float* src = qkv + kQDim + kKvDim + g * kHeadDim;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) vnew[lane + 32 * i] = src[lane + 32 * i];
+  }
+  // past positions of this split: K and V rows of head g
+#pragma unroll
+  for (int it = 0; it < kAttnChunk * (kHeadDim / 4) / kThreads; ++it) {
+    const int idx = threadIdx.x + it * kThreads;
+    const int j = idx / (kHeadDim / 4), d4 = idx - j * (kHeadDim / 4);
+    if (j >= n || s0 + j == pos) continue;
+    const float4* row = reinterpret_cast<const float4*>(kv + (size_t)(s0 + j) * 2 * kKvDim + g * kHeadDim);
+    reinterpret_cast<float4*>(ks + j * kHeadDim)[d4] = row[d4];
+    reinterpret_cast<float4*>(vs + j * kHeadDim)[d4] = row[kKvDim / 4 + d4];
+  }
+  __syncthreads();
+  if (pos >= s0 && pos < s0 + n && threadIdx.x < kHeadDim) {
+    const int j = pos - s0, d = threadIdx.x;
+    ks[j * kHeadDim + d] = knew[d];
+    vs[j * kHeadDim + d] = vnew[d];
+    kv[(size_t)pos * 2 * kKvDim + g * kHeadDim + d] = knew[d];
+    kv[(size_t)pos * 2 * kKvDim + kKvDim + g * kHeadDim + d] = vnew[d];
+  }
   __syncthreads();
   const float scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
-  const float4 q4 = reinterpret_cast<const float4*>(qs)[lane];
-  for (int p = warp; p < S; p += kWarps) {
-    const float4 k = reinterpret_cast<const float4*>(kv + (size_t)p * 2 * kKvDim + g * kHeadDim)[lane];
-    const float d = warp_sum(k.x * q4.x + k.y * q4.y + k.z * q4.z + k.w * q4.w);
-    if (lane == 0) sc[p] = d * scale;
+  for (int j = warp; j < n; j += kWarps) {
+    const float4 k4 = reinterpret_cast<const float4*>(ks + j * kHeadDim)[lane];
+#pragma unroll
+    for (int h = 0; h < kGroup; ++h) {
+      const float4 q4 = reinterpret_cast<const float4*>(qs[h])[lane];
+      const float d = warp_sum(k4.x * q4.x + k4.y * q4.y + k4.z * q4.z + k4.w * q4.w);
+      if (lane == 0) sc[h][j] = d * scale;
+    }
   }
   __syncthreads();
-  float m = -INFINITY;
-  for (int p = threadIdx.x; p < S; p += kThreads) m = fmaxf(m, sc[p]);
-  m = block_max(m, red);
-  float sum = 0.f;
-  for (int p = threadIdx.x; p < S; p += kThreads) {
-    const float e = expf(sc[p] - m);
-    sc[p] = e;
-    sum += e;
+  float* pb = part + (size_t)g * kGroup * part_stride * (kHeadDim + 2);
+  if (warp < kGroup) {  // per-head max, exponentials and sum over this split
+    const int h = warp;
+    float m = -INFINITY;
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h][j]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int j = lane; j < n; j += 32) {
+      const float e = expf(sc[h][j] - m);
+      sc[h][j] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      float* ph = pb + ((size_t)h * part_stride + split) * (kHeadDim + 2);
+      ph[0] = m;
+      ph[1] = l;
+    }
   }
-  sum = block_sum(sum, red);
   __syncthreads();
-  const int d = threadIdx.x & (kHeadDim - 1), half = threadIdx.x >> 7;
-  float acc = 0.f;
-  for (int p = half; p < S; p += 2)
-    acc = fmaf(sc[p], kv[(size_t)p * 2 * kKvDim + kKvDim + g * kHeadDim + d], acc);
-  if (half == 1) acc2[d] = acc;
+  {
+    const int h = threadIdx.x / kHeadDim, d = threadIdx.x % kHeadDim;  // 256 threads = 2 heads
+    float acc = 0.f;
+    for (int j = 0; j < n; ++j) acc = fmaf(sc[h][j], vs[j * kHeadDim + d], acc);
+    pb[((size_t)h * part_stride + split) * (kHeadDim + 2) + 2 + d] = acc;
+  }
+  __threadfence();
   __syncthreads();
-  if (half == 0) out[h * kHeadDim + d] = (acc + acc2[d]) * (1.0f / sum);
+  if (threadIdx.x == 0) last = atomicAdd(&counters[g], 1) == splits - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  {
+    const int h = threadIdx.x / kHeadDim, d = threadIdx.x % kHeadDim;
+    const float* ph = pb + (size_t)h * part_stride * (kHeadDim + 2);
+    float M = -INFINITY;
+#pragma unroll 8
+    for (int sp = 0; sp < splits; ++sp) M = fmaxf(M, __ldcg(ph + (size_t)sp * (kHeadDim + 2)));
+    float L = 0.f, A = 0.f;
+    for (int sp0 = 0; sp0 < splits; sp0 += 8) {  // eight splits' loads in flight
+      float mv[8], lv[8], av[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float* q = ph + (size_t)min(sp0 + i, splits - 1) * (kHeadDim + 2);
+        mv[i] = __ldcg(q);
+        lv[i] = __ldcg(q + 1);
+        av[i] = __ldcg(q + 2 + d);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (sp0 + i >= splits) break;
+        const float e = expf(mv[i] - M);
+        L = fmaf(lv[i], e, L);
+        A = fmaf(av[i], e, A);
+      }
+    }
+    out[(g * kGroup + h) * kHeadDim + d] = A * (1.0f / L);
+  }
+  if (threadIdx.x == 0) counters[g] = 0;
 }
 
-int gemv_grid(int rows) {
-  const int g = (rows + kWarps - 1) / kWarps;
-  return g < 148 * 8 ? g : 148 * 8;
+int g_gemv_slots = 148 * 2;  // GEMV grid cap: resident CTAs (set at configuration)
+
+int gemv_grid(int units) {
+  const int g = (units + kWarps - 1) / kWarps;
+  return g < g_gemv_slots ? g : g_gemv_slots;
 }
 
 }  // namespace
@@ -219,7 +308,9 @@ struct Layer32 {
   float *in_ln = nullptr, *post_ln = nullptr, *qn = nullptr, *kn = nullptr;
   float *rc = nullptr, *rs = nullptr, *kv = nullptr;
   float *x = nullptr, *t_qkv = nullptr, *t_q = nullptr, *t_att = nullptr, *t_h = nullptr,
-        *t_act = nullptr, *t_out = nullptr;
+        *t_act = nullptr, *t_out = nullptr, *part = nullptr;
+  int* counters = nullptr;
+  int max_splits = 0;
   unsigned set_mask = 0;
   int len = 0;
 
@@ -242,14 +333,19 @@ struct Layer32 {
     t_h = dalloc<float>(kHidden);
     t_act = dalloc<float>(kInter);
     t_out = dalloc<float>(kHidden);
+    max_splits = (max_seq + kAttnChunk - 1) / kAttnChunk;
+    part = dalloc<float>((size_t)kQHeads * max_splits * (kHeadDim + 2));
+    counters = dalloc<int>(kKvHeads);
+    ORX_CHECK(cudaMemset(counters, 0, kKvHeads * sizeof(int)));
     launch_rope_table(rc, rs, max_seq, theta, 0);
     ORX_CHECK(cudaMemset(kv, 0, (size_t)max_seq * 2 * kKvDim * 4));
     ORX_CHECK(cudaDeviceSynchronize());
   }
   ~Layer32() {
     for (float* p : {qkv, o, gu, down, in_ln, post_ln, qn, kn, rc, rs, kv, x, t_qkv, t_q, t_att,
-                     t_h, t_act, t_out})
+                     t_h, t_act, t_out, part})
       if (p) cudaFree(p);
+    if (counters) cudaFree(counters);
   }
 
   // Layer-relative tensor names as in thinker.model.layers.N.<name>.weight.
@@ -304,17 +400,25 @@ struct Layer32 {
   }
 
   // One row: xin (device [2048]) at position pos -> xout (device [2048]).
+  // Five launches chained by programmatic dependent launch.
   void row(const float* xin, int pos, float* xout, cudaStream_t s) {
-    l32_gemv_kernel<kL32Store><<<gemv_grid(kQkvDim), kThreads, kHidden * 4, s>>>(
-        qkv, xin, in_ln, eps, kHidden, kQkvDim, nullptr, t_qkv);
-    l32_qk_kernel<<<1, 32 * (kQHeads + kKvHeads), 0, s>>>(t_qkv, qn, kn, rc, rs, pos, eps, t_q, kv);
-    l32_attn_kernel<<<kQHeads, kThreads, (size_t)(pos + 1) * 4, s>>>(t_q, kv, pos + 1, t_att);
-    l32_gemv_kernel<kL32Resid><<<gemv_grid(kHidden), kThreads, kQDim * 4, s>>>(
-        o, t_att, nullptr, eps, kQDim, kHidden, xin, t_h);
-    l32_gemv_kernel<kL32Swiglu><<<gemv_grid(kInter), kThreads, kHidden * 4, s>>>(
-        gu, t_h, post_ln, eps, kHidden, 2 * kInter, nullptr, t_act);
-    l32_gemv_kernel<kL32Resid><<<gemv_grid(kHidden), kThreads, kInter * 4, s>>>(
-        down, t_act, nullptr, eps, kInter, kHidden, t_h, xout);
+    ORX_CHECK(launch_pdl(l32_gemv_kernel<kL32Store>, dim3(gemv_grid(kQkvDim)), dim3(kThreads),
+                         kHidden * 4, s, (const float*)qkv, xin, (const float*)in_ln, eps, kHidden,
+                         kQkvDim, (const float*)nullptr, t_qkv));
+    const int splits = (pos + 1 + kAttnChunk - 1) / kAttnChunk;
+    ORX_CHECK(launch_pdl(l32_attn_kernel, dim3(splits, kKvHeads), dim3(kThreads),
+                         (size_t)2 * kAttnChunk * kHeadDim * 4, s, (const float*)t_qkv,
+                         (const float*)qn, (const float*)kn, (const float*)rc, (const float*)rs, pos,
+                         eps, kv, part, max_splits, counters, t_att));
+    ORX_CHECK(launch_pdl(l32_gemv_kernel<kL32Resid>, dim3(gemv_grid(kHidden)), dim3(kThreads),
+                         kQDim * 4, s, (const float*)o, (const float*)t_att, (const float*)nullptr,
+                         eps, kQDim, kHidden, xin, t_h));
+    ORX_CHECK(launch_pdl(l32_gemv_kernel<kL32Swiglu>, dim3(gemv_grid(kInter)), dim3(kThreads),
+                         kHidden * 4, s, (const float*)gu, (const float*)t_h, (const float*)post_ln,
+                         eps, kHidden, 2 * kInter, (const float*)nullptr, t_act));
+    ORX_CHECK(launch_pdl(l32_gemv_kernel<kL32Resid>, dim3(gemv_grid(kHidden)), dim3(kThreads),
+                         kInter * 4, s, (const float*)down, (const float*)t_act,
+                         (const float*)nullptr, eps, kInter, kHidden, (const float*)t_h, xout));
   }
 
   // T rows (device [T, 2048]) at positions pos0.. -> device [T, 2048].
@@ -334,9 +438,17 @@ Layer32* layer32_create(int max_seq_len, float eps, float theta) {
   once_per_device(configured, [] {
     cudaFuncSetAttribute(l32_gemv_kernel<kL32Resid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kInter * 4);
-    cudaFuncSetAttribute(l32_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(l32_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         2 * kAttnChunk * kHeadDim * 4);
+    int per_sm = 0, dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, l32_gemv_kernel<kL32Swiglu>,
+                                                      kThreads, kHidden * 4) == cudaSuccess &&
+        per_sm > 0)
+      g_gemv_slots = sms * per_sm;
   });
-  if (max_seq_len < 1 || (size_t)max_seq_len * 4 > 200 * 1024)
+  if (max_seq_len < 1 || max_seq_len > (1 << 20))
     throw std::invalid_argument("max_seq_len out of range for the fp32 layer");
   return new Layer32(max_seq_len, eps, theta);
 }

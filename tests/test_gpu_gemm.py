@@ -34,10 +34,22 @@ def test_tc_gemm_vs_f64(cuda, M, K, N):
     assert run(cuda, M, K, N) < 5e-4
 
 
-def test_tc_gemm_rejects_unsupported(cuda):
+def test_tc_gemm_rejects_bad_arguments(cuda):
+    """Argument errors are caught on the host, before any launch."""
+    import torch
     from orator_b200._lib import OrxError, call
-    with pytest.raises(OrxError):
-        call("orx_linear_pre", C.c_void_p(1), C.c_void_p(1), None, C.c_void_p(1), 4, 100, 128, 0, None)
+    x = torch.zeros(4, 128, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(128, 128, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros(4, 128, device="cuda")
+    args = [C.c_void_p(x.data_ptr()), C.c_void_p(w.data_ptr()), None, C.c_void_p(out.data_ptr())]
+    with pytest.raises(OrxError):  # activation code out of range
+        call("orx_linear_pre", *args, 4, 128, 128, 7, None)
+    with pytest.raises(OrxError):  # null weight
+        call("orx_linear_pre", args[0], None, None, args[3], 4, 128, 128, 0, None)
+    with pytest.raises(OrxError):  # odd address for a bf16 operand
+        call("orx_linear_pre", C.c_void_p(x.data_ptr() + 1), args[1], None, args[3], 4, 128, 128, 0,
+             None)
+    torch.cuda.synchronize()
 
 
 def test_gemm_deterministic(cuda):
