@@ -635,6 +635,161 @@ def tower_reference_gpu_rate(weights, mel, utts: int = 8):
         shutil.rmtree(d, ignore_errors=True)
 
 
+SF_CHUNK_FRAMES, SF_CACHE = 341 * 8, 376  # 340-frame chunk + 1 right context; spkcache + FIFO
+
+
+def sortformer_flops(n_frames: int = SF_CHUNK_FRAMES, n_cache: int = SF_CACHE,
+                     conf_layers: int = 17, dec_layers: int = 18) -> float:
+    """Algorithmic fp32 FLOPs (2 per MAC) of one streaming step: the
+    pre-encode convolutions and Linear, the conformer stack (attention counted
+    over the T x T scores it uses) and the decoder with its head."""
+    cl = lambda x: (x + 2 - 3) // 2 + 1
+    h0 = cl(n_frames)
+    h1 = cl(h0)
+    h2 = cl(h1)
+    T = n_cache + h2
+    P = 2 * T - 1
+    macs = h0 * 64 * 256 * 9 + h1 * 32 * 256 * (9 + 256) + h2 * 16 * 256 * (9 + 256) + h2 * 4096 * 512
+    lay = (2 * T * 512 * 2048 * 2 + T * 512 * 1536 + P * 512 * 512 + 8 * T * T * 64 * 3
+           + T * 512 * 512 + T * 512 * 1024 + T * 512 * 9 + T * 512 * 512)
+    dec = T * 192 * 576 + 8 * T * T * 24 * 2 + T * 192 * 192 + 2 * T * 192 * 768
+    macs += conf_layers * lay + T * 512 * 192 + dec_layers * dec + T * 192 * 192 + T * 192 * 4
+    return 2.0 * macs
+
+
+def run_config4(torch, cpu: bool, ref_gpu: bool, reps: int = 5):
+    """Config 4: one streaming Sortformer step (17 FastConformer + 18
+    transformer layers, fp32, seed 3): pre-encode of a 2728-frame N(0, 1)
+    log-mel chunk (340 + 1 frames after 8x subsampling) behind 376 speaker-cache
+    + FIFO rows, T = 717, the encoder, decoder and speaker head. Device time with
+    CUDA events; e2e through the C ABI from host mel and cache to host
+    probabilities."""
+    from orator_b200.sortformer import Sortformer
+    g = torch.Generator(device="cuda").manual_seed(3)
+    mel = torch.randn(128 * SF_CHUNK_FRAMES, device="cuda", generator=g)
+    cache = torch.randn(SF_CACHE * 512, device="cuda", generator=g)
+    T = SF_CACHE + 341
+    preds = torch.empty(T, 4, device="cuda")
+    m = Sortformer(17, 18)
+    m.init_synthetic(3)
+    s = torch.cuda.current_stream()
+    for _ in range(3):
+        m.step_device(mel.data_ptr(), SF_CHUNK_FRAMES, SF_CHUNK_FRAMES, cache.data_ptr(), SF_CACHE,
+                      preds.data_ptr(), s)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        e0.record(s)
+        m.step_device(mel.data_ptr(), SF_CHUNK_FRAMES, SF_CHUNK_FRAMES, cache.data_ptr(), SF_CACHE,
+                      preds.data_ptr(), s)
+        e1.record(s)
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ms = statistics.median(ts)
+    flops = sortformer_flops()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            bf16, kind = float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        bf16, kind = 1590.0, "fallback"
+    peak = bf16 / 3.0
+    tf = flops / (ms * 1e-3) / 1e12
+    hm, hc = mel.cpu().numpy().reshape(128, SF_CHUNK_FRAMES), cache.cpu().numpy().reshape(SF_CACHE, 512)
+    m.step(hm, hc)
+    e2e = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        m.step(hm, hc)
+        e2e.append(time.perf_counter() - t0)
+    e2e_s = statistics.median(e2e)
+    audio = 340 * 0.08  # seconds of audio one step advances (chunk_len x 80 ms frames)
+    res = {"workload": "config4: streaming Sortformer step, 17 FastConformer (d 512) + 18 transformer "
+                       "(d 192) layers, fp32 weights (seed 3), 2728-frame chunk + 376 cache/FIFO rows, T=717",
+           "value": 1e3 / ms, "unit": "steps/s", "ms_per_step": ms,
+           "audio_seconds_per_s": audio * 1e3 / ms,
+           "roofline": {"bound": "tensor (fp32 as 3 bf16 products)", "achieved": tf, "peak": peak,
+                        "peak_kind": f"{kind} cuBLAS bf16 burst / 3", "unit": "TFLOP/s",
+                        "frac": tf / peak, "flops_per_step": flops,
+                        "nominal_fp32_simt_tflops": 148 * 128 * 2 * 1.965e9 / 1e12},
+           "e2e": {"value": 1.0 / e2e_s, "unit": "steps/s",
+                   "h2d_bytes_per_step": (128 * SF_CHUNK_FRAMES + SF_CACHE * 512) * 4,
+                   "d2h_bytes_per_step": T * 4 * 4}}
+    m.close()
+    if cpu or ref_gpu:
+        from oracle import sortformer_oracle as SO
+        from orator_b200 import synth_f32
+
+        def gpu_normal(seed, tid, n, std, mean):
+            buf = torch.empty(n, dtype=torch.float32, device="cuda")
+            synth_f32(buf.data_ptr(), n, seed, tid, std, mean, False)
+            return buf.cpu().numpy()
+        w = SO.synthetic_weights(17, 18, normal=gpu_normal)
+        if cpu:
+            threads = os.cpu_count() or 1
+            torch.set_num_threads(threads)
+            o = SO.SortformerOracle(w, 17, 18)
+            t0 = time.perf_counter()
+            emb, t2, v2 = o.pre_encode(hm, SF_CHUNK_FRAMES)
+            o.encode_decode(np.concatenate([hc, emb]), SF_CACHE + v2)
+            dt = time.perf_counter() - t0
+            res["cpu_baseline"] = {"value": 1.0 / dt, "unit": "steps/s", "cores": threads, "kind": "port",
+                                   "sample": "one full step (torch fp32 restatement)"}
+        if ref_gpu:
+            res["reference_gpu"] = sortformer_reference_gpu_rate(w, hm, hc)
+            if "value" in res["reference_gpu"]:
+                res["reference_gpu"]["ours_over_reference"] = res["value"] / res["reference_gpu"]["value"]
+    return res
+
+
+def sortformer_reference_gpu_rate(weights, mel, cache, steps: int = 3):
+    """The reference's own ConformerPreEncode / ConformerLayer x 17 /
+    SortformerDecoder (oracle/_ref) on this GPU, one step per call through
+    their public host-to-host Forward methods."""
+    lib_path = os.path.join(ROOT, "oracle", "_ref", "libref_asr.so")
+    if not os.path.exists(lib_path):
+        return {"unavailable": "oracle/_ref/libref_asr.so not built (oracle/build_ref.sh)"}
+    import ctypes as C
+    import shutil
+    from oracle import sortformer_oracle as SO
+    d = tempfile.mkdtemp(prefix="ref_sf_")
+    try:
+        path = SO.write_safetensors(os.path.join(d, "sf.safetensors"), weights, 17, 18)
+        L = C.CDLL(lib_path)
+        L.ref_sf_create.restype = C.c_void_p
+        L.ref_sf_create.argtypes = [C.c_char_p, C.c_int, C.c_int]
+        L.ref_sf_destroy.argtypes = [C.c_void_p]
+        L.ref_sf_preencode.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                       C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.ref_sf_encdec.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        h = C.c_void_p(L.ref_sf_create(path.encode(), 17, 18))
+        if not h:
+            return {"unavailable": "reference Sortformer failed to load"}
+        n = mel.shape[1]
+        x = np.ascontiguousarray(mel, np.float32)
+        emb = np.empty((341, 512), np.float32)
+        preds = np.empty((SF_CACHE + 341, 4), np.float32)
+        t2, v2 = C.c_int(), C.c_int()
+
+        def one():
+            L.ref_sf_preencode(h, x.ctypes.data_as(C.c_void_p), 128, n, n,
+                               emb.ctypes.data_as(C.c_void_p), C.byref(t2), C.byref(v2))
+            cat = np.ascontiguousarray(np.concatenate([cache, emb]), np.float32)
+            L.ref_sf_encdec(h, cat.ctypes.data_as(C.c_void_p), cat.shape[0], SF_CACHE + v2.value,
+                            preds.ctypes.data_as(C.c_void_p))
+        one()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            one()
+        dt = time.perf_counter() - t0
+        L.ref_sf_destroy(h)
+        return {"value": steps / dt, "unit": "steps/s",
+                "sample": f"{steps} steps of ConformerPreEncode::Forward + ForwardEncoderDecoder "
+                          "(host in, host out)"}
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+
+
 def vad_reference_gpu_rate(pcm, streams: int = 16):
     """The reference's own GpuVad (oracle/_ref) on this GPU: one stream at a
     time, as it is built, for a sample of streams x all 100 steps (its
@@ -827,6 +982,9 @@ def run_ours(args):
     if world == 1 and not args.no_config5:
         line["config5"] = run_config5(torch, cpu=not args.no_cpu_baseline,
                                       ref_gpu=not args.no_reference_gpu)
+    if world == 1 and not args.no_config4:
+        line["config4"] = run_config4(torch, cpu=not args.no_cpu_baseline,
+                                      ref_gpu=not args.no_reference_gpu)
     if world == 1 and not args.no_tower:
         line["tower"] = run_tower(torch, cpu=not args.no_cpu_baseline,
                                   ref_gpu=not args.no_reference_gpu)
@@ -853,6 +1011,13 @@ def main():
                     help="skip timing the reference's own CUDA decoder (oracle/_ref)")
     ap.add_argument("--no-config1", action="store_true", help="skip the config-1 fp32 layer run")
     ap.add_argument("--no-config5", action="store_true", help="skip the config-5 detector run")
+    ap.add_argument("--config1-only", action="store_true",
+                    help="run only the config-1 fp32 layer timing (profiling)")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only config 2's 400-row prefill timing (profiling)")
+    ap.add_argument("--no-config4", action="store_true", help="skip the config-4 Sortformer run")
+    ap.add_argument("--config4-only", action="store_true",
+                    help="run only the config-4 Sortformer step (profiling)")
     ap.add_argument("--no-tower", action="store_true", help="skip the audio tower run")
     ap.add_argument("--tower-only", type=int, default=0, metavar="UTTS",
                     help="run only the audio tower leg over UTTS utterances (profiling)")
@@ -865,6 +1030,22 @@ def main():
     NEW_TOKENS = args.tokens
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.config4_only:
+        import torch
+        print(json.dumps(run_config4(torch, cpu=False, ref_gpu=False)), flush=True)
+        return
+    if args.config1_only:
+        import torch
+        print(json.dumps(run_config1(torch, peaks()[0], cpu=False)), flush=True)
+        return
+    if args.prefill_only:
+        import torch
+        from orator_b200 import AsrTextConfig, AsrTextDecoder
+        dec = AsrTextDecoder(AsrTextConfig(max_seq_len=2816))
+        dec.init_synthetic(SEED)
+        prompt = build_prompt_gpu(dec, torch)
+        print(json.dumps(measure_prefill(dec, torch, prompt, torch.cuda.current_stream())), flush=True)
         return
     if args.tower_only:
         import torch

@@ -299,6 +299,41 @@ int orx_tower_forward(orx_tower* t, const float* mel, int n_frames, float* out, 
 int orx_tower_forward_batch(orx_tower* t, const float* d_mel, const int* frames, int n,
                             float* d_out, int* out_rows, void* stream);
 
+/* ---- Streaming Sortformer diarizer network (ConformerPreEncode,
+ * ConformerLayer x 17, SortformerDecoder: include/model/conformer_preencode.h,
+ * conformer_layer.h, sortformer_decoder.h), fp32 model. ---- */
+typedef struct orx_sf orx_sf;
+/* `conf_layers` FastConformer layers (17 in the reference) and `dec_layers`
+ * transformer layers (18), d 512 / 192, 4 speakers. */
+int orx_sf_create(int conf_layers, int dec_layers, orx_sf** out);
+void orx_sf_destroy(orx_sf* s);
+/* One fp32 host tensor by checkpoint name (encoder.pre_encode.*,
+ * encoder.layers.N.*, sortformer_modules.*, transformer_encoder.layers.N.*),
+ * as the reference's LoadWeights read them. */
+int orx_sf_set_tensor(orx_sf* s, const char* name, const float* data, size_t numel);
+/* Every known tensor of one F32 safetensors file (SafeTensorReader). */
+int orx_sf_load_safetensors(orx_sf* s, const char* path);
+/* Seeded synthetic weights (no reference counterpart; test and bench data). */
+int orx_sf_init_synthetic(orx_sf* s, int seed);
+int orx_sf_weights_complete(const orx_sf* s, int* complete);
+/* ConformerPreEncode::Forward (conformer_preencode.cu:196-279): mel
+ * [128, n_frames] freq-major -> out [T2, 512], T2 = three stride-2 stages of
+ * n_frames; *valid_out = the same of `valid`. on_device: pointers are device
+ * memory and the call is asynchronous on `stream`; else host, synchronous. */
+int orx_sf_pre_encode(orx_sf* s, const float* mel, int n_frames, int valid, float* out, int* T_out,
+                      int* valid_out, int on_device, void* stream);
+/* SortformerDiarizer::ForwardEncoderDecoder (streaming_sortformer.cc:391-418):
+ * emb [T, 512] -> per-frame speaker probabilities preds [T, 4], rows >= valid
+ * zero. */
+int orx_sf_forward(orx_sf* s, const float* emb, int T, int valid, float* preds, int on_device,
+                   void* stream);
+/* One streaming step (StreamMelChunk's network part, streaming_sortformer.cc
+ * :468-537): pre-encode the chunk's mel, put the n_cache speaker-cache + FIFO
+ * rows [n_cache, 512] in front, run the encoder and decoder: preds [T, 4]
+ * with T = n_cache + T2 (*T_out), valid rows n_cache + valid2 (*valid_out). */
+int orx_sf_step(orx_sf* s, const float* mel, int n_frames, int valid, const float* cache,
+                int n_cache, float* preds, int* T_out, int* valid_out, int on_device, void* stream);
+
 /* Seeded synthetic fp32 data on the device, bit-exact with oracle/synth.py
  * (test and benchmark inputs; no reference counterpart). */
 int orx_synth_f32(float* d_out, long long n, int seed, int tensor_id, double std, float mean,

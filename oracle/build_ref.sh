@@ -20,7 +20,9 @@ NVCC="${NVCC:-nvcc}"
 GEN="-gencode arch=compute_100a,code=sm_100a"
 objs=()
 for f in src/model/asr_text_decoder.cu src/model/asr_gemm.cu src/model/asr_ops.cu \
-         src/pipeline/gpu_vad.cu src/model/asr_audio_tower.cu; do
+         src/pipeline/gpu_vad.cu src/model/asr_audio_tower.cu \
+         src/model/conformer_preencode.cu src/model/conformer_layer.cu \
+         src/model/sortformer_decoder.cu; do
   o="$OUT/obj/$(basename "$f").o"
   "$NVCC" -std=c++20 -O3 $GEN -Xcompiler -fPIC -I"$R/include" -c "$R/$f" -o "$o"
   objs+=("$o")

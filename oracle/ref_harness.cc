@@ -6,6 +6,7 @@
 // sharded_safetensor.cc, src/core/tensor.cc) into oracle/_ref/libref_asr.so.
 // It drives orator::model::AsrTextDecoder exactly as
 // test/unit/model/test_asr_decoder.cc:46-51 does.  The product never links it.
+#include <cmath>
 #include <cstring>
 #include <exception>
 #include <memory>
@@ -19,6 +20,10 @@
 #include "model/asr_gemm.h"
 #include "model/asr_ops.cuh"
 #include "model/asr_text_decoder.h"
+#include "model/conformer_layer.h"
+#include "model/conformer_preencode.h"
+#include "model/sortformer_decoder.h"
+#include "io/safetensor.h"
 #include "pipeline/gpu_vad.h"
 
 namespace {
@@ -276,5 +281,87 @@ int ref_gpuvad_push_drain(void* h, const float* pcm, int n, int finalize, long* 
 
 void ref_truncate(void* p, int len) { static_cast<RefHandle*>(p)->dec->TruncateCache(len); }
 int ref_cache_len(void* p) { return static_cast<RefHandle*>(p)->dec->cache_len(); }
+
+// ---- the reference's Sortformer network pieces (conformer_preencode.cu,
+// conformer_layer.cu, sortformer_decoder.cu), assembled as
+// SortformerDiarizer::ForwardEncoderDecoder does
+// (src/model/streaming_sortformer.cc:391-418) ----
+struct RefSortformer {
+  std::unique_ptr<orator::io::SafeTensorReader> r;
+  std::unique_ptr<orator::model::ConformerPreEncode> pre;
+  std::vector<std::unique_ptr<orator::model::ConformerLayer>> layers;
+  std::unique_ptr<orator::model::SortformerDecoder> dec;
+  float* dx = nullptr;
+  float* dpe = nullptr;
+  size_t cap = 0;
+};
+void* ref_sf_create(const char* path, int conf_layers, int dec_layers) {
+  try {
+    auto* h = new RefSortformer;
+    h->r = std::make_unique<orator::io::SafeTensorReader>(path);
+    h->pre = std::make_unique<orator::model::ConformerPreEncode>();
+    h->pre->LoadWeights(*h->r);
+    for (int l = 0; l < conf_layers; ++l) {
+      auto layer = std::make_unique<orator::model::ConformerLayer>(512);
+      layer->LoadWeights(*h->r, "encoder.layers." + std::to_string(l));
+      h->layers.push_back(std::move(layer));
+    }
+    h->dec = std::make_unique<orator::model::SortformerDecoder>(512, 192, 8, 768, dec_layers, 4);
+    h->dec->LoadWeights(*h->r);
+    return h;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return nullptr;
+  }
+}
+void ref_sf_destroy(void* p) {
+  auto* h = static_cast<RefSortformer*>(p);
+  if (h->dx) cudaFree(h->dx);
+  if (h->dpe) cudaFree(h->dpe);
+  delete h;
+}
+// mel [n_mels, n_frames] (host, freq-major) -> out [T2, 512] (host); writes
+// T2 and the valid length; returns 0 or -1.
+int ref_sf_preencode(void* p, const float* mel, int n_mels, int n_frames, int valid, float* out,
+                     int* T2, int* valid2) {
+  try {
+    auto v = static_cast<RefSortformer*>(p)->pre->Forward(mel, n_mels, n_frames, valid, T2,
+                                                          valid2, nullptr);
+    std::memcpy(out, v.data(), v.size() * sizeof(float));
+    return 0;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return -1;
+  }
+}
+// ForwardEncoderDecoder: emb [T, 512] (host) -> preds [T, 4] (host).
+int ref_sf_encdec(void* p, const float* emb, int T, int valid, float* preds) {
+  try {
+    auto* h = static_cast<RefSortformer*>(p);
+    const int D = 512;
+    const float xscale = std::sqrt(static_cast<float>(D));
+    std::vector<float> xin(static_cast<size_t>(T) * D);
+    for (size_t i = 0; i < xin.size(); ++i) xin[i] = emb[i] * xscale;
+    std::vector<float> pe = orator::model::ConformerLayer::BuildPosEmb(T, D);
+    if (xin.size() + pe.size() > h->cap) {
+      if (h->dx) cudaFree(h->dx);
+      if (h->dpe) cudaFree(h->dpe);
+      cudaMalloc(&h->dx, xin.size() * 4);
+      cudaMalloc(&h->dpe, pe.size() * 4);
+      h->cap = xin.size() + pe.size();
+    }
+    cudaMemcpy(h->dx, xin.data(), xin.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(h->dpe, pe.data(), pe.size() * 4, cudaMemcpyHostToDevice);
+    for (auto& l : h->layers) l->Forward(h->dx, T, valid, h->dpe, nullptr);
+    auto pr = h->dec->Forward(h->dx, T, valid, nullptr);
+    for (int f = valid; f < T; ++f)
+      for (int s = 0; s < 4; ++s) pr[static_cast<size_t>(f) * 4 + s] = 0.0f;
+    std::memcpy(preds, pr.data(), pr.size() * sizeof(float));
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return -1;
+  }
+}
 
 }  // extern "C"

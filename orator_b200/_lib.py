@@ -131,6 +131,19 @@ _SIGS = {
                                     C.POINTER(C.c_int), C.c_void_p]),
     "orx_tower_forward_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                           C.c_void_p, C.POINTER(C.c_int), C.c_void_p]),
+    "orx_sf_create": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "orx_sf_destroy": (None, [C.c_void_p]),
+    "orx_sf_set_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]),
+    "orx_sf_load_safetensors": (C.c_int, [C.c_void_p, C.c_char_p]),
+    "orx_sf_init_synthetic": (C.c_int, [C.c_void_p, C.c_int]),
+    "orx_sf_weights_complete": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "orx_sf_pre_encode": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                    C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int, C.c_void_p]),
+    "orx_sf_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                                 C.c_void_p]),
+    "orx_sf_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                              C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int,
+                              C.c_void_p]),
     "orx_synth_f32": (C.c_int, [C.c_void_p, C.c_longlong, C.c_int, C.c_int, C.c_double,
                                 C.c_float, C.c_int, C.c_void_p]),
 }

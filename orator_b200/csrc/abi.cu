@@ -32,6 +32,22 @@ struct orx_tower {
   int device = 0;
 };
 
+struct orx_sf {
+  orx::Sortformer* s = nullptr;
+  int device = 0;
+  float* stage = nullptr;  // host calls: device copies of the inputs and outputs
+  size_t cap = 0;
+  float* ensure(size_t floats) {
+    if (floats > cap) {
+      orx::check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+      if (stage) cudaFree(stage);
+      stage = orx::dalloc<float>(floats);
+      cap = floats;
+    }
+    return stage;
+  }
+};
+
 struct orx_batch {
   orx::BatchDecoder* b = nullptr;
   int device = 0;
@@ -553,6 +569,9 @@ int* gemm_err_word() {
 void linear_pre(const uint16_t* in_bf16, const uint16_t* W_bf16, const float* bias,
                 float* out_f32, int M, int K, int N, int act, cudaStream_t s) {
   if (act < 0 || act > 2) throw std::invalid_argument("act must be 0 (none), 1 (GELU) or 2 (ReLU)");
+  if (reinterpret_cast<uintptr_t>(in_bf16) % 2 || reinterpret_cast<uintptr_t>(W_bf16) % 2 ||
+      reinterpret_cast<uintptr_t>(out_f32) % 4 || reinterpret_cast<uintptr_t>(bias) % 4)
+    throw std::invalid_argument("misaligned operand (bf16 needs 2-byte, fp32 4-byte alignment)");
   if (K % 8 != 0 || !orx::tc_available() ||
       reinterpret_cast<uintptr_t>(in_bf16) % 16 != 0 || reinterpret_cast<uintptr_t>(W_bf16) % 16 != 0) {
     // shapes a tensor map cannot describe (rows must be 16-byte multiples)
@@ -897,6 +916,143 @@ int orx_tower_forward_batch(orx_tower* t, const float* d_mel, const int* frames,
     DeviceScope ds(t->device);
     const int rows = t->t->forward_device(d_mel, frames, n, d_out, S(stream));
     if (out_rows) *out_rows = rows;
+  });
+}
+
+int orx_sf_create(int conf_layers, int dec_layers, orx_sf** out) {
+  return guard([&] {
+    need(out, "out");
+    *out = nullptr;
+    auto* h = new orx_sf;
+    try {
+      orx::check(cudaGetDevice(&h->device), "cudaGetDevice");
+      h->s = new orx::Sortformer(conf_layers, dec_layers);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+void orx_sf_destroy(orx_sf* s) {
+  if (!s) return;
+  DeviceScope ds(s->device);
+  delete s->s;
+  if (s->stage) cudaFree(s->stage);
+  delete s;
+}
+
+int orx_sf_set_tensor(orx_sf* s, const char* name, const float* data, size_t numel) {
+  return guard([&] {
+    need(s, "sortformer");
+    need(name, "name");
+    need(data, "data");
+    DeviceScope ds(s->device);
+    s->s->set_tensor(name, data, numel, false);
+  });
+}
+
+int orx_sf_load_safetensors(orx_sf* s, const char* path) {
+  return guard([&] {
+    need(s, "sortformer");
+    need(path, "path");
+    DeviceScope ds(s->device);
+    s->s->load_safetensors(path);
+  });
+}
+
+int orx_sf_init_synthetic(orx_sf* s, int seed) {
+  return guard([&] {
+    need(s, "sortformer");
+    DeviceScope ds(s->device);
+    s->s->init_synthetic(seed);
+  });
+}
+
+int orx_sf_weights_complete(const orx_sf* s, int* complete) {
+  return guard([&] {
+    need(s, "sortformer");
+    need(complete, "complete");
+    *complete = s->s->complete() ? 1 : 0;
+  });
+}
+
+int orx_sf_pre_encode(orx_sf* s, const float* mel, int n_frames, int valid, float* out, int* T_out,
+                      int* valid_out, int on_device, void* stream) {
+  return guard([&] {
+    need(s, "sortformer");
+    need(mel, "mel");
+    need(out, "out");
+    if (n_frames <= 0) throw std::invalid_argument("n_frames must be positive");
+    DeviceScope ds(s->device);
+    int v2 = 0, T2 = 0;
+    if (on_device) {
+      T2 = s->s->pre_encode_device(mel, n_frames, valid, out, &v2, S(stream));
+    } else {
+      auto cl = [](int x) { return (x + 2 - 3) / 2 + 1; };
+      const int t2 = cl(cl(cl(n_frames)));
+      const size_t nin = (size_t)128 * n_frames, nout = (size_t)t2 * 512;
+      float* d = s->ensure(nin + nout);
+      orx::check(cudaMemcpyAsync(d, mel, nin * 4, cudaMemcpyHostToDevice, S(stream)), "copy in");
+      T2 = s->s->pre_encode_device(d, n_frames, valid, d + nin, &v2, S(stream));
+      orx::check(cudaMemcpyAsync(out, d + nin, nout * 4, cudaMemcpyDeviceToHost, S(stream)), "copy out");
+      orx::check(cudaStreamSynchronize(S(stream)), "sync");
+    }
+    if (T_out) *T_out = T2;
+    if (valid_out) *valid_out = v2;
+  });
+}
+
+int orx_sf_forward(orx_sf* s, const float* emb, int T, int valid, float* preds, int on_device,
+                   void* stream) {
+  return guard([&] {
+    need(s, "sortformer");
+    need(emb, "emb");
+    need(preds, "preds");
+    if (T <= 0) throw std::invalid_argument("T must be positive");
+    DeviceScope ds(s->device);
+    if (on_device) {
+      s->s->encode_decode_device(emb, T, valid, preds, S(stream));
+    } else {
+      const size_t nin = (size_t)T * 512, nout = (size_t)T * 4;
+      float* d = s->ensure(nin + nout);
+      orx::check(cudaMemcpyAsync(d, emb, nin * 4, cudaMemcpyHostToDevice, S(stream)), "copy in");
+      s->s->encode_decode_device(d, T, valid, d + nin, S(stream));
+      orx::check(cudaMemcpyAsync(preds, d + nin, nout * 4, cudaMemcpyDeviceToHost, S(stream)), "copy out");
+      orx::check(cudaStreamSynchronize(S(stream)), "sync");
+    }
+  });
+}
+
+int orx_sf_step(orx_sf* s, const float* mel, int n_frames, int valid, const float* cache,
+                int n_cache, float* preds, int* T_out, int* valid_out, int on_device, void* stream) {
+  return guard([&] {
+    need(s, "sortformer");
+    need(mel, "mel");
+    need(preds, "preds");
+    if (n_frames <= 0) throw std::invalid_argument("n_frames must be positive");
+    if (n_cache < 0) throw std::invalid_argument("n_cache must be >= 0");
+    if (n_cache > 0) need(cache, "cache");
+    DeviceScope ds(s->device);
+    int T = 0, v = 0;
+    if (on_device) {
+      T = s->s->step_device(mel, n_frames, valid, cache, n_cache, preds, &v, S(stream));
+    } else {
+      auto cl = [](int x) { return (x + 2 - 3) / 2 + 1; };
+      const int tt = n_cache + cl(cl(cl(n_frames)));
+      const size_t nin = (size_t)128 * n_frames, nc = (size_t)n_cache * 512, nout = (size_t)tt * 4;
+      float* d = s->ensure(nin + nc + nout);
+      orx::check(cudaMemcpyAsync(d, mel, nin * 4, cudaMemcpyHostToDevice, S(stream)), "copy in");
+      if (nc)
+        orx::check(cudaMemcpyAsync(d + nin, cache, nc * 4, cudaMemcpyHostToDevice, S(stream)), "copy in");
+      T = s->s->step_device(d, n_frames, valid, d + nin, n_cache, d + nin + nc, &v, S(stream));
+      orx::check(cudaMemcpyAsync(preds, d + nin + nc, nout * 4, cudaMemcpyDeviceToHost, S(stream)),
+                 "copy out");
+      orx::check(cudaStreamSynchronize(S(stream)), "sync");
+    }
+    if (T_out) *T_out = T;
+    if (valid_out) *valid_out = v;
   });
 }
 

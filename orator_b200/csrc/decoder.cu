@@ -14,6 +14,7 @@ namespace orx {
 // of CTAs covers the SMs (the short projections o / down / qkv at small T).
 GemmWs::~GemmWs() {
   if (ws) cudaFree(ws);
+  if (cnt) cudaFree(cnt);
 }
 
 int proj_splits(int N, int K, int T, int num_sms) {
@@ -48,11 +49,20 @@ size_t proj_ws_floats(int N, int K, int T, int num_sms) {
 void GemmWs::reserve(size_t floats, cudaStream_t s) {
   if (floats <= cap) return;
   ORX_CHECK(cudaStreamSynchronize(s));
+  if (!cnt) {
+    cnt = dalloc<int>(kTickets);
+    ORX_CHECK(cudaMemset(cnt, 0, kTickets * sizeof(int)));
+  }
   if (ws) cudaFree(ws);
   ws = dalloc<float>(floats);
   cap = floats;
   ++gen;
 }
+
+// The in-kernel split-K fixup (gemm_tc.cu) measured slower than the separate
+// reduction kernel at prefill sizes (12.5 vs 5.3 ms for config 2's prefill),
+// so the reduction kernel stays the default.
+constexpr bool kFixup = false;
 
 void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi,
               float* out_f32, uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s,
@@ -63,6 +73,8 @@ void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int
   if (splits > 1) {
     w.reserve((size_t)splits * T * N, s);
     g.ws = w.ws;
+    const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+    if (kFixup && (long long)((N + 127) / 128) * ((T + bn - 1) / bn) <= GemmWs::kTickets) g.tile_cnt = w.cnt;
   }
   launch_gemm_tc(X, W, g, splits, s);
 }

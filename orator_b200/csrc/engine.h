@@ -44,7 +44,9 @@ struct ModelConfig {
 // stream synchronize) and bumps `gen`, so owners of captured graphs can tell
 // that the old address is gone.
 struct GemmWs {
+  static constexpr int kTickets = 1 << 15;  // split-K fixup tickets (tiles per projection)
   float* ws = nullptr;
+  int* cnt = nullptr;  // kTickets zeroed ints, allocated with the first workspace
   size_t cap = 0;
   uint64_t gen = 0;
   void reserve(size_t floats, cudaStream_t s);
@@ -309,6 +311,34 @@ class AudioTower {
   int forward_host(const float* mel, int n_frames, float* out, cudaStream_t s);
   int device_error() const;
   static int output_length(int frames);
+
+ private:
+  struct Impl;
+  Impl* p_;
+};
+
+// Streaming Sortformer diarizer network (sortformer.cu): pre-encode,
+// FastConformer stack and transformer decoder with the speaker head.
+class Sortformer {
+ public:
+  Sortformer(int conf_layers, int dec_layers);
+  ~Sortformer();
+  Sortformer(const Sortformer&) = delete;
+  Sortformer& operator=(const Sortformer&) = delete;
+  // fp32 tensor by checkpoint name, from host or device memory.
+  void set_tensor(const std::string& name, const float* data, size_t numel, bool device);
+  void load_safetensors(const std::string& path);
+  void init_synthetic(int seed);
+  bool complete() const;
+  // mel [128, n_frames] freq-major (device) -> d_out [T2, 512]; returns T2.
+  int pre_encode_device(const float* d_mel, int n_frames, int valid, float* d_out, int* valid_out,
+                        cudaStream_t s);
+  // emb [T, 512] -> preds [T, 4] (ForwardEncoderDecoder).
+  void encode_decode_device(const float* d_emb, int T, int valid, float* d_preds, cudaStream_t s);
+  // One streaming chunk: [cache rows | pre_encode(mel)] -> preds [T, 4]; returns T.
+  int step_device(const float* d_mel, int n_frames, int valid, const float* d_cache, int n_cache,
+                  float* d_preds, int* valid_out, cudaStream_t s);
+  int device_error() const;
 
  private:
   struct Impl;

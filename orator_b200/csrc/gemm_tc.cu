@@ -15,8 +15,10 @@
 //   * 4 epilogue warps: tcgen05.ld of their 32 TMEM lanes (= 32 weight
 //     rows), then fp32 store, residual add, SwiGLU on [64 gate | 64 up] tiles
 //     with the bf16 cast of the reference, or bias + GELU / ReLU (Linear);
-//     with split K they write fp32 partials that a reduction kernel sums in
-//     split order (deterministic).
+//     with split K they write fp32 partials, and the CTA that finishes a
+//     tile's last split sums them in split order and runs the epilogue
+//     (deterministic; a separate reduction kernel when no ticket array is
+//     given).
 // Replaces Bf16WmmaKernel2 (include/model/gemm.cuh:394-459) and the
 // F32ToBf16 / AddResidual / SwiGLU launches around it.
 // No TMA multicast anywhere: every CTA loads its own tiles.
@@ -97,6 +99,7 @@ struct TcSmem {
   uint64_t acc_full[2];   // MMA -> epilogue: accumulator buffer ready
   uint64_t acc_empty[2];  // epilogue -> MMA: accumulator buffer drained
   uint32_t tmem_base;
+  int fix_last;           // split-K fixup: this CTA holds the tile's last split
   float swap[64][33];     // SwiGLU: up rows handed to the gate-row warps
 };
 
@@ -238,16 +241,9 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
       const int rloc = quarter * 32 + lane;  // row within the 128-row tile
       const int row = m0 + rloc;
       const uint32_t tbase = tmem + b * kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        float v[32];
-        tmem_ld32(tbase + c0, v);
-        if (splits > 1) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int t = n0 + c0 + i;
-            if (c0 + i < BN && t < g.T) g.ws[((long long)kz * g.T + t) * g.N + row] = v[i];
-          }
-        } else if (g.epi == kEpiSwiglu) {
+      // Output stage of 32 finished accumulator columns (tokens n0 + c0 ..).
+      auto finish = [&](float* v, int c0) {
+        if (g.epi == kEpiSwiglu) {
           asm volatile("bar.sync 1, 128;" ::: "memory");
           if (rloc >= 64) {
 #pragma unroll
@@ -276,11 +272,26 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
                 y = 0.5f * y * (1.0f + erff(y * 0.70710678118654752440f));
               else if (g.act == 2)
                 y = fmaxf(y, 0.0f);
+              else if (g.act == 3)
+                y = y / (1.0f + expf(-y));
+              else if (g.act == 4)
+                y = 1.0f / (1.0f + expf(-y));
               if (c0 + i < BN && t < g.T) {
                 const long long o = (long long)t * g.ldo + row;
-                if (g.out_bf16) g.out_bf16[o] = f2bf(y);
-                else if (g.resid) g.out_f32[o] += y;
-                else g.out_f32[o] = y;
+                if (g.out_bf16) {
+                  const uint16_t hi = f2bf(y);
+                  g.out_bf16[o] = hi;
+                  if (g.split3) {  // [hi | hi | lo] operand of the next fp32-grade GEMM
+                    g.out_bf16[o + g.N] = hi;
+                    g.out_bf16[o + 2 * g.N] = f2bf(y - bf2f(hi));
+                  }
+                } else if (g.resid == 2) {
+                  g.out_f32[o] += 0.5f * y;
+                } else if (g.resid) {
+                  g.out_f32[o] += y;
+                } else {
+                  g.out_f32[o] = y;
+                }
               }
             }
           }
@@ -298,10 +309,52 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
             if (c0 + i < BN && t < g.T) g.out_f32[(long long)t * g.ldo + row] = r[i] + v[i];
           }
         }
+      };
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tbase + c0, v);
+        if (splits > 1) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = n0 + c0 + i;
+            if (c0 + i < BN && t < g.T) g.ws[((long long)kz * g.T + t) * g.N + row] = v[i];
+          }
+        } else {
+          finish(v, c0);
+        }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
+      if (splits > 1 && g.tile_cnt) {
+        // Split-K fixup: the CTA that stores the tile's last partial sums all
+        // of them in split order (the same result whichever CTA is last)
+        // and runs the epilogue; the ticket is reset for the next launch.
+        const int tile = it / splits;
+        __threadfence();  // this thread's partial stores before the ticket
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) {
+          sm.fix_last = atomicAdd(&g.tile_cnt[tile], 1) == splits - 1;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (sm.fix_last) {
+          __threadfence();
+          for (int c0 = 0; c0 < BN; c0 += 32) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            for (int z = 0; z < splits; ++z) {  // 32 loads in flight per split
+              const float* pz = g.ws + ((long long)z * g.T + n0 + c0) * g.N + row;
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (c0 + i < BN && n0 + c0 + i < g.T) v[i] += __ldcg(pz + (long long)i * g.N);
+            }
+            finish(v, c0);
+          }
+          if (threadIdx.x == 64) g.tile_cnt[tile] = 0;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // fix_last is reused by the next item
+      }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -488,7 +541,9 @@ void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int s
     fprintf(stderr, "orx: fused RMSNorm needs residual rows of 2048\n");
     return;
   }
-  if (splits > 1) {
+  if (splits > 1 && g.tile_cnt) {
+    if (norm) launch_rmsnorm_bf16(g.out_f32, g.norm_w, g.norm_out, g.T, g.eps, s);
+  } else if (splits > 1) {
     const long long n = (long long)g.T * g.N;
     const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, 148 * 16));
     if (g.epi == kEpiSwiglu)

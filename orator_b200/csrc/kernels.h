@@ -139,12 +139,18 @@ struct TcArgs {
   const float* norm_w;
   uint16_t* norm_out;
   float eps;
-  // kEpiLinear: y = act(acc + bias[n]); act 0 none, 1 GELU (erf), 2 ReLU.
-  // The row goes to out_bf16 (rounded) when it is set, else it is stored
-  // into out_f32, or added to it when `resid` is set.
+  // kEpiLinear: y = act(acc + bias[n]); act 0 none, 1 GELU (erf), 2 ReLU,
+  // 3 SiLU, 4 sigmoid. The row goes to out_bf16 (rounded) when it is set --
+  // with `split3`, as [bf16(y) | bf16(y) | bf16(y - bf16(y))] at columns
+  // n, N + n, 2N + n (ldo = 3N) -- else it is stored into out_f32, or added
+  // to it when `resid` is 1 (half of it when 2).
   const float* bias;
   int act;
   int resid;
+  int split3;
+  // Split-K fixup tickets, one int per (m tile, token tile), zero between
+  // launches (the fixup resets them). nullptr: a reduction kernel instead.
+  int* tile_cnt;
 };
 // X: [T, K] bf16 row-major (device), W: [N, K] bf16. splits divides K / 64.
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,

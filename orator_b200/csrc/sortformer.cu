@@ -1,0 +1,857 @@
+// Streaming Sortformer diarizer network on B200 (fp32 model, fp32-grade
+// arithmetic): the pre-encode, the 17 FastConformer layers and the 18-layer
+// transformer decoder with its speaker head.
+//
+// Replaces ConformerPreEncode (src/model/conformer_preencode.cu:196-279),
+// ConformerLayer (src/model/conformer_layer.cu:330-452), SortformerDecoder
+// (src/model/sortformer_decoder.cu:240-333) and the network part of
+// SortformerDiarizer (ForwardEncoderDecoder, src/model/streaming_sortformer.cc
+// :391-418; the [spkcache | fifo | chunk] concatenation of StreamMelChunk,
+// :500-537).
+//
+// Every Linear / pointwise convolution runs on the tcgen05 GEMM (gemm_tc.cu)
+// with fp32-grade accuracy from bf16 operands: an fp32 operand x is split into
+// hi = bf16(x) and lo = bf16(x - hi), the activation row is stored as
+// [hi | hi | lo] and the weight row as [Wh | Wl | Wh], so one GEMM of depth
+// 3K sums xh*Wh + xh*Wl + xl*Wh in fp32 (relative error about 2^-16 per
+// product, against 2^-24 for the reference's fp32 SGEMM). LayerNorms, the
+// depthwise convolutions and the GEMM epilogues write activations directly
+// in that split form. Attention (relative-position MHSA in the conformer,
+// plain MHSA in the decoder), softmax, LayerNorm, BatchNorm and the
+// convolutions of the pre-encode stay fp32 on the SIMT pipes.
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "engine.h"
+#include "kernels.h"
+#include "safetensors.h"
+
+namespace orx {
+namespace {
+
+constexpr int kD = 512, kHeads = 8, kDk = 64, kDff = 2048, kKc = 9, kCh = 256, kMel = 128;
+constexpr int kDD = 192, kDHeads = 8, kDDk = 24, kDDff = 768, kSpk = 4;
+constexpr int kF0 = 64, kF1 = 32, kF2 = 16;  // frequency bins after each stride-2 stage
+constexpr float kEps = 1e-5f;
+constexpr float kMaskScore = -1e30f;         // the reference's masked score
+
+int conv_len(int x) { return (x + 2 - 3) / 2 + 1; }
+int grid_for(long long n, int threads = 256) {
+  const long long b = (n + threads - 1) / threads;
+  return static_cast<int>(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
+}
+
+__device__ __forceinline__ void put_split(uint16_t* row, int K, int k, float v) {
+  const uint16_t hi = f2bf(v);
+  row[k] = hi;
+  row[K + k] = hi;
+  row[2 * K + k] = f2bf(v - bf2f(hi));
+}
+
+// x [M, K] fp32 -> [M, 3K] split bf16, optionally ReLU'd, scaled, or with rows
+// >= valid zeroed.
+__global__ void __launch_bounds__(256) sf_split_kernel(const float* __restrict__ x,
+                                                       uint16_t* __restrict__ out, long long M,
+                                                       int K, int relu, int valid) {
+  const long long n = M * K;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / K;
+    const int k = static_cast<int>(i - r * K);
+    float v = x[i];
+    if (relu) v = fmaxf(v, 0.f);
+    if (r >= valid) v = 0.f;
+    put_split(out + r * 3 * K, K, k, v);
+  }
+}
+
+// LayerNorm of rows of D (<= 512) fp32, one warp per row (two-pass mean and
+// variance); writes fp32 (out_f32, may alias x) and / or the split form.
+__global__ void __launch_bounds__(256) sf_layernorm_kernel(const float* x, const float* __restrict__ g,
+                                                           const float* __restrict__ b,
+                                                           float* out_f32, uint16_t* out_split,
+                                                           int M, int D) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  if (r >= M) return;
+  const float* xr = x + (long long)r * D;
+  float v[16];
+  const int per = D / 32;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (i < per) {
+      v[i] = xr[lane + 32 * i];
+      s += v[i];
+    }
+  const float mean = warp_sum(s) / D;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (i < per) {
+      const float t = v[i] - mean;
+      ss += t * t;
+    }
+  const float inv = rsqrtf(warp_sum(ss) / D + kEps);
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (i < per) {
+      const int d = lane + 32 * i;
+      const float y = (v[i] - mean) * inv * g[d] + b[d];
+      if (out_f32) out_f32[(long long)r * D + d] = y;
+      if (out_split) put_split(out_split + (long long)r * 3 * D, D, d, y);
+    }
+}
+
+__global__ void sf_scale_kernel(const float* __restrict__ x, float* __restrict__ y, long long n,
+                                float s) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = x[i] * s;
+}
+
+__global__ void sf_mask_rows_kernel(float* x, int T, int D, int valid) {
+  const long long n = (long long)T * D;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    if (i / D >= valid) x[i] = 0.f;
+}
+
+// ---- pre-encode ----------------------------------------------------------
+// conv 1 -> 256, 3x3, stride 2, pad 1 over the time-major mel (frames >= valid
+// read as zero) + bias, ReLU, rows >= valid0 zeroed. One CTA per output time
+// row; output channel-last [H0][64][256].
+__global__ void __launch_bounds__(256) sf_conv0_kernel(const float* __restrict__ mel, int n_frames,
+                                                       int valid, const float* __restrict__ w,
+                                                       const float* __restrict__ b, int valid0,
+                                                       float* __restrict__ out) {
+  __shared__ float xs[3][kMel + 2];
+  __shared__ float ws[kCh * 9];
+  __shared__ float bs[kCh];
+  const int h = blockIdx.x;
+  for (int i = threadIdx.x; i < kCh * 9; i += blockDim.x) ws[i] = w[i];
+  for (int i = threadIdx.x; i < kCh; i += blockDim.x) bs[i] = b[i];
+  for (int i = threadIdx.x; i < 3 * (kMel + 2); i += blockDim.x) {
+    const int ky = i / (kMel + 2), f = i - ky * (kMel + 2) - 1;
+    const int t = 2 * h - 1 + ky;
+    float v = 0.f;
+    if (t >= 0 && t < n_frames && t < valid && f >= 0 && f < kMel) v = mel[(long long)f * n_frames + t];
+    xs[ky][f + 1] = v;
+  }
+  __syncthreads();
+  float* o = out + (long long)h * kF0 * kCh;
+  for (int idx = threadIdx.x; idx < kF0 * kCh; idx += blockDim.x) {
+    const int wo = idx / kCh, c = idx - wo * kCh;
+    float acc = bs[c];
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) acc += xs[ky][2 * wo + kx] * ws[c * 9 + ky * 3 + kx];
+    o[idx] = h < valid0 ? fmaxf(acc, 0.f) : 0.f;
+  }
+}
+
+// Depthwise 3x3 stride-2 pad-1 conv + bias over channel-last [Hi][Wi][256]
+// (input time rows >= in_valid read as zero) -> split bf16 [Ho * Wo][3 * 256].
+__global__ void __launch_bounds__(256) sf_dwconv_kernel(const float* __restrict__ in, int Hi, int Wi,
+                                                        int in_valid, const float* __restrict__ w,
+                                                        const float* __restrict__ b, int Ho, int Wo,
+                                                        uint16_t* __restrict__ out) {
+  const long long n = (long long)Ho * Wo * kCh;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = static_cast<int>(i % kCh);
+    const long long r = i / kCh;
+    const int wo = static_cast<int>(r % Wo), ho = static_cast<int>(r / Wo);
+    float acc = b[c];
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky) {
+      const int hi = 2 * ho - 1 + ky;
+      if (hi < 0 || hi >= Hi || hi >= in_valid) continue;
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) {
+        const int wi = 2 * wo - 1 + kx;
+        if (wi < 0 || wi >= Wi) continue;
+        acc += in[((long long)hi * Wi + wi) * kCh + c] * w[c * 9 + ky * 3 + kx];
+      }
+    }
+    put_split(out + r * 3 * kCh, kCh, c, acc);
+  }
+}
+
+// ---- conformer attention with relative positions --------------------------
+// score(i, j) = ((q_i + u) . k_j + (q_i + v) . p_{T-1-i+j}) / 8, keys >= valid
+// at -1e30 (RelShiftScoresKernel + AttnSoftmaxKernel of the reference).
+// qkv: [T][1536] fp32 (q | k | v), p: [2T-1][512] fp32. A CTA serves one head
+// and 16 consecutive query rows (a warp each); key tiles of 32 stream through
+// shared memory with the 47 position rows they need. Output: split bf16
+// [T][3 * 512] (input of linear_out).
+constexpr int kAr = 16, kAk = 32;
+constexpr int kRs = kDk + 4;   // padded row (floats): 16-byte reads, lane rows 4 banks apart
+constexpr int kDRs = kDDk + 4;
+__global__ void __launch_bounds__(kAr * 32) sf_relattn_kernel(const float* __restrict__ qkv,
+                                                              const float* __restrict__ p,
+                                                              const float* __restrict__ bu,
+                                                              const float* __restrict__ bv, int T,
+                                                              int valid, uint16_t* __restrict__ out) {
+  __shared__ __align__(16) float squ[kAr][kDk];
+  __shared__ __align__(16) float sqv[kAr][kDk];
+  __shared__ __align__(16) float sk[kAk][kRs];
+  __shared__ __align__(16) float sv[kAk][kDk];
+  __shared__ __align__(16) float sp[kAr + kAk - 1][kRs];
+  const int h = blockIdx.y, i0 = blockIdx.x * kAr;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = i0 + warp;
+  const bool active = i < T;
+  if (active) {
+    const float* q = qkv + (long long)i * 3 * kD + h * kDk;
+    for (int d = lane; d < kDk; d += 32) {
+      squ[warp][d] = q[d] + bu[h * kDk + d];
+      sqv[warp][d] = q[d] + bv[h * kDk + d];
+    }
+  }
+  const float scale = 0.125f;  // 1 / sqrt(64)
+  float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
+  // The next tile's K / V / position rows are loaded into registers while the
+  // current tile is being scored (one tile of global loads in flight).
+  constexpr int kKv4 = kAk * (kDk / 4) / (kAr * 32);               // float4 of K (and V) per thread
+  constexpr int kP4 = ((kAr + kAk - 1) * (kDk / 4) + kAr * 32 - 1) / (kAr * 32);
+  float4 rk[kKv4], rv[kKv4], rp[kP4];
+  auto fetch = [&](int j0) {
+    const int mbase = T - 1 - (i0 + kAr - 1) + j0;  // position row of (i0 + 15, j0)
+#pragma unroll
+    for (int e = 0; e < kKv4; ++e) {
+      const int idx = threadIdx.x + e * kAr * 32;
+      const int jj = idx / (kDk / 4), d4 = idx - jj * (kDk / 4), j = j0 + jj;
+      rk[e] = rv[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < T) {
+        const float4* base = reinterpret_cast<const float4*>(qkv + (long long)j * 3 * kD + h * kDk);
+        rk[e] = base[kD / 4 + d4];
+        rv[e] = base[2 * kD / 4 + d4];
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < kP4; ++e) {
+      const int idx = threadIdx.x + e * kAr * 32;
+      const int rr = idx / (kDk / 4), d4 = idx - rr * (kDk / 4), mrow = mbase + rr;
+      rp[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (rr < kAr + kAk - 1 && mrow >= 0 && mrow < 2 * T - 1)
+        rp[e] = reinterpret_cast<const float4*>(p + (long long)mrow * kD + h * kDk)[d4];
+    }
+  };
+  fetch(0);
+  for (int j0 = 0; j0 < T; j0 += kAk) {
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < kKv4; ++e) {
+      const int idx = threadIdx.x + e * kAr * 32;
+      const int jj = idx / (kDk / 4), d4 = idx - jj * (kDk / 4);
+      *reinterpret_cast<float4*>(&sk[jj][4 * d4]) = rk[e];
+      *reinterpret_cast<float4*>(&sv[jj][4 * d4]) = rv[e];
+    }
+#pragma unroll
+    for (int e = 0; e < kP4; ++e) {
+      const int idx = threadIdx.x + e * kAr * 32;
+      const int rr = idx / (kDk / 4), d4 = idx - rr * (kDk / 4);
+      if (rr < kAr + kAk - 1) *reinterpret_cast<float4*>(&sp[rr][4 * d4]) = rp[e];
+    }
+    __syncthreads();
+    if (j0 + kAk < T) fetch(j0 + kAk);
+    if (!active) continue;
+    const int j = j0 + lane;
+    const int pr = (kAr - 1 - warp) + lane;  // row T-1-i+j relative to mbase
+    float ac = 0.f, bd = 0.f;
+#pragma unroll
+    for (int d4 = 0; d4 < kDk / 4; ++d4) {
+      const float4 k4 = *reinterpret_cast<const float4*>(&sk[lane][4 * d4]);
+      const float4 u4 = *reinterpret_cast<const float4*>(&squ[warp][4 * d4]);
+      const float4 p4 = *reinterpret_cast<const float4*>(&sp[pr][4 * d4]);
+      const float4 w4 = *reinterpret_cast<const float4*>(&sqv[warp][4 * d4]);
+      ac = fmaf(u4.x, k4.x, ac);
+      ac = fmaf(u4.y, k4.y, ac);
+      ac = fmaf(u4.z, k4.z, ac);
+      ac = fmaf(u4.w, k4.w, ac);
+      bd = fmaf(w4.x, p4.x, bd);
+      bd = fmaf(w4.y, p4.y, bd);
+      bd = fmaf(w4.z, p4.z, bd);
+      bd = fmaf(w4.w, p4.w, bd);
+    }
+    float s = j < valid ? (ac + bd) * scale : kMaskScore;
+    const bool in = j < T;
+    if (!in) s = -INFINITY;
+    const float mn = fmaxf(m, warp_max(s));
+    const float corr = expf(m - mn);
+    const float pj = in ? expf(s - mn) : 0.f;
+    l = l * corr + warp_sum(pj);
+    a0 *= corr;
+    a1 *= corr;
+    const int nj = min(kAk, T - j0);
+    for (int jj = 0; jj < nj; ++jj) {
+      const float w = __shfl_sync(0xffffffffu, pj, jj);
+      a0 = fmaf(w, sv[jj][lane], a0);
+      a1 = fmaf(w, sv[jj][lane + 32], a1);
+    }
+    m = mn;
+  }
+  if (!active) return;
+  const float inv = 1.0f / l;
+  uint16_t* o = out + (long long)i * 3 * kD;
+  put_split(o, kD, h * kDk + lane, a0 * inv);
+  put_split(o, kD, h * kDk + lane + 32, a1 * inv);
+}
+
+// Decoder attention (8 heads of 24), keys >= valid at -1e30; qkv [T][576].
+__global__ void __launch_bounds__(kAr * 32) sf_attn_kernel(const float* __restrict__ qkv, int T,
+                                                           int valid, uint16_t* __restrict__ out) {
+  __shared__ __align__(16) float sq[kAr][kDDk];
+  __shared__ __align__(16) float sk[kAk][kDRs];
+  __shared__ __align__(16) float sv[kAk][kDDk];
+  const int h = blockIdx.y, i0 = blockIdx.x * kAr;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = i0 + warp;
+  const bool active = i < T;
+  if (active && lane < kDDk) sq[warp][lane] = qkv[(long long)i * 3 * kDD + h * kDDk + lane];
+  const float scale = 1.0f / sqrtf(static_cast<float>(kDDk));
+  float m = -INFINITY, l = 0.f, a = 0.f;
+  // next tile's K / V rows in registers while the current one is scored
+  constexpr int kN4 = kAk * (kDDk / 4);  // 192 float4 of K (and V) per tile
+  float4 rk = make_float4(0.f, 0.f, 0.f, 0.f), rv = rk;
+  auto fetch = [&](int j0) {
+    rk = rv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (threadIdx.x >= kN4) return;
+    const int jj = threadIdx.x / (kDDk / 4), d4 = threadIdx.x - jj * (kDDk / 4), j = j0 + jj;
+    if (j < T) {
+      const float4* base = reinterpret_cast<const float4*>(qkv + (long long)j * 3 * kDD + h * kDDk);
+      rk = base[kDD / 4 + d4];
+      rv = base[2 * kDD / 4 + d4];
+    }
+  };
+  fetch(0);
+  for (int j0 = 0; j0 < T; j0 += kAk) {
+    __syncthreads();
+    if (threadIdx.x < kN4) {
+      const int jj = threadIdx.x / (kDDk / 4), d4 = threadIdx.x - jj * (kDDk / 4);
+      *reinterpret_cast<float4*>(&sk[jj][4 * d4]) = rk;
+      *reinterpret_cast<float4*>(&sv[jj][4 * d4]) = rv;
+    }
+    __syncthreads();
+    if (j0 + kAk < T) fetch(j0 + kAk);
+    if (!active) continue;
+    const int j = j0 + lane;
+    float dot = 0.f;
+#pragma unroll
+    for (int d4 = 0; d4 < kDDk / 4; ++d4) {
+      const float4 k4 = *reinterpret_cast<const float4*>(&sk[lane][4 * d4]);
+      const float4 q4 = *reinterpret_cast<const float4*>(&sq[warp][4 * d4]);
+      dot = fmaf(q4.x, k4.x, dot);
+      dot = fmaf(q4.y, k4.y, dot);
+      dot = fmaf(q4.z, k4.z, dot);
+      dot = fmaf(q4.w, k4.w, dot);
+    }
+    float s = j < valid ? dot * scale : kMaskScore;
+    const bool in = j < T;
+    if (!in) s = -INFINITY;
+    const float mn = fmaxf(m, warp_max(s));
+    const float corr = expf(m - mn);
+    const float pj = in ? expf(s - mn) : 0.f;
+    l = l * corr + warp_sum(pj);
+    a *= corr;
+    const int nj = min(kAk, T - j0);
+    for (int jj = 0; jj < nj; ++jj) {
+      const float w = __shfl_sync(0xffffffffu, pj, jj);
+      if (lane < kDDk) a = fmaf(w, sv[jj][lane], a);
+    }
+    m = mn;
+  }
+  if (!active || lane >= kDDk) return;
+  put_split(out + (long long)i * 3 * kDD, kDD, h * kDDk + lane, a / l);
+}
+
+// Conv module middle: GLU of pointwise_conv1's output (rows >= valid zero),
+// depthwise conv k9 (zero padding) + bias, BatchNorm (running statistics),
+// SiLU -> split bf16 [T][3 * 512] (input of pointwise_conv2).
+__global__ void __launch_bounds__(256) sf_convmod_kernel(const float* __restrict__ pw1, int T,
+                                                         int valid, const float* __restrict__ dw,
+                                                         const float* __restrict__ dwb,
+                                                         const float* __restrict__ mean,
+                                                         const float* __restrict__ var,
+                                                         const float* __restrict__ gamma,
+                                                         const float* __restrict__ beta,
+                                                         uint16_t* __restrict__ out) {
+  const long long n = (long long)T * kD;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = static_cast<int>(i % kD), t = static_cast<int>(i / kD);
+    float acc = dwb[c];
+#pragma unroll
+    for (int kk = 0; kk < kKc; ++kk) {
+      const int ti = t + kk - kKc / 2;
+      if (ti < 0 || ti >= T || ti >= valid) continue;
+      const float a = pw1[(long long)ti * 2 * kD + c], g = pw1[(long long)ti * 2 * kD + kD + c];
+      acc += a * (1.0f / (1.0f + expf(-g))) * dw[c * kKc + kk];
+    }
+    const float y = (acc - mean[c]) * rsqrtf(var[c] + kEps) * gamma[c] + beta[c];
+    put_split(out + (long long)t * 3 * kD, kD, c, y / (1.0f + expf(-y)));
+  }
+}
+
+// Weight row of a Linear in split form: W3[n] = [Wh | Wl | Wh] of W[n]
+// (columns permuted from c * F + f to f * C + c when C > 0).
+__global__ void sf_make_w3_kernel(const float* __restrict__ W, uint16_t* __restrict__ W3, int N,
+                                  int K, int C, int F) {
+  const long long n = (long long)N * K;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / K;
+    const int k = static_cast<int>(i - r * K);
+    int src = k;
+    if (C > 0) {
+      const int f = k / C, c = k - f * C;
+      src = c * F + f;
+    }
+    const float v = W[r * K + src];
+    const uint16_t hi = f2bf(v);
+    uint16_t* row = W3 + r * 3 * K;
+    row[k] = hi;
+    row[K + k] = f2bf(v - bf2f(hi));
+    row[2 * K + k] = hi;
+  }
+}
+
+}  // namespace
+
+struct Sortformer::Impl {
+  int L = 0, DL = 0;
+  int* err = nullptr;
+  // One entry per checkpoint tensor.
+  enum Kind { kVec, kLin, kLinPerm };
+  struct Entry {
+    std::string name;
+    Kind kind;
+    void* dst;      // fp32 vector, or the W3 block (row offset applied)
+    size_t numel;
+    int N, K;       // Linear shape
+    int tkind;      // synthetic init: 0 matrix, 1 bias, 2 gain, 3 BN variance
+    size_t fan_in;
+  };
+  std::vector<Entry> entries;
+  std::vector<bool> have;
+  std::vector<void*> allocs;
+
+  // pre-encode
+  float *c0w, *c0b, *c2w, *c2b, *c3b, *c5w, *c5b, *c6b, *outb;
+  uint16_t *c3w, *c6w, *outw;
+  struct Conf {
+    float *ln1g, *ln1b, *ff1b1, *ff1b2, *lnag, *lnab, *qkvb, *ob, *bu, *bv, *lncg, *lncb, *pw1b,
+        *dww, *dwb, *bng, *bnb, *bnm, *bnv, *pw2b, *ln2g, *ln2b, *ff2b1, *ff2b2, *lnog, *lnob;
+    uint16_t *ff1w1, *ff1w2, *qkvw, *ow, *posw, *pw1w, *pw2w, *ff2w1, *ff2w2;
+  };
+  std::vector<Conf> C;
+  float *projb, *hidb, *spkb;
+  uint16_t *projw, *hidw, *spkw;
+  struct Dec {
+    float *qkvb, *ob, *inb, *outb, *ln1g, *ln1b, *ln2g, *ln2b;
+    uint16_t *qkvw, *ow, *inw, *outw;
+  };
+  std::vector<Dec> Dl;
+
+  // scratch
+  struct Buf {
+    void* p = nullptr;
+    size_t cap = 0;
+    template <class T>
+    T* get(size_t n) {
+      if (n * sizeof(T) > cap) {
+        ORX_CHECK(cudaDeviceSynchronize());
+        if (p) cudaFree(p);
+        cap = n * sizeof(T) + 4096;
+        ORX_CHECK(cudaMalloc(&p, cap));
+      }
+      return static_cast<T*>(p);
+    }
+    ~Buf() {
+      if (p) cudaFree(p);
+    }
+  };
+  Buf b_a, b_b, b_s1, b_s2, b_x, b_qkv, b_p, b_pe, b_pes, b_big, b_mel, b_out, b_emb;
+  std::vector<float> pe_host;
+  int pe_T = -1;
+
+  float* F(size_t n) {
+    float* p = dalloc<float>(n);
+    allocs.push_back(p);
+    return p;
+  }
+  uint16_t* B3(size_t N, size_t K) {
+    uint16_t* p = dalloc<uint16_t>(N * 3 * K);
+    allocs.push_back(p);
+    return p;
+  }
+  void vec(const std::string& n, float* d, size_t numel, int tk) {
+    entries.push_back({n, kVec, d, numel, 0, 0, tk, 0});
+  }
+  void lin(const std::string& n, uint16_t* w3, int N, int K, Kind k = kLin) {
+    entries.push_back({n, k, w3, (size_t)N * K, N, K, 0, (size_t)K});
+  }
+
+  void build() {
+    const std::string P = "encoder.pre_encode.";
+    c0w = F(kCh * 9); c0b = F(kCh); c2w = F(kCh * 9); c2b = F(kCh); c3b = F(kCh);
+    c5w = F(kCh * 9); c5b = F(kCh); c6b = F(kCh); outb = F(kD);
+    c3w = B3(kCh, kCh); c6w = B3(kCh, kCh); outw = B3(kD, kCh * kF2);
+    entries.push_back({P + "conv.0.weight", kVec, c0w, kCh * 9, 0, 0, 0, 9});
+    vec(P + "conv.0.bias", c0b, kCh, 1);
+    entries.push_back({P + "conv.2.weight", kVec, c2w, kCh * 9, 0, 0, 0, 9});
+    vec(P + "conv.2.bias", c2b, kCh, 1);
+    lin(P + "conv.3.weight", c3w, kCh, kCh);
+    vec(P + "conv.3.bias", c3b, kCh, 1);
+    entries.push_back({P + "conv.5.weight", kVec, c5w, kCh * 9, 0, 0, 0, 9});
+    vec(P + "conv.5.bias", c5b, kCh, 1);
+    lin(P + "conv.6.weight", c6w, kCh, kCh);
+    vec(P + "conv.6.bias", c6b, kCh, 1);
+    lin(P + "out.weight", outw, kD, kCh * kF2, kLinPerm);
+    vec(P + "out.bias", outb, kD, 1);
+    C.resize(L);
+    for (int i = 0; i < L; ++i) {
+      Conf& c = C[i];
+      const std::string p = "encoder.layers." + std::to_string(i) + ".";
+      c.ln1g = F(kD); c.ln1b = F(kD); c.ff1w1 = B3(kDff, kD); c.ff1b1 = F(kDff);
+      c.ff1w2 = B3(kD, kDff); c.ff1b2 = F(kD);
+      c.lnag = F(kD); c.lnab = F(kD); c.qkvw = B3(3 * kD, kD); c.qkvb = F(3 * kD);
+      c.ow = B3(kD, kD); c.ob = F(kD); c.posw = B3(kD, kD); c.bu = F(kD); c.bv = F(kD);
+      c.lncg = F(kD); c.lncb = F(kD); c.pw1w = B3(2 * kD, kD); c.pw1b = F(2 * kD);
+      c.dww = F(kD * kKc); c.dwb = F(kD); c.bng = F(kD); c.bnb = F(kD); c.bnm = F(kD); c.bnv = F(kD);
+      c.pw2w = B3(kD, kD); c.pw2b = F(kD);
+      c.ln2g = F(kD); c.ln2b = F(kD); c.ff2w1 = B3(kDff, kD); c.ff2b1 = F(kDff);
+      c.ff2w2 = B3(kD, kDff); c.ff2b2 = F(kD); c.lnog = F(kD); c.lnob = F(kD);
+      vec(p + "norm_feed_forward1.weight", c.ln1g, kD, 2);
+      vec(p + "norm_feed_forward1.bias", c.ln1b, kD, 1);
+      lin(p + "feed_forward1.linear1.weight", c.ff1w1, kDff, kD);
+      vec(p + "feed_forward1.linear1.bias", c.ff1b1, kDff, 1);
+      lin(p + "feed_forward1.linear2.weight", c.ff1w2, kD, kDff);
+      vec(p + "feed_forward1.linear2.bias", c.ff1b2, kD, 1);
+      vec(p + "norm_self_att.weight", c.lnag, kD, 2);
+      vec(p + "norm_self_att.bias", c.lnab, kD, 1);
+      const char* qkvn[3] = {"linear_q", "linear_k", "linear_v"};
+      for (int j = 0; j < 3; ++j) {
+        lin(p + "self_attn." + qkvn[j] + ".weight", c.qkvw + (size_t)j * kD * 3 * kD, kD, kD);
+        vec(p + "self_attn." + qkvn[j] + ".bias", c.qkvb + j * kD, kD, 1);
+      }
+      lin(p + "self_attn.linear_out.weight", c.ow, kD, kD);
+      vec(p + "self_attn.linear_out.bias", c.ob, kD, 1);
+      lin(p + "self_attn.linear_pos.weight", c.posw, kD, kD);
+      vec(p + "self_attn.pos_bias_u", c.bu, kD, 1);
+      vec(p + "self_attn.pos_bias_v", c.bv, kD, 1);
+      vec(p + "norm_conv.weight", c.lncg, kD, 2);
+      vec(p + "norm_conv.bias", c.lncb, kD, 1);
+      lin(p + "conv.pointwise_conv1.weight", c.pw1w, 2 * kD, kD);
+      vec(p + "conv.pointwise_conv1.bias", c.pw1b, 2 * kD, 1);
+      entries.push_back({p + "conv.depthwise_conv.weight", kVec, c.dww, (size_t)kD * kKc, 0, 0, 0,
+                         (size_t)kKc});
+      vec(p + "conv.depthwise_conv.bias", c.dwb, kD, 1);
+      vec(p + "conv.batch_norm.weight", c.bng, kD, 2);
+      vec(p + "conv.batch_norm.bias", c.bnb, kD, 1);
+      vec(p + "conv.batch_norm.running_mean", c.bnm, kD, 1);
+      vec(p + "conv.batch_norm.running_var", c.bnv, kD, 3);
+      lin(p + "conv.pointwise_conv2.weight", c.pw2w, kD, kD);
+      vec(p + "conv.pointwise_conv2.bias", c.pw2b, kD, 1);
+      vec(p + "norm_feed_forward2.weight", c.ln2g, kD, 2);
+      vec(p + "norm_feed_forward2.bias", c.ln2b, kD, 1);
+      lin(p + "feed_forward2.linear1.weight", c.ff2w1, kDff, kD);
+      vec(p + "feed_forward2.linear1.bias", c.ff2b1, kDff, 1);
+      lin(p + "feed_forward2.linear2.weight", c.ff2w2, kD, kDff);
+      vec(p + "feed_forward2.linear2.bias", c.ff2b2, kD, 1);
+      vec(p + "norm_out.weight", c.lnog, kD, 2);
+      vec(p + "norm_out.bias", c.lnob, kD, 1);
+    }
+    const std::string S = "sortformer_modules.";
+    projw = B3(kDD, kD); projb = F(kDD); hidw = B3(kDD, kDD); hidb = F(kDD);
+    spkw = B3(kSpk, kDD); spkb = F(kSpk);
+    lin(S + "encoder_proj.weight", projw, kDD, kD);
+    vec(S + "encoder_proj.bias", projb, kDD, 1);
+    lin(S + "first_hidden_to_hidden.weight", hidw, kDD, kDD);
+    vec(S + "first_hidden_to_hidden.bias", hidb, kDD, 1);
+    lin(S + "single_hidden_to_spks.weight", spkw, kSpk, kDD);
+    vec(S + "single_hidden_to_spks.bias", spkb, kSpk, 1);
+    Dl.resize(DL);
+    for (int i = 0; i < DL; ++i) {
+      Dec& d = Dl[i];
+      const std::string p = "transformer_encoder.layers." + std::to_string(i) + ".";
+      d.qkvw = B3(3 * kDD, kDD); d.qkvb = F(3 * kDD); d.ow = B3(kDD, kDD); d.ob = F(kDD);
+      d.inw = B3(kDDff, kDD); d.inb = F(kDDff); d.outw = B3(kDD, kDDff); d.outb = F(kDD);
+      d.ln1g = F(kDD); d.ln1b = F(kDD); d.ln2g = F(kDD); d.ln2b = F(kDD);
+      const char* qkvn[3] = {"query_net", "key_net", "value_net"};
+      for (int j = 0; j < 3; ++j) {
+        lin(p + "first_sub_layer." + qkvn[j] + ".weight", d.qkvw + (size_t)j * kDD * 3 * kDD, kDD, kDD);
+        vec(p + "first_sub_layer." + qkvn[j] + ".bias", d.qkvb + j * kDD, kDD, 1);
+      }
+      lin(p + "first_sub_layer.out_projection.weight", d.ow, kDD, kDD);
+      vec(p + "first_sub_layer.out_projection.bias", d.ob, kDD, 1);
+      lin(p + "second_sub_layer.dense_in.weight", d.inw, kDDff, kDD);
+      vec(p + "second_sub_layer.dense_in.bias", d.inb, kDDff, 1);
+      lin(p + "second_sub_layer.dense_out.weight", d.outw, kDD, kDDff);
+      vec(p + "second_sub_layer.dense_out.bias", d.outb, kDD, 1);
+      vec(p + "layer_norm_1.weight", d.ln1g, kDD, 2);
+      vec(p + "layer_norm_1.bias", d.ln1b, kDD, 1);
+      vec(p + "layer_norm_2.weight", d.ln2g, kDD, 2);
+      vec(p + "layer_norm_2.bias", d.ln2b, kDD, 1);
+    }
+    have.assign(entries.size(), false);
+  }
+
+  // Linear on the split operands: out = act(X3 . W3^T + bias), X3 [M][3K].
+  void gemm(const uint16_t* X3, const uint16_t* W3, int M, int K, int N, const float* bias, int act,
+            float* out_f32, uint16_t* out_split, int resid, cudaStream_t s) {
+    TcArgs g = {};
+    g.N = N;
+    g.K = 3 * K;
+    g.T = M;
+    g.epi = kEpiLinear;
+    g.out_f32 = out_f32;
+    g.out_bf16 = out_split;
+    g.split3 = out_split ? 1 : 0;
+    g.ldo = out_split ? 3 * N : N;
+    g.err = err;
+    g.bias = bias;
+    g.act = act;
+    g.resid = resid;
+    launch_gemm_tc(X3, W3, g, 1, s);
+    check(cudaGetLastError(), "sortformer gemm");
+  }
+  void ln(const float* x, const float* g, const float* b, float* of, uint16_t* os, int M, int Dm,
+          cudaStream_t s) {
+    sf_layernorm_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, g, b, of, os, M, Dm);
+    check(cudaGetLastError(), "sortformer layernorm");
+  }
+};
+
+Sortformer::Sortformer(int conf_layers, int dec_layers) : p_(new Impl) {
+  if (conf_layers < 0 || conf_layers > 64 || dec_layers < 0 || dec_layers > 64)
+    throw std::invalid_argument("layer counts must be in [0, 64]");
+  p_->L = conf_layers;
+  p_->DL = dec_layers;
+  p_->err = dalloc<int>(1);
+  ORX_CHECK(cudaMemset(p_->err, 0, sizeof(int)));
+  p_->build();
+}
+
+Sortformer::~Sortformer() {
+  cudaDeviceSynchronize();
+  for (void* q : p_->allocs) cudaFree(q);
+  cudaFree(p_->err);
+  delete p_;
+}
+
+bool Sortformer::complete() const {
+  for (bool b : p_->have)
+    if (!b) return false;
+  return true;
+}
+
+void Sortformer::set_tensor(const std::string& name, const float* data, size_t numel, bool device) {
+  Impl& p = *p_;
+  for (size_t i = 0; i < p.entries.size(); ++i) {
+    const auto& e = p.entries[i];
+    if (e.name != name) continue;
+    if (numel != e.numel)
+      throw std::invalid_argument("tensor " + name + " has " + std::to_string(numel) +
+                                  " elements, expected " + std::to_string(e.numel));
+    const cudaMemcpyKind kind = device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    if (e.kind == Impl::kVec) {
+      ORX_CHECK(cudaMemcpy(e.dst, data, numel * 4, kind));
+    } else {
+      float* tmp = dalloc<float>(numel);
+      ORX_CHECK(cudaMemcpy(tmp, data, numel * 4, kind));
+      sf_make_w3_kernel<<<grid_for((long long)numel), 256>>>(
+          tmp, static_cast<uint16_t*>(e.dst), e.N, e.K, e.kind == Impl::kLinPerm ? kCh : 0, kF2);
+      ORX_CHECK(cudaGetLastError());
+      ORX_CHECK(cudaDeviceSynchronize());
+      cudaFree(tmp);
+    }
+    p.have[i] = true;
+    return;
+  }
+  throw std::invalid_argument("unknown Sortformer tensor " + name);
+}
+
+void Sortformer::load_safetensors(const std::string& path) {
+  SafeTensorsFile f(path);
+  for (const auto& kv : f.tensors()) {
+    if (kv.second.dtype != "F32") continue;
+    bool known = false;
+    for (const auto& e : p_->entries)
+      if (e.name == kv.first) known = true;
+    if (!known) continue;  // tensors of other modules, or of layers beyond the configured counts
+    set_tensor(kv.first, static_cast<const float*>(kv.second.data), kv.second.nbytes / 4, false);
+  }
+  if (!complete()) throw std::invalid_argument("checkpoint is missing Sortformer tensors");
+}
+
+void Sortformer::init_synthetic(int seed) {
+  Impl& p = *p_;
+  size_t big = 0;
+  for (const auto& e : p.entries) big = std::max(big, e.numel);
+  float* tmp = dalloc<float>(big);
+  for (size_t i = 0; i < p.entries.size(); ++i) {
+    const auto& e = p.entries[i];
+    const int tid = 90000 + static_cast<int>(i);
+    double sd = 0.02;
+    float mean = 0.f;
+    if (e.fan_in) sd = 1.0 / std::sqrt(static_cast<double>(e.fan_in));
+    else if (e.tkind == 2) mean = 1.f;
+    else if (e.tkind == 3) sd = 0.1;
+    launch_synth_f32(tmp, (long long)e.numel, seed, tid, sd, mean, 0, 0);
+    ORX_CHECK(cudaGetLastError());
+    if (e.tkind == 3) {  // running variance 1 + |N(0, 0.1^2)|
+      std::vector<float> h(e.numel);
+      ORX_CHECK(cudaMemcpy(h.data(), tmp, e.numel * 4, cudaMemcpyDeviceToHost));
+      for (auto& v : h) v = 1.0f + std::fabs(v);
+      ORX_CHECK(cudaMemcpy(tmp, h.data(), e.numel * 4, cudaMemcpyHostToDevice));
+    }
+    set_tensor(e.name, tmp, e.numel, true);
+  }
+  cudaFree(tmp);
+}
+
+int Sortformer::pre_encode_device(const float* d_mel, int n_frames, int valid, float* d_out,
+                                  int* valid_out, cudaStream_t s) {
+  Impl& p = *p_;
+  if (!complete()) throw std::invalid_argument("Sortformer weights are incomplete");
+  if (n_frames <= 0) throw std::invalid_argument("n_frames must be positive");
+  valid = std::max(0, std::min(valid, n_frames));
+  const int H0 = conv_len(n_frames), H1 = conv_len(H0), H2 = conv_len(H1);
+  const int v0 = conv_len(valid), v1 = conv_len(v0), v2 = conv_len(v1);
+  float* a = p.b_a.get<float>((size_t)H0 * kF0 * kCh);
+  uint16_t* sp = p.b_s1.get<uint16_t>((size_t)H1 * kF1 * 3 * kCh);
+  float* b = p.b_b.get<float>((size_t)H1 * kF1 * kCh);
+  sf_conv0_kernel<<<H0, 256, 0, s>>>(d_mel, n_frames, valid, p.c0w, p.c0b, v0, a);
+  check(cudaGetLastError(), "sortformer conv0");
+  sf_dwconv_kernel<<<grid_for((long long)H1 * kF1 * kCh), 256, 0, s>>>(a, H0, kF0, v0, p.c2w, p.c2b,
+                                                                      H1, kF1, sp);
+  check(cudaGetLastError(), "sortformer dwconv");
+  p.gemm(sp, p.c3w, H1 * kF1, kCh, kCh, p.c3b, 2, b, nullptr, 0, s);
+  sf_dwconv_kernel<<<grid_for((long long)H2 * kF2 * kCh), 256, 0, s>>>(b, H1, kF1, v1, p.c5w, p.c5b,
+                                                                      H2, kF2, sp);
+  check(cudaGetLastError(), "sortformer dwconv");
+  p.gemm(sp, p.c6w, H2 * kF2, kCh, kCh, p.c6b, 2, a, nullptr, 0, s);  // [H2][16][256] = [H2][4096]
+  uint16_t* fs = p.b_s2.get<uint16_t>((size_t)H2 * 3 * kCh * kF2);
+  sf_split_kernel<<<grid_for((long long)H2 * kCh * kF2), 256, 0, s>>>(a, fs, H2, kCh * kF2, 0, v2);
+  check(cudaGetLastError(), "sortformer split");
+  p.gemm(fs, p.outw, H2, kCh * kF2, kD, p.outb, 0, d_out, nullptr, 0, s);
+  if (valid_out) *valid_out = v2;
+  return H2;
+}
+
+void Sortformer::encode_decode_device(const float* d_emb, int T, int valid, float* d_preds,
+                                      cudaStream_t s) {
+  Impl& p = *p_;
+  if (!complete()) throw std::invalid_argument("Sortformer weights are incomplete");
+  if (T <= 0) throw std::invalid_argument("T must be positive");
+  valid = std::max(0, std::min(valid, T));
+  const int P = 2 * T - 1;
+  float* x = p.b_x.get<float>((size_t)T * kD);
+  uint16_t* s1 = p.b_s1.get<uint16_t>((size_t)T * 3 * kDff);
+  uint16_t* s2 = p.b_s2.get<uint16_t>((size_t)T * 3 * kDff);
+  float* qkv = p.b_qkv.get<float>((size_t)T * 3 * kD);
+  float* pp = p.b_p.get<float>((size_t)P * kD);
+  float* big = p.b_big.get<float>((size_t)T * 2 * kD);
+  // relative positional encoding (ConformerLayer::BuildPosEmb), in fp32 as
+  // the reference computes it, cached per T
+  if (p.pe_T != T) {
+    p.pe_host.assign((size_t)P * kD, 0.f);
+    for (int idx = 0; idx < P; ++idx) {
+      const float pos = static_cast<float>(T - 1 - idx);
+      for (int i = 0; i < kD; i += 2) {
+        const float div = std::exp(-(std::log(10000.0f)) * static_cast<float>(i) / kD);
+        p.pe_host[(size_t)idx * kD + i] = std::sin(pos * div);
+        p.pe_host[(size_t)idx * kD + i + 1] = std::cos(pos * div);
+      }
+    }
+    float* pe = p.b_pe.get<float>((size_t)P * kD);
+    ORX_CHECK(cudaMemcpyAsync(pe, p.pe_host.data(), (size_t)P * kD * 4, cudaMemcpyHostToDevice, s));
+    uint16_t* pes = p.b_pes.get<uint16_t>((size_t)P * 3 * kD);
+    sf_split_kernel<<<grid_for((long long)P * kD), 256, 0, s>>>(pe, pes, P, kD, 0, P);
+    check(cudaGetLastError(), "sortformer split");
+    ORX_CHECK(cudaStreamSynchronize(s));  // the host table is reused next call
+    p.pe_T = T;
+  }
+  const uint16_t* pes = static_cast<const uint16_t*>(p.b_pes.p);
+  sf_scale_kernel<<<grid_for((long long)T * kD), 256, 0, s>>>(d_emb, x, (long long)T * kD,
+                                                              std::sqrt(static_cast<float>(kD)));
+  check(cudaGetLastError(), "sortformer scale");
+  const dim3 agrid((T + kAr - 1) / kAr, kHeads);
+  for (int li = 0; li < p.L; ++li) {
+    const Impl::Conf& c = p.C[li];
+    p.ln(x, c.ln1g, c.ln1b, nullptr, s1, T, kD, s);
+    p.gemm(s1, c.ff1w1, T, kD, kDff, c.ff1b1, 3, nullptr, s2, 0, s);
+    p.gemm(s2, c.ff1w2, T, kDff, kD, c.ff1b2, 0, x, nullptr, 2, s);
+    p.ln(x, c.lnag, c.lnab, nullptr, s1, T, kD, s);
+    p.gemm(s1, c.qkvw, T, kD, 3 * kD, c.qkvb, 0, qkv, nullptr, 0, s);
+    p.gemm(pes, c.posw, P, kD, kD, nullptr, 0, pp, nullptr, 0, s);
+    sf_relattn_kernel<<<agrid, kAr * 32, 0, s>>>(qkv, pp, c.bu, c.bv, T, valid, s2);
+    check(cudaGetLastError(), "sortformer attention");
+    p.gemm(s2, c.ow, T, kD, kD, c.ob, 0, x, nullptr, 1, s);
+    p.ln(x, c.lncg, c.lncb, nullptr, s1, T, kD, s);
+    p.gemm(s1, c.pw1w, T, kD, 2 * kD, c.pw1b, 0, big, nullptr, 0, s);
+    sf_convmod_kernel<<<grid_for((long long)T * kD), 256, 0, s>>>(big, T, valid, c.dww, c.dwb, c.bnm,
+                                                                  c.bnv, c.bng, c.bnb, s2);
+    check(cudaGetLastError(), "sortformer conv module");
+    p.gemm(s2, c.pw2w, T, kD, kD, c.pw2b, 0, x, nullptr, 1, s);
+    p.ln(x, c.ln2g, c.ln2b, nullptr, s1, T, kD, s);
+    p.gemm(s1, c.ff2w1, T, kD, kDff, c.ff2b1, 3, nullptr, s2, 0, s);
+    p.gemm(s2, c.ff2w2, T, kDff, kD, c.ff2b2, 0, x, nullptr, 2, s);
+    p.ln(x, c.lnog, c.lnob, x, nullptr, T, kD, s);
+  }
+  // ---- decoder ----
+  float* xd = big;  // [T][192]
+  sf_split_kernel<<<grid_for((long long)T * kD), 256, 0, s>>>(x, s1, T, kD, 0, T);
+  check(cudaGetLastError(), "sortformer split");
+  p.gemm(s1, p.projw, T, kD, kDD, p.projb, 0, xd, nullptr, 0, s);
+  sf_split_kernel<<<grid_for((long long)T * kDD), 256, 0, s>>>(xd, s1, T, kDD, 0, T);
+  check(cudaGetLastError(), "sortformer split");
+  const dim3 dgrid((T + kAr - 1) / kAr, kDHeads);
+  for (int li = 0; li < p.DL; ++li) {
+    const Impl::Dec& d = p.Dl[li];
+    p.gemm(s1, d.qkvw, T, kDD, 3 * kDD, d.qkvb, 0, qkv, nullptr, 0, s);
+    sf_attn_kernel<<<dgrid, kAr * 32, 0, s>>>(qkv, T, valid, s2);
+    check(cudaGetLastError(), "sortformer decoder attention");
+    p.gemm(s2, d.ow, T, kDD, kDD, d.ob, 0, xd, nullptr, 1, s);
+    p.ln(xd, d.ln1g, d.ln1b, xd, s1, T, kDD, s);
+    p.gemm(s1, d.inw, T, kDD, kDDff, d.inb, 2, nullptr, s2, 0, s);
+    p.gemm(s2, d.outw, T, kDDff, kDD, d.outb, 0, xd, nullptr, 1, s);
+    p.ln(xd, d.ln2g, d.ln2b, xd, s1, T, kDD, s);
+  }
+  sf_split_kernel<<<grid_for((long long)T * kDD), 256, 0, s>>>(xd, s1, T, kDD, 1, T);
+  check(cudaGetLastError(), "sortformer split");
+  p.gemm(s1, p.hidw, T, kDD, kDD, p.hidb, 2, nullptr, s2, 0, s);
+  p.gemm(s2, p.spkw, T, kDD, kSpk, p.spkb, 4, d_preds, nullptr, 0, s);
+  sf_mask_rows_kernel<<<grid_for((long long)T * kSpk), 256, 0, s>>>(d_preds, T, kSpk, valid);
+  check(cudaGetLastError(), "sortformer mask");
+}
+
+int Sortformer::step_device(const float* d_mel, int n_frames, int valid, const float* d_cache,
+                            int n_cache, float* d_preds, int* valid_out, cudaStream_t s) {
+  Impl& p = *p_;
+  if (n_cache < 0) throw std::invalid_argument("cache rows must be >= 0");
+  const int H2 = conv_len(conv_len(conv_len(n_frames)));
+  float* emb = p.b_emb.get<float>((size_t)(n_cache + H2) * kD);
+  if (n_cache > 0)
+    ORX_CHECK(cudaMemcpyAsync(emb, d_cache, (size_t)n_cache * kD * 4, cudaMemcpyDeviceToDevice, s));
+  int v2 = 0;
+  pre_encode_device(d_mel, n_frames, valid, emb + (size_t)n_cache * kD, &v2, s);
+  const int T = n_cache + H2, vcat = n_cache + v2;
+  encode_decode_device(emb, T, vcat, d_preds, s);
+  if (valid_out) *valid_out = vcat;
+  return T;
+}
+
+int Sortformer::device_error() const {
+  int e = 0;
+  ORX_CHECK(cudaMemcpy(&e, p_->err, sizeof(int), cudaMemcpyDeviceToHost));
+  return e;
+}
+
+}  // namespace orx

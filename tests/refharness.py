@@ -125,3 +125,49 @@ class RefTower:
         if self.h:
             self.L.ref_tower_destroy(self.h)
             self.h = None
+
+
+class RefSortformer:
+    """The reference's ConformerPreEncode / ConformerLayer / SortformerDecoder
+    (src/model/conformer_preencode.cu, conformer_layer.cu, sortformer_decoder.cu),
+    unmodified, from one F32 safetensors file."""
+
+    def __init__(self, path: str, conf_layers: int, dec_layers: int):
+        L = C.CDLL(LIB)
+        L.ref_sf_create.restype = C.c_void_p
+        L.ref_sf_create.argtypes = [C.c_char_p, C.c_int, C.c_int]
+        L.ref_sf_destroy.argtypes = [C.c_void_p]
+        L.ref_sf_preencode.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                       C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.ref_sf_encdec.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.ref_last_error.restype = C.c_char_p
+        h = L.ref_sf_create(path.encode(), conf_layers, dec_layers)
+        if not h:
+            raise RuntimeError(L.ref_last_error().decode())
+        self.L, self.h = L, C.c_void_p(h)
+
+    def pre_encode(self, mel, valid):
+        mel = np.ascontiguousarray(mel, np.float32)
+        n = mel.shape[1]
+        T2 = n
+        for _ in range(3):
+            T2 = (T2 + 2 - 3) // 2 + 1
+        out = np.empty((T2, 512), np.float32)
+        t, v = C.c_int(), C.c_int()
+        assert self.L.ref_sf_preencode(self.h, mel.ctypes.data_as(C.c_void_p), 128, n, valid,
+                                       out.ctypes.data_as(C.c_void_p), C.byref(t), C.byref(v)) == 0
+        assert t.value == T2
+        return out, v.value
+
+    def encode_decode(self, emb, valid):
+        emb = np.ascontiguousarray(emb, np.float32)
+        T = emb.shape[0]
+        out = np.empty((T, 4), np.float32)
+        assert self.L.ref_sf_encdec(self.h, emb.ctypes.data_as(C.c_void_p), T, valid,
+                                    out.ctypes.data_as(C.c_void_p)) == 0
+        return out
+
+    def close(self):
+        if self.h:
+            self.L.ref_sf_destroy(self.h)
+            self.h = None
