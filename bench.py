@@ -392,8 +392,8 @@ def run_config1(torch, hbm, cpu: bool):
                        "(KV 513 fp32), seed 0, B=1",
            "gpu_us_per_step": us, "bytes_per_step": nbytes,
            "achieved_gbs": nbytes / (us * 1e-6) / 1e9, "frac": nbytes / (us * 1e-6) / 1e9 / hbm,
-           "note": "6 launches per row (norm+qkv GEMV, q/k norm+RoPE+KV store, attention, "
-                   "o GEMV, norm+gate/up GEMV, down GEMV), median of 100 reps, L2 not flushed"}
+           "note": "5 launches per row chained by programmatic dependent launch (norm+qkv GEMV, "
+                   "attention with q/k norm+RoPE+KV store, o GEMV, norm+gate/up GEMV, down GEMV), median of 100 reps, L2 not flushed"}
     if cpu:
         from oracle import decoder_oracle as D
         threads = os.cpu_count() or 1

@@ -150,3 +150,19 @@ def test_full_size_step_vs_reference(cuda, tmp_path):
         r.close()
         m.close()
         m2.close()
+
+
+def test_oracle_pinned_to_reference(weights, ref):
+    """The CPU restatement against the reference's own CUDA classes on the
+    same weights and inputs: the oracle's pin."""
+    o = SO.SortformerOracle(weights, CL, DL)
+    mel = SO.synthetic_mel(6, 300)
+    e_o, _, v_o = o.pre_encode(mel, 260)
+    e_r, v_r = ref.pre_encode(mel, 260)
+    assert v_o == v_r
+    note("pre_encode oracle vs reference", rel(e_o, e_r))
+    assert rel(e_o, e_r) <= EMB_TOL
+    emb = SO.synth.normal_f32(6, 92500, 120 * 512, 1.0).reshape(120, 512)
+    p_o, p_r = o.encode_decode(emb, 100), ref.encode_decode(emb, 100)
+    note("encode_decode oracle vs reference", float(np.abs(p_o - p_r).max()))
+    assert np.abs(p_o - p_r).max() <= PRED_TOL

@@ -190,3 +190,17 @@ def test_full_depth_vs_reference(cuda, tmp_path):
         ref.close()
         t.close()
         t2.close()
+
+
+@pytest.mark.parametrize("n", [350, 57])
+def test_oracle_pinned_to_reference(weights, ref_dir, n):
+    """The CPU restatement against the reference's own AsrAudioTower (run on
+    this GPU) on the same checkpoint and mel: the oracle's pin."""
+    if not refharness.available():
+        pytest.skip("reference build (oracle/_ref) absent")
+    ref = refharness.RefTower(ref_dir, LAYERS)
+    try:
+        mel = mel_for(n)
+        close(TO.TowerOracle(weights, LAYERS).forward(mel), ref.forward(mel), f"oracle vs reference n={n}")
+    finally:
+        ref.close()
