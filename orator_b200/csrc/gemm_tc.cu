@@ -251,74 +251,100 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
           }
           asm volatile("bar.sync 1, 128;" ::: "memory");
           if (rloc < 64) {
+            const int lim = min(min(32, BN - c0), g.T - (n0 + c0));
+            uint16_t* po = g.out_bf16 + (long long)(n0 + c0) * g.ldo + (m0 >> 1) + rloc;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int t = n0 + c0 + i;
-              if (c0 + i < BN && t < g.T) {
+            for (int i = 0; i < 32; ++i)
+              if (i < lim) {
                 const float gt = v[i], up = sm.swap[rloc][i];
-                g.out_bf16[(long long)t * g.ldo + (m0 >> 1) + rloc] =
-                    f2bf((gt / (1.0f + expf(-gt))) * up);
+                po[(long long)i * g.ldo] = f2bf((gt / (1.0f + expf(-gt))) * up);
               }
-            }
           }
         } else if (g.epi == kEpiLinear) {
-          if (row < g.N) {
+          // Straight-line per mode: the activation and the output kind are
+          // chosen once per 32-column chunk, stores are predicated.
+          const int lim = min(min(32, BN - c0), g.T - (n0 + c0));
+          if (row < g.N && lim > 0) {
             const float bv = g.bias ? g.bias[row] : 0.f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int t = n0 + c0 + i;
-              float y = v[i] + bv;
-              if (g.act == 1)
-                y = 0.5f * y * (1.0f + erff(y * 0.70710678118654752440f));
-              else if (g.act == 2)
-                y = fmaxf(y, 0.0f);
-              else if (g.act == 3)
-                y = y / (1.0f + expf(-y));
-              else if (g.act == 4)
-                y = 1.0f / (1.0f + expf(-y));
-              if (c0 + i < BN && t < g.T) {
-                const long long o = (long long)t * g.ldo + row;
-                if (g.out_bf16) {
-                  const uint16_t hi = f2bf(y);
-                  g.out_bf16[o] = hi;
-                  if (g.split3) {  // [hi | hi | lo] operand of the next fp32-grade GEMM
-                    g.out_bf16[o + g.N] = hi;
-                    g.out_bf16[o + 2 * g.N] = f2bf(y - bf2f(hi));
+            for (int i = 0; i < 32; ++i) v[i] += bv;
+            switch (g.act) {
+              case 1:
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  v[i] = 0.5f * v[i] * (1.0f + erff(v[i] * 0.70710678118654752440f));
+                break;
+              case 2:
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
+                break;
+              case 3:
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = v[i] / (1.0f + expf(-v[i]));
+                break;
+              case 4:
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 1.0f / (1.0f + expf(-v[i]));
+                break;
+              default:
+                break;
+            }
+            const long long base = (long long)(n0 + c0) * g.ldo + row;
+            if (g.out_bf16) {
+              uint16_t* po = g.out_bf16 + base;
+              if (g.split3) {  // [hi | hi | lo] operand of the next fp32-grade GEMM
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (i < lim) {
+                    const uint16_t hi = f2bf(v[i]);
+                    uint16_t* q = po + (long long)i * g.ldo;
+                    q[0] = hi;
+                    q[g.N] = hi;
+                    q[2 * g.N] = f2bf(v[i] - bf2f(hi));
                   }
-                } else if (g.resid == 2) {
-                  g.out_f32[o] += 0.5f * y;
-                } else if (g.resid) {
-                  g.out_f32[o] += y;
-                } else {
-                  g.out_f32[o] = y;
-                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (i < lim) po[(long long)i * g.ldo] = f2bf(v[i]);
+              }
+            } else {
+              float* po = g.out_f32 + base;
+              if (g.resid) {
+                const float sc = g.resid == 2 ? 0.5f : 1.0f;
+                float r[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = i < lim ? po[(long long)i * g.ldo] : 0.f;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (i < lim) po[(long long)i * g.ldo] = r[i] + sc * v[i];
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (i < lim) po[(long long)i * g.ldo] = v[i];
               }
             }
           }
         } else {
           float r[32];
+          const int lim = min(min(32, BN - c0), g.T - (n0 + c0));
+          float* po = g.out_f32 + (long long)(n0 + c0) * g.ldo + row;
+          const bool rd = g.epi == kEpiResid;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int t = n0 + c0 + i;
-            r[i] = (g.epi == kEpiResid && c0 + i < BN && t < g.T)
-                       ? g.out_f32[(long long)t * g.ldo + row] : 0.f;
-          }
+          for (int i = 0; i < 32; ++i) r[i] = (rd && i < lim) ? po[(long long)i * g.ldo] : 0.f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int t = n0 + c0 + i;
-            if (c0 + i < BN && t < g.T) g.out_f32[(long long)t * g.ldo + row] = r[i] + v[i];
-          }
+          for (int i = 0; i < 32; ++i)
+            if (i < lim) po[(long long)i * g.ldo] = r[i] + v[i];
         }
       };
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
         tmem_ld32(tbase + c0, v);
         if (splits > 1) {
+          const int lim = min(min(32, BN - c0), g.T - (n0 + c0));
+          float* pw = g.ws + ((long long)kz * g.T + n0 + c0) * g.N + row;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int t = n0 + c0 + i;
-            if (c0 + i < BN && t < g.T) g.ws[((long long)kz * g.T + t) * g.N + row] = v[i];
-          }
+          for (int i = 0; i < 32; ++i)
+            if (i < lim) pw[(long long)i * g.N] = v[i];
         } else {
           finish(v, c0);
         }
