@@ -59,11 +59,6 @@ void GemmWs::reserve(size_t floats, cudaStream_t s) {
   ++gen;
 }
 
-// The in-kernel split-K fixup (gemm_tc.cu) measured slower than the separate
-// reduction kernel at prefill sizes (12.5 vs 5.3 ms for config 2's prefill),
-// so the reduction kernel stays the default.
-constexpr bool kFixup = false;
-
 void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int T, int epi,
               float* out_f32, uint16_t* out_bf16, int ldo, int* err, int num_sms, cudaStream_t s,
               const float* norm_w, uint16_t* norm_out, float eps) {
@@ -73,8 +68,6 @@ void run_proj(GemmWs& w, const uint16_t* X, const uint16_t* W, int N, int K, int
   if (splits > 1) {
     w.reserve((size_t)splits * T * N, s);
     g.ws = w.ws;
-    const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
-    if (kFixup && (long long)((N + 127) / 128) * ((T + bn - 1) / bn) <= GemmWs::kTickets) g.tile_cnt = w.cnt;
   }
   launch_gemm_tc(X, W, g, splits, s);
 }

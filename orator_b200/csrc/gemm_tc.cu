@@ -12,13 +12,12 @@
 //   * warp 1 / one lane: MMA issuer — 4 x tcgen05.mma (K = 16 each) per stage
 //     into a TMEM accumulator of BN fp32 columns, tcgen05.commit releases the
 //     stage;
-//   * 4 epilogue warps: tcgen05.ld of their 32 TMEM lanes (= 32 weight
-//     rows), then fp32 store, residual add, SwiGLU on [64 gate | 64 up] tiles
-//     with the bf16 cast of the reference, or bias + GELU / ReLU (Linear);
-//     with split K they write fp32 partials, and the CTA that finishes a
-//     tile's last split sums them in split order and runs the epilogue
-//     (deterministic; a separate reduction kernel when no ticket array is
-//     given).
+//   * 8 epilogue warps (two per 32-lane TMEM quarter, one for the even and
+//     one for the odd 32-column chunks): tcgen05.ld of their 32 TMEM lanes
+//     (= 32 weight rows), then fp32 store, residual add, SwiGLU on
+//     [64 gate | 64 up] tiles with the bf16 cast of the reference, or bias +
+//     GELU / ReLU (Linear); with split K they write fp32 partials, summed in
+//     split order by a reduction kernel (deterministic).
 // Replaces Bf16WmmaKernel2 (include/model/gemm.cuh:394-459) and the
 // F32ToBf16 / AddResidual / SwiGLU launches around it.
 // No TMA multicast anywhere: every CTA loads its own tiles.
@@ -99,15 +98,17 @@ struct TcSmem {
   uint64_t acc_full[2];   // MMA -> epilogue: accumulator buffer ready
   uint64_t acc_empty[2];  // epilogue -> MMA: accumulator buffer drained
   uint32_t tmem_base;
-  int fix_last;           // split-K fixup: this CTA holds the tile's last split
-  float swap[64][33];     // SwiGLU: up rows handed to the gate-row warps
+  // SwiGLU, per column half of the epilogue: up rows handed to the gate-row
+  // threads, gate rows of columns 16-31 handed to the up-row threads
+  float swap_up[2][64][33];
+  float swap_gate[2][64][17];
 };
 
 // Persistent, warp-specialised GEMM. Work items (m tile, n tile, k split) are
 // strided over the CTAs; warp 0 streams TMA stages continuously across items,
 // warp 1 issues the MMAs into one of two TMEM accumulators, and warps 2-5 run
 // the epilogue of item i while the MMAs of item i + 1 proceed.
-constexpr int kTcWarps = 6;
+constexpr int kTcWarps = 10;  // producer, MMA, 8 epilogue warps (two per TMEM lane quarter)
 constexpr int kTcThreadsP = kTcWarps * 32;
 
 template <int BN, int STAGES>
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
       }
       for (int b = 0; b < 2; ++b) {
         mbar_init(&sm.acc_full[b], 1);
-        mbar_init(&sm.acc_empty[b], 4);  // one arrival per epilogue warp
+        mbar_init(&sm.acc_empty[b], 8);  // one arrival per epilogue warp
       }
       fence_mbar_init();
     }
@@ -226,11 +227,12 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
       }
     }
   } else {
-    // ---- epilogue warps 2..5: TMEM lane quarter = warp % 4 ----
+    // ---- epilogue warps 2..9: TMEM lane quarter = warp % 4; warps 2-5
+    // drain the even 32-column chunks, warps 6-9 the odd ones ----
     pdl_wait();
     const int quarter = warp & 3;
-    const int ew = warp - 2;  // 0..3 for the named barrier
-    (void)ew;
+    const int half = (warp - 2) >> 2;
+    const int bar_id = 1 + half;  // named barrier of this half's 128 threads
     int j = 0;
     for (int it = blockIdx.x; it < items; it += gridDim.x, ++j) {
       int m0, n0, kz;
@@ -244,19 +246,32 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
       // Output stage of 32 finished accumulator columns (tokens n0 + c0 ..).
       auto finish = [&](float* v, int c0) {
         if (g.epi == kEpiSwiglu) {
-          asm volatile("bar.sync 1, 128;" ::: "memory");
+          // gate row j pairs with up row j + 64; the gate-row threads finish
+          // columns 0-15 of the chunk, the up-row threads columns 16-31
+          asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
           if (rloc >= 64) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) sm.swap[rloc - 64][i] = v[i];
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (rloc < 64) {
-            const int lim = min(min(32, BN - c0), g.T - (n0 + c0));
-            uint16_t* po = g.out_bf16 + (long long)(n0 + c0) * g.ldo + (m0 >> 1) + rloc;
+            for (int i = 0; i < 32; ++i) sm.swap_up[half][rloc - 64][i] = v[i];
+          } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
+            for (int i = 16; i < 32; ++i) sm.swap_gate[half][rloc][i - 16] = v[i];
+          }
+          asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+          const int lim = min(min(32, BN - c0), g.T - (n0 + c0));
+          const int jr = rloc & 63;
+          uint16_t* po = g.out_bf16 + (long long)(n0 + c0) * g.ldo + (m0 >> 1) + jr;
+          if (rloc < 64) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
               if (i < lim) {
-                const float gt = v[i], up = sm.swap[rloc][i];
+                const float gt = v[i], up = sm.swap_up[half][jr][i];
+                po[(long long)i * g.ldo] = f2bf((gt / (1.0f + expf(-gt))) * up);
+              }
+          } else {
+#pragma unroll
+            for (int i = 16; i < 32; ++i)
+              if (i < lim) {
+                const float gt = sm.swap_gate[half][jr][i - 16], up = v[i];
                 po[(long long)i * g.ldo] = f2bf((gt / (1.0f + expf(-gt))) * up);
               }
           }
@@ -336,7 +351,7 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
             if (i < lim) po[(long long)i * g.ldo] = r[i] + v[i];
         }
       };
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = half * 32; c0 < BN; c0 += 64) {
         float v[32];
         tmem_ld32(tbase + c0, v);
         if (splits > 1) {
@@ -352,35 +367,6 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
-      if (splits > 1 && g.tile_cnt) {
-        // Split-K fixup: the CTA that stores the tile's last partial sums all
-        // of them in split order (the same result whichever CTA is last)
-        // and runs the epilogue; the ticket is reset for the next launch.
-        const int tile = it / splits;
-        __threadfence();  // this thread's partial stores before the ticket
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (threadIdx.x == 64) {
-          sm.fix_last = atomicAdd(&g.tile_cnt[tile], 1) == splits - 1;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (sm.fix_last) {
-          __threadfence();
-          for (int c0 = 0; c0 < BN; c0 += 32) {
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-            for (int z = 0; z < splits; ++z) {  // 32 loads in flight per split
-              const float* pz = g.ws + ((long long)z * g.T + n0 + c0) * g.N + row;
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (c0 + i < BN && n0 + c0 + i < g.T) v[i] += __ldcg(pz + (long long)i * g.N);
-            }
-            finish(v, c0);
-          }
-          if (threadIdx.x == 64) g.tile_cnt[tile] = 0;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // fix_last is reused by the next item
-      }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -567,9 +553,7 @@ void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int s
     fprintf(stderr, "orx: fused RMSNorm needs residual rows of 2048\n");
     return;
   }
-  if (splits > 1 && g.tile_cnt) {
-    if (norm) launch_rmsnorm_bf16(g.out_f32, g.norm_w, g.norm_out, g.T, g.eps, s);
-  } else if (splits > 1) {
+  if (splits > 1) {
     const long long n = (long long)g.T * g.N;
     const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, 148 * 16));
     if (g.epi == kEpiSwiglu)

@@ -148,9 +148,6 @@ struct TcArgs {
   int act;
   int resid;
   int split3;
-  // Split-K fixup tickets, one int per (m tile, token tile), zero between
-  // launches (the fixup resets them). nullptr: a reduction kernel instead.
-  int* tile_cnt;
 };
 // X: [T, K] bf16 row-major (device), W: [N, K] bf16. splits divides K / 64.
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
