@@ -20,20 +20,23 @@ GemmWs::~GemmWs() {
 int proj_splits(int N, int K, int T, int num_sms) {
   const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   const int tiles = (N / 128) * ((T + bn - 1) / bn);
-  // Split-K by a small cost model of the persistent GEMM: rounds of items per
-  // CTA x k-blocks per item x time per k-block (weight + activation bytes at
-  // the per-SM share of HBM bandwidth, or the tensor time of the tile), plus
-  // the reduce kernel's extra traffic and launch.
+  // Split-K by a small cost model of the persistent GEMM, calibrated on B200
+  // (64, 400 and 3200 token rows): rounds of items per CTA x k-blocks per item
+  // x time per k-block, the largest of (a) the weight box at the CTA's share
+  // of HBM bandwidth (about 55 GB/s per streaming CTA at most), (b) weight +
+  // activation boxes at about 120 GB/s of L2-to-SM bandwidth, (c) the tensor
+  // time of the tile; plus the reduction kernel, which reads and writes the
+  // fp32 partials at about 3 TB/s and costs a launch.
   auto cost = [&](int sp) {
     const int items = tiles * sp, active = items < num_sms ? items : num_sms;
     const double rounds = (items + num_sms - 1) / num_sms;
     const double kb = K / 64.0 / sp;
-    const double bytes = (128.0 + bn) * 64 * 2;
-    const double per_sm_bw = std::min(6.4e12 / active, 55e9);  // measured per-CTA stream rate
-    const double t_mem = bytes / per_sm_bw;
-    const double t_mma = 2.0 * 128 * bn * 64 / 10.8e12;
-    const double red = sp > 1 ? (sp * 8.0 * T * N) / 6.4e12 + 3e-6 : 0.0;
-    return rounds * kb * std::max(t_mem, t_mma) + red;
+    const double w_bytes = 128.0 * 64 * 2, x_bytes = bn * 64 * 2.0;
+    const double per_sm_hbm = std::min(6.4e12 / active, 55e9);
+    const double t_unit = std::max({w_bytes / per_sm_hbm, (w_bytes + x_bytes) / 120e9,
+                                    2.0 * 128 * bn * 64 / 10.8e12});
+    const double red = sp > 1 ? (sp * 8.0 * T * N) / 3e12 + 4e-6 : 0.0;
+    return rounds * kb * t_unit + red;
   };
   int splits = 1;
   for (int sp = 2; sp <= 16; sp *= 2)
