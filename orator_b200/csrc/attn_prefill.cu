@@ -37,7 +37,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(pf_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar[kSlots];
-  const int tile = blockIdx.x, h = blockIdx.y;
+  // items in tile-major order (tiles arrive longest-first): blocks of one
+  // launch wave take whole tiles, heaviest first
+  const int tile = blockIdx.x / kKvHeads, h = blockIdx.x % kKvHeads;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const PrefillTile ti = a.tiles[tile];
   const int* pt = a.page_table + (long long)ti.tab * a.max_pages;
@@ -261,7 +263,7 @@ void launch_attn_prefill(const PrefillAttnArgs& a, int ntiles, const uint16_t* k
   });
   CUtensorMap map;
   if (!make_tmap_2d(&map, kv_pool, pool_rows, kHeadDim, 64, kPage)) return;
-  launch_pdl(attn_prefill_kernel, dim3(ntiles, kKvHeads), dim3(kPfThreads), kPfSmem, s, map, a);
+  launch_pdl(attn_prefill_kernel, dim3(ntiles * kKvHeads), dim3(kPfThreads), kPfSmem, s, map, a);
 }
 
 int prefill_tile_rows() { return kPfRows; }

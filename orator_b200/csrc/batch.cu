@@ -419,6 +419,11 @@ void BatchDecoder::prefill(const int* sids, const int* lens, int n, const float*
         tiles.push_back({sids[i], base + t0, std::min(tr, lens[i] - t0), row + t0});
       row += lens[i];
     }
+    // longest key range first: the launch's first wave takes the heaviest
+    // (tile, head) items and the short ones fill in behind them
+    std::stable_sort(tiles.begin(), tiles.end(), [](const PrefillTile& x, const PrefillTile& y) {
+      return x.pos0 + x.nrows > y.pos0 + y.nrows;
+    });
     ntiles_ = static_cast<int>(tiles.size());
     if (ntiles_ > tiles_cap_) {
       if (d_tiles_) cudaFree(d_tiles_);

@@ -195,8 +195,10 @@ void Decoder::forward_prefill(int T, int pos0, cudaStream_t s) {
     tiles_cap_ = ntiles;
   }
   ORX_CHECK(cudaStreamSynchronize(s));  // h_tiles_ may still feed an earlier copy
-  for (int i = 0; i < ntiles; ++i)
-    h_tiles_[i] = {0, pos0 + i * tr, std::min(tr, T - i * tr), i * tr};
+  for (int i = 0; i < ntiles; ++i) {  // longest key range first (see the batched prefill)
+    const int k = ntiles - 1 - i;
+    h_tiles_[i] = {0, pos0 + k * tr, std::min(tr, T - k * tr), k * tr};
+  }
   ORX_CHECK(cudaMemcpyAsync(d_tiles_, h_tiles_, sizeof(PrefillTile) * ntiles,
                             cudaMemcpyHostToDevice, s));
   for (int l = 0; l < c.num_layers; ++l) {
