@@ -18,8 +18,6 @@ GemmWs::~GemmWs() {
 }
 
 int proj_splits(int N, int K, int T, int num_sms) {
-  const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
-  const int tiles = (N / 128) * ((T + bn - 1) / bn);
   // Split-K by a small cost model of the persistent GEMM, calibrated on B200
   // (64, 400 and 3200 token rows): rounds of items per CTA x k-blocks per item
   // x time per k-block, the largest of (a) the weight box at the CTA's share
@@ -28,6 +26,8 @@ int proj_splits(int N, int K, int T, int num_sms) {
   // time of the tile; plus the reduction kernel, which reads and writes the
   // fp32 partials at about 3 TB/s and costs a launch.
   auto cost = [&](int sp) {
+    const int bn = tc_token_tile(N, T, sp, num_sms);
+    const int tiles = (N / 128) * ((T + bn - 1) / bn);
     const int items = tiles * sp, active = items < num_sms ? items : num_sms;
     const double rounds = (items + num_sms - 1) / num_sms;
     const double kb = K / 64.0 / sp;

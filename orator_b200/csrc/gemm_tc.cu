@@ -122,8 +122,10 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
   const int mt = (g.N + 127) / 128, nt = (g.T + BN - 1) / BN;
   const int items = mt * nt * splits;
   const int kper = g.K / splits, KT = (kper + kBK - 1) / kBK;
-  constexpr int kTmemCols = 2 * (BN < 32 ? 32 : BN);  // two accumulators
-  constexpr int kAccCols = kTmemCols / 2;
+  // two accumulators of BN columns; the allocation is a power of two >= 32
+  constexpr int kAccCols = BN < 32 ? 32 : BN;
+  constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128
+                          : 2 * kAccCols <= 256 ? 256 : 512;
   int* err = g.err;
 
   if (warp == 0) {
@@ -526,10 +528,35 @@ bool make_tmap_2d(void* map, const void* base, long long rows, int cols, int box
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+int tc_sms() {
+  static int sms_of[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& v = sms_of[dev & 63];
+  if (v <= 0) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  return v > 0 ? v : 148;
+}
+
+// Token columns per tile. Up to 128 rows: the next power of two. Above, 144
+// or 256, whichever finishes sooner on `sms` CTAs: rounds of (weight tile x
+// token tile x split) items times the time of one k-block, the larger of the
+// boxes at about 120 GB/s of L2-to-SM bandwidth and the tensor time (144
+// balances 400-row prefills: 3 tiles of 144 instead of 256 + 144).
+int tc_token_tile(int N, int T, int splits, int sms) {
+  if (T <= 128 || sms <= 0) return T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+  auto cost = [&](int bn) {
+    const long long items = (long long)((N + 127) / 128) * ((T + bn - 1) / bn) * splits;
+    const double rounds = (double)((items + sms - 1) / sms);
+    const double kb = std::max((16384.0 + bn * 128.0) / 120e9, 2.0 * 128 * bn * 64 / 10.8e12);
+    return rounds * kb;
+  };
+  return cost(144) < cost(256) ? 144 : 256;
+}
+
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
                     cudaStream_t s) {
   if (g.T <= 0) return;
-  int bn = g.T <= 16 ? 16 : g.T <= 32 ? 32 : g.T <= 64 ? 64 : g.T <= 128 ? 128 : 256;
+  int bn = g.epi == kEpiLinear ? tc_token_tile(g.N, g.T, splits, 0) : tc_token_tile(g.N, g.T, splits, tc_sms());
   if (g.epi == kEpiLinear && splits == 1) {
     // No split-K here: narrower token tiles until the tiles cover most SMs
     // (the weight tile is then re-read from L2 by more CTAs).
@@ -546,6 +573,7 @@ void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int s
     case 32: launch_bn<32, 8>(mw, mx, g, splits, s); break;
     case 64: launch_bn<64, 8>(mw, mx, g, splits, s); break;
     case 128: launch_bn<128, 6>(mw, mx, g, splits, s); break;
+    case 144: launch_bn<144, 5>(mw, mx, g, splits, s); break;
     default: launch_bn<256, 4>(mw, mx, g, splits, s); break;
   }
   const bool norm = g.norm_w != nullptr;

@@ -153,6 +153,9 @@ struct TcArgs {
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
                     cudaStream_t s);
 bool tc_available();
+// Token-tile width launch_gemm_tc uses for a projection (sms 0: powers of two only).
+int tc_token_tile(int N, int T, int splits, int sms);
+int tc_sms();
 
 // Argmax over fp32 logits with up to two banned ids into st (finalize sets st->tok).
 void launch_argmax(const float* logits, int n, int ban0, int ban1, StepState* st, int* out_dev,
