@@ -359,9 +359,11 @@ __global__ void __launch_bounds__(kTcThreadsP, 1)
         if (splits > 1) {
           const int lim = min(min(32, BN - c0), g.T - (n0 + c0));
           float* pw = g.ws + ((long long)kz * g.T + n0 + c0) * g.N + row;
+          if (row < g.N) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < lim) pw[(long long)i * g.N] = v[i];
+            for (int i = 0; i < 32; ++i)
+              if (i < lim) pw[(long long)i * g.N] = v[i];
+          }
         } else {
           finish(v, c0);
         }
@@ -471,6 +473,45 @@ __global__ void __launch_bounds__(256) splitk_reduce_norm_kernel(TcArgs g, int s
       make_uint4(pk[0], pk[1], pk[2], pk[3]);
 }
 
+// Linear epilogue after split-K: y = act(sum of the partials in split order
+// + bias), stored as in the GEMM epilogue (bf16, the split3 operand form, or
+// fp32 with an optional residual add).
+__global__ void splitk_linear_kernel(TcArgs g, int splits) {
+  pdl_trigger();
+  pdl_wait();
+  const long long n = (long long)g.T * g.N;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    float v = 0.f;
+    for (int z = 0; z < splits; ++z) v += g.ws[z * n + i];
+    const long long t = i / g.N;
+    const int row = static_cast<int>(i % g.N);
+    if (g.bias) v += g.bias[row];
+    switch (g.act) {
+      case 1: v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f)); break;
+      case 2: v = fmaxf(v, 0.0f); break;
+      case 3: v = v / (1.0f + expf(-v)); break;
+      case 4: v = 1.0f / (1.0f + expf(-v)); break;
+      default: break;
+    }
+    const long long o = t * g.ldo + row;
+    if (g.out_bf16) {
+      const uint16_t hi = f2bf(v);
+      if (g.split3) {
+        g.out_bf16[o] = hi;
+        g.out_bf16[o + g.N] = hi;
+        g.out_bf16[o + 2 * g.N] = f2bf(v - bf2f(hi));
+      } else {
+        g.out_bf16[o] = hi;
+      }
+    } else if (g.resid) {
+      g.out_f32[o] += (g.resid == 2 ? 0.5f : 1.0f) * v;
+    } else {
+      g.out_f32[o] = v;
+    }
+  }
+}
+
 // SwiGLU after split-K: output j of token t pairs gate row (j/64)*128 + j%64
 // with the up row 64 further in the same 128-row tile.
 __global__ void splitk_swiglu_kernel(TcArgs g, int splits) {
@@ -553,11 +594,45 @@ int tc_token_tile(int N, int T, int splits, int sms) {
   return cost(144) < cost(256) ? 144 : 256;
 }
 
+// Cost model as for the decoder projections (rounds x k-blocks x time per
+// k-block + the reduction), with a floor of 0.45 us per k-block: the latency
+// of one stage of a CTA's ring, measured on B200 for these small tiles.
+int linear_plan(int N, int K, int T, int sms, int* bn_out) {
+  int best_bn = 32, best_sp = 1;
+  double best = 1e30;
+  const int mt = (N + 127) / 128;
+  for (int bn : {32, 64, 128, 256}) {
+    if (bn > 32 && (bn >> 1) >= T) break;
+    for (int sp : {1, 2, 3, 4, 6, 8}) {
+      if (K % (64 * sp) != 0 || (sp > 1 && K / sp < 128)) continue;
+      const long long items = (long long)mt * ((T + bn - 1) / bn) * sp;
+      const int active = static_cast<int>(std::min<long long>(items, sms));
+      const double rounds = (double)((items + sms - 1) / sms);
+      const double kb = K / 64.0 / sp;
+      const double w_bytes = 128.0 * 64 * 2, x_bytes = bn * 64 * 2.0;
+      const double per_sm_hbm = std::min(6.4e12 / active, 55e9);
+      const double t_unit = std::max({0.45e-6, w_bytes / per_sm_hbm, (w_bytes + x_bytes) / 120e9,
+                                      2.0 * 128 * bn * 64 / 10.8e12});
+      const double red = sp > 1 ? (sp * 8.0 * T * N) / 3e12 + 4e-6 : 0.0;
+      const double c = rounds * kb * t_unit + red;
+      if (c < best * 0.97) {  // prefer the earlier (simpler) plan on near ties
+        best = c;
+        best_bn = bn;
+        best_sp = sp;
+      }
+    }
+  }
+  *bn_out = best_bn;
+  return best_sp;
+}
+
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
                     cudaStream_t s) {
   if (g.T <= 0) return;
   int bn = g.epi == kEpiLinear ? tc_token_tile(g.N, g.T, splits, 0) : tc_token_tile(g.N, g.T, splits, tc_sms());
-  if (g.epi == kEpiLinear && splits == 1) {
+  if (g.bn_hint > 0) {
+    bn = g.bn_hint;
+  } else if (g.epi == kEpiLinear && splits == 1) {
     // No split-K here: narrower token tiles until the tiles cover most SMs
     // (the weight tile is then re-read from L2 by more CTAs).
     const int mt = (g.N + 127) / 128;
@@ -586,6 +661,8 @@ void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int s
     const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, 148 * 16));
     if (g.epi == kEpiSwiglu)
       launch_pdl(splitk_swiglu_kernel, dim3(grid), dim3(256), 0, s, g, splits);
+    else if (g.epi == kEpiLinear)
+      launch_pdl(splitk_linear_kernel, dim3(grid), dim3(256), 0, s, g, splits);
     else if (norm)
       launch_pdl(splitk_reduce_norm_kernel, dim3(g.T), dim3(256), 0, s, g, splits);
     else

@@ -148,7 +148,12 @@ struct TcArgs {
   int act;
   int resid;
   int split3;
+  int bn_hint;  // token-tile width to use (0: chosen by launch_gemm_tc)
 };
+// kEpiLinear with split K: token-tile width (*bn) and split count for an
+// N x K Linear over T rows on `sms` CTAs; split counts divide K / 64. The
+// partials need splits * T * N floats of workspace in TcArgs::ws.
+int linear_plan(int N, int K, int T, int sms, int* bn);
 // X: [T, K] bf16 row-major (device), W: [N, K] bf16. splits divides K / 64.
 void launch_gemm_tc(const uint16_t* X, const uint16_t* W, const TcArgs& g, int splits,
                     cudaStream_t s);

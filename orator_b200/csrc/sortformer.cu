@@ -476,7 +476,7 @@ struct Sortformer::Impl {
       if (p) cudaFree(p);
     }
   };
-  Buf b_a, b_b, b_s1, b_s2, b_x, b_qkv, b_p, b_pe, b_pes, b_big, b_mel, b_out, b_emb;
+  Buf b_a, b_b, b_s1, b_s2, b_x, b_qkv, b_p, b_pe, b_pes, b_big, b_mel, b_out, b_emb, b_ws;
   std::vector<float> pe_host;
   int pe_T = -1;
 
@@ -618,7 +618,12 @@ struct Sortformer::Impl {
     g.bias = bias;
     g.act = act;
     g.resid = resid;
-    launch_gemm_tc(X3, W3, g, 1, s);
+    // split K where the Linear has too few tiles to cover the SMs
+    int bn = 0;
+    const int splits = linear_plan(N, 3 * K, M, tc_sms(), &bn);
+    g.bn_hint = bn;
+    if (splits > 1) g.ws = b_ws.get<float>((size_t)splits * M * N);
+    launch_gemm_tc(X3, W3, g, splits, s);
     check(cudaGetLastError(), "sortformer gemm");
   }
   void ln(const float* x, const float* g, const float* b, float* of, uint16_t* os, int M, int Dm,
