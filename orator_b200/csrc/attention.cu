@@ -383,7 +383,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_store_kernel(
   const int tab = row_table ? row_table[row] : 0;
   const int page = page_table[(long long)tab * max_pages + pos / kPage];
   float* x = qkv + (long long)row * kQkvDim;
-  for (int hd = warp; hd < kQHeads + kKvHeads; hd += 8) {
+  // grid.y 0-2: heads 8y .. 8y+7 (16 q heads, then 8 k heads), one per warp;
+  // grid.y 3: the V rows
+  for (int hd = blockIdx.y * 8 + warp; blockIdx.y < 3 && hd < kQHeads + kKvHeads; hd += 24) {
     const bool isk = hd >= kQHeads;
     float* xh = x + hd * kHeadDim;
     const float* w = isk ? kn : qn;
@@ -412,7 +414,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_store_kernel(
       for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = f2bf(o[i]);
     }
   }
-  {
+  if (blockIdx.y == 3) {
     const int kh = warp;  // 8 warps, 8 V heads
     const float* vh = x + kQDim + kKvDim + kh * kHeadDim;
     uint16_t* dst = kv + (long long)page * kPageElems + kHalfPageElems +
@@ -442,7 +444,7 @@ void launch_qk_norm_rope_store(float* qkv, int rows, const float* qn, const floa
                                const int* page_table, int max_pages, const int* row_table,
                                const int* row_pos, int pos_base, cudaStream_t s) {
   if (rows <= 0) return;
-  launch_pdl(qk_norm_rope_store_kernel, dim3(rows), dim3(256), 0, s, qkv, qn, kn, cos, sin,
+  launch_pdl(qk_norm_rope_store_kernel, dim3(rows, 4), dim3(256), 0, s, qkv, qn, kn, cos, sin,
              kv_layer, page_table, max_pages, row_table, row_pos, pos_base);
 }
 
