@@ -190,66 +190,182 @@ __global__ void __launch_bounds__(256) tower_layernorm_kernel(const float* __res
 
 // Bidirectional attention inside segments. qkv [n][3072] fp32 (q | k | v,
 // 16 heads of 64 each); out [n][1024] bf16. A CTA serves one head and up to
-// 16 consecutive query rows of one segment (a warp per row); keys stream
-// through shared memory in tiles of 32 shared by all 16 warps. Lane j scores
-// key j of the tile; lanes own output dims lane and lane + 32.
+// 64 consecutive query rows of one segment (4 warps x 16 rows); the segment's
+// keys stream through shared memory in blocks of 64, and QK^T and PV run on
+// tensor cores (mma.sync m16n8k16, bf16) with every fp32 operand split into a
+// bf16 high part and a bf16 remainder: a.b ~ ah.bh + ah.bl + al.bh, which
+// keeps the products to fp32-grade accuracy (error about 2^-16 relative)
+// like the fp32 dot products of the reference's one-warp-per-(token, head)
+// kernel (asr_audio_tower.cu:207). Online softmax in fp32 per query row.
 struct AttnTile {
   int row0, nrows, seg0, seg1;
 };
-constexpr int kAttnRows = 16, kAttnKeys = 32;
+constexpr int kAttnRows = 64, kAttnKeys = 64;
+constexpr int kAttnLd = kDh + 8;  // bf16 row stride in shared memory (conflict-free fragments)
 
-__global__ void __launch_bounds__(kAttnRows * 32) tower_attn_kernel(
+__device__ __forceinline__ void split_bf16(float x, uint16_t& hi, uint16_t& lo) {
+  hi = f2bf(x);
+  lo = f2bf(x - bf2f(hi));
+}
+__device__ __forceinline__ uint32_t pack2(uint16_t a, uint16_t b) {
+  return static_cast<uint32_t>(a) | (static_cast<uint32_t>(b) << 16);
+}
+
+__global__ void __launch_bounds__(128) tower_attn_kernel(
     const float* __restrict__ qkv, const AttnTile* __restrict__ tiles, uint16_t* __restrict__ out,
     float scale) {
-  __shared__ float sq[kAttnRows][kDh];
-  __shared__ float sk[kAttnKeys][kDh + 1];
-  __shared__ float sv[kAttnKeys][kDh];
+  __shared__ __align__(16) uint16_t skh[kAttnKeys][kAttnLd], skl[kAttnKeys][kAttnLd];
+  __shared__ __align__(16) uint16_t svh[kDh][kAttnLd], svl[kDh][kAttnLd];  // V transposed
   const AttnTile t = tiles[blockIdx.x];
   const int h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool active = warp < t.nrows;
-  const int row = t.row0 + warp;
-  if (active) {
-    const float* qr = qkv + static_cast<long long>(row) * (3 * kD) + h * kDh;
-    sq[warp][lane] = qr[lane];
-    sq[warp][lane + 32] = qr[lane + 32];
+  const int g = lane >> 2, tq = lane & 3;
+  const int r0 = t.row0 + warp * 16;  // this warp's first query row
+  const bool wactive = warp * 16 < t.nrows;
+  // Q fragments (A operand) of 4 k-steps, high and low parts
+  uint32_t qh[4][4], ql[4][4];
+  {
+    const bool v0 = warp * 16 + g < t.nrows, v1 = warp * 16 + g + 8 < t.nrows;
+    const float* q0 = qkv + static_cast<long long>(r0 + g) * (3 * kD) + h * kDh;
+    const float* q1 = q0 + 8LL * (3 * kD);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const int c = ks * 16 + 2 * tq;
+      const float2 a00 = v0 ? *reinterpret_cast<const float2*>(q0 + c) : make_float2(0.f, 0.f);
+      const float2 a10 = v1 ? *reinterpret_cast<const float2*>(q1 + c) : make_float2(0.f, 0.f);
+      const float2 a01 = v0 ? *reinterpret_cast<const float2*>(q0 + c + 8) : make_float2(0.f, 0.f);
+      const float2 a11 = v1 ? *reinterpret_cast<const float2*>(q1 + c + 8) : make_float2(0.f, 0.f);
+      const float f[8] = {a00.x, a00.y, a10.x, a10.y, a01.x, a01.y, a11.x, a11.y};
+      uint16_t hh[8], ll[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) split_bf16(f[i], hh[i], ll[i]);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        qh[ks][r] = pack2(hh[2 * r], hh[2 * r + 1]);
+        ql[ks][r] = pack2(ll[2 * r], ll[2 * r + 1]);
+      }
+    }
   }
-  float m = -1e30f, l = 0.f, a0 = 0.f, a1 = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
   for (int j0 = t.seg0; j0 < t.seg1; j0 += kAttnKeys) {
-    __syncthreads();
+    __syncthreads();  // the previous block's readers are done
     for (int idx = threadIdx.x; idx < kAttnKeys * kDh; idx += blockDim.x) {
       const int jj = idx / kDh, d = idx - jj * kDh, j = j0 + jj;
       const bool ok = j < t.seg1;
       const float* base = qkv + static_cast<long long>(j) * (3 * kD) + h * kDh + d;
-      sk[jj][d] = ok ? base[kD] : 0.f;
-      sv[jj][d] = ok ? base[2 * kD] : 0.f;
+      uint16_t hi, lo;
+      split_bf16(ok ? base[kD] : 0.f, hi, lo);
+      skh[jj][d] = hi;
+      skl[jj][d] = lo;
+      split_bf16(ok ? base[2 * kD] : 0.f, hi, lo);
+      svh[d][jj] = hi;
+      svl[d][jj] = lo;
     }
     __syncthreads();
-    if (!active) continue;
-    float s = 0.f;
-#pragma unroll 16
-    for (int d = 0; d < kDh; ++d) s = fmaf(sq[warp][d], sk[lane][d], s);
-    const bool valid = j0 + lane < t.seg1;
-    s = valid ? s * scale : -INFINITY;
-    const float mn = fmaxf(m, warp_max(s));
-    const float corr = expf(m - mn);
-    const float p = valid ? expf(s - mn) : 0.f;
-    l = l * corr + warp_sum(p);
-    a0 *= corr;
-    a1 *= corr;
-    const int nj = min(kAttnKeys, t.seg1 - j0);
-    for (int jj = 0; jj < nj; ++jj) {
-      const float pj = __shfl_sync(0xffffffffu, p, jj);
-      a0 = fmaf(pj, sv[jj][lane], a0);
-      a1 = fmaf(pj, sv[jj][lane + 32], a1);
+    if (!wactive) continue;
+    // S = Q K^T over 8 key tiles of 8
+    float sc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      const int key = nt * 8 + g;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const int c = ks * 16 + 2 * tq;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&skh[key][c]);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&skh[key][c + 8]);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&skl[key][c]);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&skl[key][c + 8]);
+        mma_bf16(sc[nt], ql[ks][0], ql[ks][1], ql[ks][2], ql[ks][3], bh0, bh1);
+        mma_bf16(sc[nt], qh[ks][0], qh[ks][1], qh[ks][2], qh[ks][3], bl0, bl1);
+        mma_bf16(sc[nt], qh[ks][0], qh[ks][1], qh[ks][2], qh[ks][3], bh0, bh1);
+      }
     }
-    m = mn;
+    // online softmax: rows g (c0, c1) and g + 8 (c2, c3)
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool ok = j0 + nt * 8 + 2 * tq + e < t.seg1;
+        sc[nt][e] = ok ? sc[nt][e] * scale : -INFINITY;
+        sc[nt][2 + e] = ok ? sc[nt][2 + e] * scale : -INFINITY;
+        mx0 = fmaxf(mx0, sc[nt][e]);
+        mx1 = fmaxf(mx1, sc[nt][2 + e]);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float c0 = expf(m0 - mn0), c1 = expf(m1 - mn1);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sc[nt][e] = sc[nt][e] == -INFINITY ? 0.f : expf(sc[nt][e] - mn0);
+        sc[nt][2 + e] = sc[nt][2 + e] == -INFINITY ? 0.f : expf(sc[nt][2 + e] - mn1);
+        s0 += sc[nt][e];
+        s1 += sc[nt][2 + e];
+      }
+    }
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+    l0 = l0 * c0 + s0;
+    l1 = l1 * c1 + s1;
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o[i][0] *= c0; o[i][1] *= c0;
+      o[i][2] *= c1; o[i][3] *= c1;
+    }
+    // O += P V over 4 key steps of 16
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint16_t ph[8], pl[8];
+      const float pv[8] = {sc[2 * kk][0], sc[2 * kk][1], sc[2 * kk][2], sc[2 * kk][3],
+                           sc[2 * kk + 1][0], sc[2 * kk + 1][1], sc[2 * kk + 1][2], sc[2 * kk + 1][3]};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) split_bf16(pv[i], ph[i], pl[i]);
+      // A fragment: (row g, keys 2t..), (row g+8, keys 2t..), (row g, keys 2t+8..), (row g+8, keys 2t+8..)
+      const uint32_t ah0 = pack2(ph[0], ph[1]), ah1 = pack2(ph[2], ph[3]);
+      const uint32_t ah2 = pack2(ph[4], ph[5]), ah3 = pack2(ph[6], ph[7]);
+      const uint32_t al0 = pack2(pl[0], pl[1]), al1 = pack2(pl[2], pl[3]);
+      const uint32_t al2 = pack2(pl[4], pl[5]), al3 = pack2(pl[6], pl[7]);
+      const int c = kk * 16 + 2 * tq;
+#pragma unroll
+      for (int nd = 0; nd < 8; ++nd) {
+        const int dim = nd * 8 + g;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&svh[dim][c]);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&svh[dim][c + 8]);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&svl[dim][c]);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&svl[dim][c + 8]);
+        mma_bf16(o[nd], al0, al1, al2, al3, bh0, bh1);
+        mma_bf16(o[nd], ah0, ah1, ah2, ah3, bl0, bl1);
+        mma_bf16(o[nd], ah0, ah1, ah2, ah3, bh0, bh1);
+      }
+    }
   }
-  if (!active) return;
-  const float invl = l > 0.f ? 1.0f / l : 0.f;
-  uint16_t* o = out + static_cast<long long>(row) * kD + h * kDh;
-  o[lane] = f2bf(a0 * invl);
-  o[lane + 32] = f2bf(a1 * invl);
+  if (!wactive) return;
+  const float i0 = l0 > 0.f ? 1.0f / l0 : 0.f, i1 = l1 > 0.f ? 1.0f / l1 : 0.f;
+  const bool v0 = warp * 16 + g < t.nrows, v1 = warp * 16 + g + 8 < t.nrows;
+  uint16_t* o0 = out + static_cast<long long>(r0 + g) * kD + h * kDh;
+  uint16_t* o1 = o0 + 8LL * kD;
+#pragma unroll
+  for (int nd = 0; nd < 8; ++nd) {
+    const int c = nd * 8 + 2 * tq;
+    if (v0) *reinterpret_cast<uint32_t*>(o0 + c) = pack2(f2bf(o[nd][0] * i0), f2bf(o[nd][1] * i0));
+    if (v1) *reinterpret_cast<uint32_t*>(o1 + c) = pack2(f2bf(o[nd][2] * i1), f2bf(o[nd][3] * i1));
+  }
 }
 
 // Weight re-layouts applied once at load (host side).
@@ -677,7 +793,7 @@ int AudioTower::forward_device(const float* d_mel, const int* frames, int n_utt,
     const Impl::Layer& l = p.L[li];
     tower_layernorm_kernel<<<ln_grid, 256, 0, s>>>(p.hid, l.ln1_g, l.ln1_b, p.xn, N);
     p.gemm(p.xn, l.qkv_w, N, kD, 3 * kD, l.qkv_b, 0, p.qkv, nullptr, 0, s);
-    tower_attn_kernel<<<dim3(static_cast<unsigned>(tiles.size()), kHeads), kAttnRows * 32, 0, s>>>(
+    tower_attn_kernel<<<dim3(static_cast<unsigned>(tiles.size()), kHeads), 128, 0, s>>>(
         p.qkv, d_tiles, p.att, scale);
     check(cudaGetLastError(), "tower attention");
     p.gemm(p.att, l.o_w, N, kD, kD, l.o_b, 0, p.hid, nullptr, 1, s);
