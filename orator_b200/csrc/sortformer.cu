@@ -192,6 +192,274 @@ __global__ void __launch_bounds__(256) sf_dwconv_kernel(const float* __restrict_
 constexpr int kAr = 16, kAk = 32;
 constexpr int kRs = kDk + 4;   // padded row (floats): 16-byte reads, lane rows 4 banks apart
 constexpr int kDRs = kDDk + 4;
+// Relative-position MHSA on tensor cores (same scores as sf_relattn_kernel
+// below, which states the math): a CTA serves one head and 64 query rows
+// (4 warps x 16); keys stream in blocks of 64 with the 128 position rows
+// that block needs. Per warp and block: AC = (Q + u) K^T and the 16 x 80
+// matrix (Q + v) P^T over the warp's position rows, staged in shared memory
+// and read back along the shifted diagonal r = T-1-i+j (the rel_shift);
+// then online softmax and O += P V. Every fp32 operand is split into bf16
+// high + remainder parts and each product uses three mma.sync m16n8k16
+// (ah.bh + ah.bl + al.bh: fp32-grade, error about 2^-16 relative).
+constexpr int kRtRows = 64, kRtKeys = 64, kRtPos = 128, kRtLd = kDk + 8, kRtBd = 81;
+struct RtSmem {
+  uint16_t kh[kRtKeys][kRtLd], kl[kRtKeys][kRtLd];
+  uint16_t vh[kDk][kRtLd], vl[kDk][kRtLd];  // V transposed: [dim][key]
+  uint16_t ph[kRtPos][kRtLd], pl[kRtPos][kRtLd];
+  float bd[4][16][kRtBd];
+};
+
+__device__ __forceinline__ void rt_split(float x, uint16_t& hi, uint16_t& lo) {
+  hi = f2bf(x);
+  lo = f2bf(x - bf2f(hi));
+}
+__device__ __forceinline__ uint32_t rt_pack(uint16_t a, uint16_t b) {
+  return static_cast<uint32_t>(a) | (static_cast<uint32_t>(b) << 16);
+}
+
+__global__ void __launch_bounds__(128) sf_relattn_tc_kernel(const float* __restrict__ qkv,
+                                                           const float* __restrict__ p,
+                                                           const float* __restrict__ bu,
+                                                           const float* __restrict__ bv, int T,
+                                                           int valid, uint16_t* __restrict__ out) {
+  extern __shared__ __align__(16) uint8_t rt_raw[];
+  RtSmem& sm = *reinterpret_cast<RtSmem*>(rt_raw);
+  const int h = blockIdx.y, i0 = blockIdx.x * kRtRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int iw = i0 + warp * 16;
+  const bool wactive = iw < T;
+  const float scale = 0.125f;  // 1 / sqrt(64)
+  // A fragments of (q + u) and (q + v), high and low parts, 4 k-steps
+  uint32_t uh[4][4], ul[4][4], vh[4][4], vl[4][4];
+  {
+    const int ra = iw + g, rb = iw + g + 8;
+    const float* qa = qkv + (long long)ra * 3 * kD + h * kDk;
+    const float* qb = qkv + (long long)rb * 3 * kD + h * kDk;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const int c = ks * 16 + 2 * tq;
+      const int cols[4] = {c, c, c + 8, c + 8};
+      float f[8];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const bool row_b = r & 1;
+        const bool ok = (row_b ? rb : ra) < T;
+        const float* q = row_b ? qb : qa;
+        f[2 * r] = ok ? q[cols[r]] : 0.f;
+        f[2 * r + 1] = ok ? q[cols[r] + 1] : 0.f;
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        uint16_t h0, l0, h1, l1;
+        const float bu0 = bu[h * kDk + cols[r]], bu1 = bu[h * kDk + cols[r] + 1];
+        const float bv0 = bv[h * kDk + cols[r]], bv1 = bv[h * kDk + cols[r] + 1];
+        rt_split(f[2 * r] + bu0, h0, l0);
+        rt_split(f[2 * r + 1] + bu1, h1, l1);
+        uh[ks][r] = rt_pack(h0, h1);
+        ul[ks][r] = rt_pack(l0, l1);
+        rt_split(f[2 * r] + bv0, h0, l0);
+        rt_split(f[2 * r + 1] + bv1, h1, l1);
+        vh[ks][r] = rt_pack(h0, h1);
+        vl[ks][r] = rt_pack(l0, l1);
+      }
+    }
+  }
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  const int rw0 = 48 - 16 * warp;  // first position row of this warp within the staged rows
+  for (int j0 = 0; j0 < T; j0 += kRtKeys) {
+    __syncthreads();
+    // stage K, V (transposed) and the block's position rows as bf16 high /
+    // low parts; every load of the block is issued before the first store
+    {
+      constexpr int kKv4 = kRtKeys * (kDk / 4) / 128, kP4 = kRtPos * (kDk / 4) / 128;
+      float4 rk[kKv4], rv[kKv4], rp[kP4];
+      const int mbase = T - 1 - (i0 + kRtRows - 1) + j0;  // position row of (i0 + 63, j0)
+#pragma unroll
+      for (int e = 0; e < kKv4; ++e) {
+        const int idx = threadIdx.x + e * 128, jj = idx >> 4, d4 = idx & 15, j = j0 + jj;
+        rk[e] = rv[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < T) {
+          const float4* base = reinterpret_cast<const float4*>(qkv + (long long)j * 3 * kD + h * kDk);
+          rk[e] = base[kD / 4 + d4];
+          rv[e] = base[2 * kD / 4 + d4];
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < kP4; ++e) {
+        const int idx = threadIdx.x + e * 128, rr = idx >> 4, d4 = idx & 15, mrow = mbase + rr;
+        rp[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (mrow >= 0 && mrow < 2 * T - 1)
+          rp[e] = reinterpret_cast<const float4*>(p + (long long)mrow * kD + h * kDk)[d4];
+      }
+#pragma unroll
+      for (int e = 0; e < kKv4; ++e) {
+        const int idx = threadIdx.x + e * 128, jj = idx >> 4, d = (idx & 15) * 4;
+        const float kf[4] = {rk[e].x, rk[e].y, rk[e].z, rk[e].w};
+        const float vf[4] = {rv[e].x, rv[e].y, rv[e].z, rv[e].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint16_t hi, lo;
+          rt_split(kf[q], hi, lo);
+          sm.kh[jj][d + q] = hi;
+          sm.kl[jj][d + q] = lo;
+          rt_split(vf[q], hi, lo);
+          sm.vh[d + q][jj] = hi;
+          sm.vl[d + q][jj] = lo;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < kP4; ++e) {
+        const int idx = threadIdx.x + e * 128, rr = idx >> 4, d = (idx & 15) * 4;
+        const float pf[4] = {rp[e].x, rp[e].y, rp[e].z, rp[e].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint16_t hi, lo;
+          rt_split(pf[q], hi, lo);
+          sm.ph[rr][d + q] = hi;
+          sm.pl[rr][d + q] = lo;
+        }
+      }
+    }
+    __syncthreads();
+    if (!wactive) continue;
+    float sc[8][4];
+    // AC = (q + u) K^T
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      const int key = nt * 8 + g;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const int c = ks * 16 + 2 * tq;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&sm.kh[key][c]);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&sm.kh[key][c + 8]);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&sm.kl[key][c]);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&sm.kl[key][c + 8]);
+        mma_bf16(sc[nt], ul[ks][0], ul[ks][1], ul[ks][2], ul[ks][3], bh0, bh1);
+        mma_bf16(sc[nt], uh[ks][0], uh[ks][1], uh[ks][2], uh[ks][3], bl0, bl1);
+        mma_bf16(sc[nt], uh[ks][0], uh[ks][1], uh[ks][2], uh[ks][3], bh0, bh1);
+      }
+    }
+    // (q + v) P^T over the warp's 80 position rows -> shared memory
+#pragma unroll
+    for (int nt = 0; nt < 10; ++nt) {
+      float bd[4] = {0.f, 0.f, 0.f, 0.f};
+      const int pr = rw0 + nt * 8 + g;  // < 128
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const int c = ks * 16 + 2 * tq;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&sm.ph[pr][c]);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&sm.ph[pr][c + 8]);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&sm.pl[pr][c]);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&sm.pl[pr][c + 8]);
+        mma_bf16(bd, vl[ks][0], vl[ks][1], vl[ks][2], vl[ks][3], bh0, bh1);
+        mma_bf16(bd, vh[ks][0], vh[ks][1], vh[ks][2], vh[ks][3], bl0, bl1);
+        mma_bf16(bd, vh[ks][0], vh[ks][1], vh[ks][2], vh[ks][3], bh0, bh1);
+      }
+      const int col = nt * 8 + 2 * tq;
+      sm.bd[warp][g][col] = bd[0];
+      sm.bd[warp][g][col + 1] = bd[1];
+      sm.bd[warp][g + 8][col] = bd[2];
+      sm.bd[warp][g + 8][col + 1] = bd[3];
+    }
+    __syncwarp();
+    // scores: BD of (row, key) sits at column 15 - row + key
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int kl = nt * 8 + 2 * tq + e, j = j0 + kl;
+        const float b0 = sm.bd[warp][g][15 - g + kl];
+        const float b1 = sm.bd[warp][g + 8][7 - g + kl];
+        float s0 = j < valid ? (sc[nt][e] + b0) * scale : kMaskScore;
+        float s1 = j < valid ? (sc[nt][2 + e] + b1) * scale : kMaskScore;
+        if (j >= T) s0 = s1 = -INFINITY;
+        sc[nt][e] = s0;
+        sc[nt][2 + e] = s1;
+        mx0 = fmaxf(mx0, s0);
+        mx1 = fmaxf(mx1, s1);
+      }
+    }
+    __syncwarp();  // bd is rewritten by the next block
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float c0 = expf(m0 - mn0), c1 = expf(m1 - mn1);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sc[nt][e] = sc[nt][e] == -INFINITY ? 0.f : expf(sc[nt][e] - mn0);
+        sc[nt][2 + e] = sc[nt][2 + e] == -INFINITY ? 0.f : expf(sc[nt][2 + e] - mn1);
+        s0 += sc[nt][e];
+        s1 += sc[nt][2 + e];
+      }
+    }
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+    l0 = l0 * c0 + s0;
+    l1 = l1 * c1 + s1;
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o[i][0] *= c0; o[i][1] *= c0;
+      o[i][2] *= c1; o[i][3] *= c1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint16_t ph[8], pl[8];
+      const float pv[8] = {sc[2 * kk][0], sc[2 * kk][1], sc[2 * kk][2], sc[2 * kk][3],
+                           sc[2 * kk + 1][0], sc[2 * kk + 1][1], sc[2 * kk + 1][2], sc[2 * kk + 1][3]};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rt_split(pv[i], ph[i], pl[i]);
+      const uint32_t ah0 = rt_pack(ph[0], ph[1]), ah1 = rt_pack(ph[2], ph[3]);
+      const uint32_t ah2 = rt_pack(ph[4], ph[5]), ah3 = rt_pack(ph[6], ph[7]);
+      const uint32_t al0 = rt_pack(pl[0], pl[1]), al1 = rt_pack(pl[2], pl[3]);
+      const uint32_t al2 = rt_pack(pl[4], pl[5]), al3 = rt_pack(pl[6], pl[7]);
+      const int c = kk * 16 + 2 * tq;
+#pragma unroll
+      for (int nd = 0; nd < 8; ++nd) {
+        const int dim = nd * 8 + g;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&sm.vh[dim][c]);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&sm.vh[dim][c + 8]);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&sm.vl[dim][c]);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&sm.vl[dim][c + 8]);
+        mma_bf16(o[nd], al0, al1, al2, al3, bh0, bh1);
+        mma_bf16(o[nd], ah0, ah1, ah2, ah3, bl0, bl1);
+        mma_bf16(o[nd], ah0, ah1, ah2, ah3, bh0, bh1);
+      }
+    }
+  }
+  if (!wactive) return;
+  const float i0f = 1.0f / l0, i1f = 1.0f / l1;
+  const int ra = iw + g, rb = iw + g + 8;
+#pragma unroll
+  for (int nd = 0; nd < 8; ++nd) {
+    const int col = h * kDk + nd * 8 + 2 * tq;
+    if (ra < T) {
+      uint16_t* orow = out + (long long)ra * 3 * kD;
+      put_split(orow, kD, col, o[nd][0] * i0f);
+      put_split(orow, kD, col + 1, o[nd][1] * i0f);
+    }
+    if (rb < T) {
+      uint16_t* orow = out + (long long)rb * 3 * kD;
+      put_split(orow, kD, col, o[nd][2] * i1f);
+      put_split(orow, kD, col + 1, o[nd][3] * i1f);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kAr * 32) sf_relattn_kernel(const float* __restrict__ qkv,
                                                               const float* __restrict__ p,
                                                               const float* __restrict__ bu,
@@ -640,6 +908,8 @@ Sortformer::Sortformer(int conf_layers, int dec_layers) : p_(new Impl) {
   p_->DL = dec_layers;
   p_->err = dalloc<int>(1);
   ORX_CHECK(cudaMemset(p_->err, 0, sizeof(int)));
+  ORX_CHECK(cudaFuncSetAttribute(sf_relattn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(RtSmem))));
   p_->build();
 }
 
@@ -796,7 +1066,8 @@ void Sortformer::encode_decode_device(const float* d_emb, int T, int valid, floa
     p.ln(x, c.lnag, c.lnab, nullptr, s1, T, kD, s);
     p.gemm(s1, c.qkvw, T, kD, 3 * kD, c.qkvb, 0, qkv, nullptr, 0, s);
     p.gemm(pes, c.posw, P, kD, kD, nullptr, 0, pp, nullptr, 0, s);
-    sf_relattn_kernel<<<agrid, kAr * 32, 0, s>>>(qkv, pp, c.bu, c.bv, T, valid, s2);
+    sf_relattn_tc_kernel<<<dim3((T + kRtRows - 1) / kRtRows, kHeads), 128, sizeof(RtSmem), s>>>(
+        qkv, pp, c.bu, c.bv, T, valid, s2);
     check(cudaGetLastError(), "sortformer attention");
     p.gemm(s2, c.ow, T, kD, kD, c.ob, 0, x, nullptr, 1, s);
     p.ln(x, c.lncg, c.lncb, nullptr, s1, T, kD, s);

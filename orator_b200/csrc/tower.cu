@@ -253,17 +253,35 @@ __global__ void __launch_bounds__(128) tower_attn_kernel(
 
   for (int j0 = t.seg0; j0 < t.seg1; j0 += kAttnKeys) {
     __syncthreads();  // the previous block's readers are done
-    for (int idx = threadIdx.x; idx < kAttnKeys * kDh; idx += blockDim.x) {
-      const int jj = idx / kDh, d = idx - jj * kDh, j = j0 + jj;
-      const bool ok = j < t.seg1;
-      const float* base = qkv + static_cast<long long>(j) * (3 * kD) + h * kDh + d;
-      uint16_t hi, lo;
-      split_bf16(ok ? base[kD] : 0.f, hi, lo);
-      skh[jj][d] = hi;
-      skl[jj][d] = lo;
-      split_bf16(ok ? base[2 * kD] : 0.f, hi, lo);
-      svh[d][jj] = hi;
-      svl[d][jj] = lo;
+    {  // stage K and V (transposed) as bf16 high / low parts, all loads first
+      constexpr int kKv4 = kAttnKeys * (kDh / 4) / 128;
+      float4 rk[kKv4], rv[kKv4];
+#pragma unroll
+      for (int e = 0; e < kKv4; ++e) {
+        const int idx = threadIdx.x + e * 128, jj = idx >> 4, d4 = idx & 15, j = j0 + jj;
+        rk[e] = rv[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < t.seg1) {
+          const float4* base = reinterpret_cast<const float4*>(qkv + static_cast<long long>(j) * (3 * kD) + h * kDh);
+          rk[e] = base[kD / 4 + d4];
+          rv[e] = base[2 * kD / 4 + d4];
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < kKv4; ++e) {
+        const int idx = threadIdx.x + e * 128, jj = idx >> 4, d = (idx & 15) * 4;
+        const float kf[4] = {rk[e].x, rk[e].y, rk[e].z, rk[e].w};
+        const float vf[4] = {rv[e].x, rv[e].y, rv[e].z, rv[e].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint16_t hi, lo;
+          split_bf16(kf[q], hi, lo);
+          skh[jj][d + q] = hi;
+          skl[jj][d + q] = lo;
+          split_bf16(vf[q], hi, lo);
+          svh[d + q][jj] = hi;
+          svl[d + q][jj] = lo;
+        }
+      }
     }
     __syncthreads();
     if (!wactive) continue;
