@@ -185,22 +185,16 @@ __global__ void __launch_bounds__(256) sf_dwconv_kernel(const float* __restrict_
 // ---- conformer attention with relative positions --------------------------
 // score(i, j) = ((q_i + u) . k_j + (q_i + v) . p_{T-1-i+j}) / 8, keys >= valid
 // at -1e30 (RelShiftScoresKernel + AttnSoftmaxKernel of the reference).
-// qkv: [T][1536] fp32 (q | k | v), p: [2T-1][512] fp32. A CTA serves one head
-// and 16 consecutive query rows (a warp each); key tiles of 32 stream through
-// shared memory with the 47 position rows they need. Output: split bf16
+// qkv: [T][1536] fp32 (q | k | v), p: [2T-1][512] fp32. Output: split bf16
 // [T][3 * 512] (input of linear_out).
-constexpr int kAr = 16, kAk = 32;
-constexpr int kRs = kDk + 4;   // padded row (floats): 16-byte reads, lane rows 4 banks apart
-constexpr int kDRs = kDDk + 4;
-// Relative-position MHSA on tensor cores (same scores as sf_relattn_kernel
-// below, which states the math): a CTA serves one head and 64 query rows
-// (4 warps x 16); keys stream in blocks of 64 with the 128 position rows
-// that block needs. Per warp and block: AC = (Q + u) K^T and the 16 x 80
-// matrix (Q + v) P^T over the warp's position rows, staged in shared memory
-// and read back along the shifted diagonal r = T-1-i+j (the rel_shift);
-// then online softmax and O += P V. Every fp32 operand is split into bf16
-// high + remainder parts and each product uses three mma.sync m16n8k16
-// (ah.bh + ah.bl + al.bh: fp32-grade, error about 2^-16 relative).
+// On tensor cores: a CTA serves one head and 64 query rows (4 warps x 16);
+// keys stream in blocks of 64 with the 128 position rows that block needs.
+// Per warp and block: AC = (Q + u) K^T and the 16 x 80 matrix (Q + v) P^T
+// over the warp's position rows, staged in shared memory and read back along
+// the shifted diagonal r = T-1-i+j (the rel_shift); then online softmax and
+// O += P V. Every fp32 operand is split into bf16 high + remainder parts and
+// each product uses three mma.sync m16n8k16 (ah.bh + ah.bl + al.bh:
+// fp32-grade, error about 2^-16 relative).
 constexpr int kRtRows = 64, kRtKeys = 64, kRtPos = 128, kRtLd = kDk + 8, kRtBd = 81;
 struct RtSmem {
   uint16_t kh[kRtKeys][kRtLd], kl[kRtKeys][kRtLd];
@@ -460,183 +454,193 @@ __global__ void __launch_bounds__(128) sf_relattn_tc_kernel(const float* __restr
   }
 }
 
-__global__ void __launch_bounds__(kAr * 32) sf_relattn_kernel(const float* __restrict__ qkv,
-                                                              const float* __restrict__ p,
-                                                              const float* __restrict__ bu,
-                                                              const float* __restrict__ bv, int T,
-                                                              int valid, uint16_t* __restrict__ out) {
-  __shared__ __align__(16) float squ[kAr][kDk];
-  __shared__ __align__(16) float sqv[kAr][kDk];
-  __shared__ __align__(16) float sk[kAk][kRs];
-  __shared__ __align__(16) float sv[kAk][kDk];
-  __shared__ __align__(16) float sp[kAr + kAk - 1][kRs];
-  const int h = blockIdx.y, i0 = blockIdx.x * kAr;
+// Decoder attention (8 heads of 24): score(i, j) = q_i . k_j / sqrt(24), keys
+// >= valid at -1e30; qkv [T][576] fp32, output split bf16 [T][3 * 192]. On
+// tensor cores with dims padded to 32 for the k16 steps; 64 query rows per CTA
+// (4 warps x 16), keys in blocks of 64, split-bf16 products (fp32-grade)
+// and online softmax, as in sf_relattn_tc_kernel.
+constexpr int kDtLdK = 40, kDtLdV = 72;
+__global__ void __launch_bounds__(128) sf_dattn_tc_kernel(const float* __restrict__ qkv, int T,
+                                                         int valid, uint16_t* __restrict__ out) {
+  __shared__ __align__(16) uint16_t kh[64][kDtLdK], kl[64][kDtLdK];
+  __shared__ __align__(16) uint16_t vh[kDDk][kDtLdV], vl[kDDk][kDtLdV];  // V transposed
+  const int h = blockIdx.y, i0 = blockIdx.x * 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int i = i0 + warp;
-  const bool active = i < T;
-  if (active) {
-    const float* q = qkv + (long long)i * 3 * kD + h * kDk;
-    for (int d = lane; d < kDk; d += 32) {
-      squ[warp][d] = q[d] + bu[h * kDk + d];
-      sqv[warp][d] = q[d] + bv[h * kDk + d];
-    }
+  const int g = lane >> 2, tq = lane & 3;
+  const int iw = i0 + warp * 16;
+  const bool wactive = iw < T;
+  const float scale = 1.0f / sqrtf(static_cast<float>(kDDk));
+  for (int idx = threadIdx.x; idx < 64 * 8; idx += 128) {  // zero the pad dims 24..31 once
+    kh[idx >> 3][kDDk + (idx & 7)] = 0;
+    kl[idx >> 3][kDDk + (idx & 7)] = 0;
   }
-  const float scale = 0.125f;  // 1 / sqrt(64)
-  float m = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f;
-  // The next tile's K / V / position rows are loaded into registers while the
-  // current tile is being scored (one tile of global loads in flight).
-  constexpr int kKv4 = kAk * (kDk / 4) / (kAr * 32);               // float4 of K (and V) per thread
-  constexpr int kP4 = ((kAr + kAk - 1) * (kDk / 4) + kAr * 32 - 1) / (kAr * 32);
-  float4 rk[kKv4], rv[kKv4], rp[kP4];
-  auto fetch = [&](int j0) {
-    const int mbase = T - 1 - (i0 + kAr - 1) + j0;  // position row of (i0 + 15, j0)
+  uint32_t qh[2][4], ql[2][4];
+  {
+    const int ra = iw + g, rb = iw + g + 8;
 #pragma unroll
-    for (int e = 0; e < kKv4; ++e) {
-      const int idx = threadIdx.x + e * kAr * 32;
-      const int jj = idx / (kDk / 4), d4 = idx - jj * (kDk / 4), j = j0 + jj;
-      rk[e] = rv[e] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < T) {
-        const float4* base = reinterpret_cast<const float4*>(qkv + (long long)j * 3 * kD + h * kDk);
-        rk[e] = base[kD / 4 + d4];
-        rv[e] = base[2 * kD / 4 + d4];
+    for (int ks = 0; ks < 2; ++ks) {
+      const int c = ks * 16 + 2 * tq;
+      const int cols[4] = {c, c, c + 8, c + 8};
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int row = (r & 1) ? rb : ra;
+        float f0 = 0.f, f1 = 0.f;
+        if (row < T && cols[r] < kDDk) {
+          const float* q = qkv + (long long)row * 3 * kDD + h * kDDk + cols[r];
+          f0 = q[0];
+          f1 = q[1];
+        }
+        uint16_t h0, l0, h1, l1;
+        rt_split(f0, h0, l0);
+        rt_split(f1, h1, l1);
+        qh[ks][r] = rt_pack(h0, h1);
+        ql[ks][r] = rt_pack(l0, l1);
       }
     }
-#pragma unroll
-    for (int e = 0; e < kP4; ++e) {
-      const int idx = threadIdx.x + e * kAr * 32;
-      const int rr = idx / (kDk / 4), d4 = idx - rr * (kDk / 4), mrow = mbase + rr;
-      rp[e] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (rr < kAr + kAk - 1 && mrow >= 0 && mrow < 2 * T - 1)
-        rp[e] = reinterpret_cast<const float4*>(p + (long long)mrow * kD + h * kDk)[d4];
-    }
-  };
-  fetch(0);
-  for (int j0 = 0; j0 < T; j0 += kAk) {
-    __syncthreads();
-#pragma unroll
-    for (int e = 0; e < kKv4; ++e) {
-      const int idx = threadIdx.x + e * kAr * 32;
-      const int jj = idx / (kDk / 4), d4 = idx - jj * (kDk / 4);
-      *reinterpret_cast<float4*>(&sk[jj][4 * d4]) = rk[e];
-      *reinterpret_cast<float4*>(&sv[jj][4 * d4]) = rv[e];
-    }
-#pragma unroll
-    for (int e = 0; e < kP4; ++e) {
-      const int idx = threadIdx.x + e * kAr * 32;
-      const int rr = idx / (kDk / 4), d4 = idx - rr * (kDk / 4);
-      if (rr < kAr + kAk - 1) *reinterpret_cast<float4*>(&sp[rr][4 * d4]) = rp[e];
-    }
-    __syncthreads();
-    if (j0 + kAk < T) fetch(j0 + kAk);
-    if (!active) continue;
-    const int j = j0 + lane;
-    const int pr = (kAr - 1 - warp) + lane;  // row T-1-i+j relative to mbase
-    float ac = 0.f, bd = 0.f;
-#pragma unroll
-    for (int d4 = 0; d4 < kDk / 4; ++d4) {
-      const float4 k4 = *reinterpret_cast<const float4*>(&sk[lane][4 * d4]);
-      const float4 u4 = *reinterpret_cast<const float4*>(&squ[warp][4 * d4]);
-      const float4 p4 = *reinterpret_cast<const float4*>(&sp[pr][4 * d4]);
-      const float4 w4 = *reinterpret_cast<const float4*>(&sqv[warp][4 * d4]);
-      ac = fmaf(u4.x, k4.x, ac);
-      ac = fmaf(u4.y, k4.y, ac);
-      ac = fmaf(u4.z, k4.z, ac);
-      ac = fmaf(u4.w, k4.w, ac);
-      bd = fmaf(w4.x, p4.x, bd);
-      bd = fmaf(w4.y, p4.y, bd);
-      bd = fmaf(w4.z, p4.z, bd);
-      bd = fmaf(w4.w, p4.w, bd);
-    }
-    float s = j < valid ? (ac + bd) * scale : kMaskScore;
-    const bool in = j < T;
-    if (!in) s = -INFINITY;
-    const float mn = fmaxf(m, warp_max(s));
-    const float corr = expf(m - mn);
-    const float pj = in ? expf(s - mn) : 0.f;
-    l = l * corr + warp_sum(pj);
-    a0 *= corr;
-    a1 *= corr;
-    const int nj = min(kAk, T - j0);
-    for (int jj = 0; jj < nj; ++jj) {
-      const float w = __shfl_sync(0xffffffffu, pj, jj);
-      a0 = fmaf(w, sv[jj][lane], a0);
-      a1 = fmaf(w, sv[jj][lane + 32], a1);
-    }
-    m = mn;
   }
-  if (!active) return;
-  const float inv = 1.0f / l;
-  uint16_t* o = out + (long long)i * 3 * kD;
-  put_split(o, kD, h * kDk + lane, a0 * inv);
-  put_split(o, kD, h * kDk + lane + 32, a1 * inv);
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float o[3][4];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int j0 = 0; j0 < T; j0 += 64) {
+    __syncthreads();
+    {
+      constexpr int kN = 64 * (kDDk / 4) / 128;  // float4 of K (and V) per thread
+      float4 rk[kN], rv[kN];
+#pragma unroll
+      for (int e = 0; e < kN; ++e) {
+        const int idx = threadIdx.x + e * 128, jj = idx / (kDDk / 4), d4 = idx % (kDDk / 4), j = j0 + jj;
+        rk[e] = rv[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < T) {
+          const float4* base = reinterpret_cast<const float4*>(qkv + (long long)j * 3 * kDD + h * kDDk);
+          rk[e] = base[kDD / 4 + d4];
+          rv[e] = base[2 * kDD / 4 + d4];
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < kN; ++e) {
+        const int idx = threadIdx.x + e * 128, jj = idx / (kDDk / 4), d = (idx % (kDDk / 4)) * 4;
+        const float kf[4] = {rk[e].x, rk[e].y, rk[e].z, rk[e].w};
+        const float vf[4] = {rv[e].x, rv[e].y, rv[e].z, rv[e].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint16_t hi, lo;
+          rt_split(kf[q], hi, lo);
+          kh[jj][d + q] = hi;
+          kl[jj][d + q] = lo;
+          rt_split(vf[q], hi, lo);
+          vh[d + q][jj] = hi;
+          vl[d + q][jj] = lo;
+        }
+      }
+    }
+    __syncthreads();
+    if (!wactive) continue;
+    float sc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      const int key = nt * 8 + g;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        const int c = ks * 16 + 2 * tq;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&kh[key][c]);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&kh[key][c + 8]);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&kl[key][c]);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&kl[key][c + 8]);
+        mma_bf16(sc[nt], ql[ks][0], ql[ks][1], ql[ks][2], ql[ks][3], bh0, bh1);
+        mma_bf16(sc[nt], qh[ks][0], qh[ks][1], qh[ks][2], qh[ks][3], bl0, bl1);
+        mma_bf16(sc[nt], qh[ks][0], qh[ks][1], qh[ks][2], qh[ks][3], bh0, bh1);
+      }
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = j0 + nt * 8 + 2 * tq + e;
+        float s0 = j < valid ? sc[nt][e] * scale : kMaskScore;
+        float s1 = j < valid ? sc[nt][2 + e] * scale : kMaskScore;
+        if (j >= T) s0 = s1 = -INFINITY;
+        sc[nt][e] = s0;
+        sc[nt][2 + e] = s1;
+        mx0 = fmaxf(mx0, s0);
+        mx1 = fmaxf(mx1, s1);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float c0 = expf(m0 - mn0), c1 = expf(m1 - mn1);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sc[nt][e] = sc[nt][e] == -INFINITY ? 0.f : expf(sc[nt][e] - mn0);
+        sc[nt][2 + e] = sc[nt][2 + e] == -INFINITY ? 0.f : expf(sc[nt][2 + e] - mn1);
+        s0 += sc[nt][e];
+        s1 += sc[nt][2 + e];
+      }
+    }
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+    l0 = l0 * c0 + s0;
+    l1 = l1 * c1 + s1;
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      o[i][0] *= c0; o[i][1] *= c0;
+      o[i][2] *= c1; o[i][3] *= c1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint16_t ph[8], pl[8];
+      const float pv[8] = {sc[2 * kk][0], sc[2 * kk][1], sc[2 * kk][2], sc[2 * kk][3],
+                           sc[2 * kk + 1][0], sc[2 * kk + 1][1], sc[2 * kk + 1][2], sc[2 * kk + 1][3]};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rt_split(pv[i], ph[i], pl[i]);
+      const uint32_t ah0 = rt_pack(ph[0], ph[1]), ah1 = rt_pack(ph[2], ph[3]);
+      const uint32_t ah2 = rt_pack(ph[4], ph[5]), ah3 = rt_pack(ph[6], ph[7]);
+      const uint32_t al0 = rt_pack(pl[0], pl[1]), al1 = rt_pack(pl[2], pl[3]);
+      const uint32_t al2 = rt_pack(pl[4], pl[5]), al3 = rt_pack(pl[6], pl[7]);
+      const int c = kk * 16 + 2 * tq;
+#pragma unroll
+      for (int nd = 0; nd < 3; ++nd) {
+        const int dim = nd * 8 + g;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&vh[dim][c]);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&vh[dim][c + 8]);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&vl[dim][c]);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&vl[dim][c + 8]);
+        mma_bf16(o[nd], al0, al1, al2, al3, bh0, bh1);
+        mma_bf16(o[nd], ah0, ah1, ah2, ah3, bl0, bl1);
+        mma_bf16(o[nd], ah0, ah1, ah2, ah3, bh0, bh1);
+      }
+    }
+  }
+  if (!wactive) return;
+  const int ra = iw + g, rb = iw + g + 8;
+#pragma unroll
+  for (int nd = 0; nd < 3; ++nd) {
+    const int col = h * kDDk + nd * 8 + 2 * tq;
+    if (ra < T) {
+      uint16_t* orow = out + (long long)ra * 3 * kDD;
+      put_split(orow, kDD, col, o[nd][0] / l0);
+      put_split(orow, kDD, col + 1, o[nd][1] / l0);
+    }
+    if (rb < T) {
+      uint16_t* orow = out + (long long)rb * 3 * kDD;
+      put_split(orow, kDD, col, o[nd][2] / l1);
+      put_split(orow, kDD, col + 1, o[nd][3] / l1);
+    }
+  }
 }
 
-// Decoder attention (8 heads of 24), keys >= valid at -1e30; qkv [T][576].
-__global__ void __launch_bounds__(kAr * 32) sf_attn_kernel(const float* __restrict__ qkv, int T,
-                                                           int valid, uint16_t* __restrict__ out) {
-  __shared__ __align__(16) float sq[kAr][kDDk];
-  __shared__ __align__(16) float sk[kAk][kDRs];
-  __shared__ __align__(16) float sv[kAk][kDDk];
-  const int h = blockIdx.y, i0 = blockIdx.x * kAr;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int i = i0 + warp;
-  const bool active = i < T;
-  if (active && lane < kDDk) sq[warp][lane] = qkv[(long long)i * 3 * kDD + h * kDDk + lane];
-  const float scale = 1.0f / sqrtf(static_cast<float>(kDDk));
-  float m = -INFINITY, l = 0.f, a = 0.f;
-  // next tile's K / V rows in registers while the current one is scored
-  constexpr int kN4 = kAk * (kDDk / 4);  // 192 float4 of K (and V) per tile
-  float4 rk = make_float4(0.f, 0.f, 0.f, 0.f), rv = rk;
-  auto fetch = [&](int j0) {
-    rk = rv = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (threadIdx.x >= kN4) return;
-    const int jj = threadIdx.x / (kDDk / 4), d4 = threadIdx.x - jj * (kDDk / 4), j = j0 + jj;
-    if (j < T) {
-      const float4* base = reinterpret_cast<const float4*>(qkv + (long long)j * 3 * kDD + h * kDDk);
-      rk = base[kDD / 4 + d4];
-      rv = base[2 * kDD / 4 + d4];
-    }
-  };
-  fetch(0);
-  for (int j0 = 0; j0 < T; j0 += kAk) {
-    __syncthreads();
-    if (threadIdx.x < kN4) {
-      const int jj = threadIdx.x / (kDDk / 4), d4 = threadIdx.x - jj * (kDDk / 4);
-      *reinterpret_cast<float4*>(&sk[jj][4 * d4]) = rk;
-      *reinterpret_cast<float4*>(&sv[jj][4 * d4]) = rv;
-    }
-    __syncthreads();
-    if (j0 + kAk < T) fetch(j0 + kAk);
-    if (!active) continue;
-    const int j = j0 + lane;
-    float dot = 0.f;
-#pragma unroll
-    for (int d4 = 0; d4 < kDDk / 4; ++d4) {
-      const float4 k4 = *reinterpret_cast<const float4*>(&sk[lane][4 * d4]);
-      const float4 q4 = *reinterpret_cast<const float4*>(&sq[warp][4 * d4]);
-      dot = fmaf(q4.x, k4.x, dot);
-      dot = fmaf(q4.y, k4.y, dot);
-      dot = fmaf(q4.z, k4.z, dot);
-      dot = fmaf(q4.w, k4.w, dot);
-    }
-    float s = j < valid ? dot * scale : kMaskScore;
-    const bool in = j < T;
-    if (!in) s = -INFINITY;
-    const float mn = fmaxf(m, warp_max(s));
-    const float corr = expf(m - mn);
-    const float pj = in ? expf(s - mn) : 0.f;
-    l = l * corr + warp_sum(pj);
-    a *= corr;
-    const int nj = min(kAk, T - j0);
-    for (int jj = 0; jj < nj; ++jj) {
-      const float w = __shfl_sync(0xffffffffu, pj, jj);
-      if (lane < kDDk) a = fmaf(w, sv[jj][lane], a);
-    }
-    m = mn;
-  }
-  if (!active || lane >= kDDk) return;
-  put_split(out + (long long)i * 3 * kDD, kDD, h * kDDk + lane, a / l);
-}
 
 // Conv module middle: GLU of pointwise_conv1's output (rows >= valid zero),
 // depthwise conv k9 (zero padding) + bias, BatchNorm (running statistics),
@@ -1057,7 +1061,6 @@ void Sortformer::encode_decode_device(const float* d_emb, int T, int valid, floa
   sf_scale_kernel<<<grid_for((long long)T * kD), 256, 0, s>>>(d_emb, x, (long long)T * kD,
                                                               std::sqrt(static_cast<float>(kD)));
   check(cudaGetLastError(), "sortformer scale");
-  const dim3 agrid((T + kAr - 1) / kAr, kHeads);
   for (int li = 0; li < p.L; ++li) {
     const Impl::Conf& c = p.C[li];
     p.ln(x, c.ln1g, c.ln1b, nullptr, s1, T, kD, s);
@@ -1088,11 +1091,10 @@ void Sortformer::encode_decode_device(const float* d_emb, int T, int valid, floa
   p.gemm(s1, p.projw, T, kD, kDD, p.projb, 0, xd, nullptr, 0, s);
   sf_split_kernel<<<grid_for((long long)T * kDD), 256, 0, s>>>(xd, s1, T, kDD, 0, T);
   check(cudaGetLastError(), "sortformer split");
-  const dim3 dgrid((T + kAr - 1) / kAr, kDHeads);
   for (int li = 0; li < p.DL; ++li) {
     const Impl::Dec& d = p.Dl[li];
     p.gemm(s1, d.qkvw, T, kDD, 3 * kDD, d.qkvb, 0, qkv, nullptr, 0, s);
-    sf_attn_kernel<<<dgrid, kAr * 32, 0, s>>>(qkv, T, valid, s2);
+    sf_dattn_tc_kernel<<<dim3((T + 63) / 64, kDHeads), 128, 0, s>>>(qkv, T, valid, s2);
     check(cudaGetLastError(), "sortformer decoder attention");
     p.gemm(s2, d.ow, T, kDD, kDD, d.ob, 0, xd, nullptr, 1, s);
     p.ln(xd, d.ln1g, d.ln1b, xd, s1, T, kDD, s);
