@@ -19,6 +19,7 @@
 // in that split form. Attention (relative-position MHSA in the conformer,
 // plain MHSA in the decoder), softmax, LayerNorm, BatchNorm and the
 // convolutions of the pre-encode stay fp32 on the SIMT pipes.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -215,8 +216,11 @@ __global__ void __launch_bounds__(128) sf_relattn_tc_kernel(const float* __restr
                                                            const float* __restrict__ p,
                                                            const float* __restrict__ bu,
                                                            const float* __restrict__ bv, int T,
-                                                           int valid, uint16_t* __restrict__ out) {
+                                                           int valid, uint16_t* __restrict__ out,
+                                                           float* __restrict__ part,
+                                                           int* __restrict__ tick) {
   extern __shared__ __align__(16) uint8_t rt_raw[];
+  __shared__ int rt_last;
   RtSmem& sm = *reinterpret_cast<RtSmem*>(rt_raw);
   const int h = blockIdx.y, i0 = blockIdx.x * kRtRows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -264,7 +268,10 @@ __global__ void __launch_bounds__(128) sf_relattn_tc_kernel(const float* __restr
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   const int rw0 = 48 - 16 * warp;  // first position row of this warp within the staged rows
-  for (int j0 = 0; j0 < T; j0 += kRtKeys) {
+  // key blocks of this CTA: gridDim.z CTAs split the blocks of a query tile
+  const int nb = (T + kRtKeys - 1) / kRtKeys, KS = gridDim.z, kz = blockIdx.z;
+  const int jb0 = (kz * nb / KS) * kRtKeys, jb1 = min(T, ((kz + 1) * nb / KS) * kRtKeys);
+  for (int j0 = jb0; j0 < jb1; j0 += kRtKeys) {
     __syncthreads();
     // stage K, V (transposed) and the block's position rows as bf16 high /
     // low parts; every load of the block is issued before the first store
@@ -434,6 +441,53 @@ __global__ void __launch_bounds__(128) sf_relattn_tc_kernel(const float* __restr
         mma_bf16(o[nd], ah0, ah1, ah2, ah3, bh0, bh1);
       }
     }
+  }
+  if (KS > 1) {
+    // Publish this CTA's (m, l, unnormalised o) in fragment order; the CTA
+    // that arrives last for the (tile, head) merges all key ranges in order
+    // (the same sums whichever CTA is last).
+    const int slot = blockIdx.y * gridDim.x + blockIdx.x;
+    float* mine = part + (((long long)slot * KS + kz) * 128 + threadIdx.x) * 36;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mine[nd * 4 + e] = o[nd][e];
+    mine[32] = m0; mine[33] = m1; mine[34] = l0; mine[35] = l1;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int tk;
+      asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(tk) : "l"(tick + slot) : "memory");
+      rt_last = tk == KS - 1;
+      if (tk == KS - 1) tick[slot] = 0;  // ready for the next launch
+    }
+    __syncthreads();
+    if (!rt_last) return;
+    float M0 = -INFINITY, M1 = -INFINITY;
+    for (int z = 0; z < KS; ++z) {
+      const float* pz = part + (((long long)slot * KS + z) * 128 + threadIdx.x) * 36;
+      M0 = fmaxf(M0, __ldcg(pz + 32));
+      M1 = fmaxf(M1, __ldcg(pz + 33));
+    }
+    float L0 = 0.f, L1 = 0.f;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+    for (int z = 0; z < KS; ++z) {
+      const float* pz = part + (((long long)slot * KS + z) * 128 + threadIdx.x) * 36;
+      const float mz0 = __ldcg(pz + 32), mz1 = __ldcg(pz + 33);
+      const float w0 = mz0 == -INFINITY ? 0.f : expf(mz0 - M0);
+      const float w1 = mz1 == -INFINITY ? 0.f : expf(mz1 - M1);
+      L0 += __ldcg(pz + 34) * w0;
+      L1 += __ldcg(pz + 35) * w1;
+#pragma unroll
+      for (int nd = 0; nd < 8; ++nd) {
+        o[nd][0] += __ldcg(pz + nd * 4 + 0) * w0;
+        o[nd][1] += __ldcg(pz + nd * 4 + 1) * w0;
+        o[nd][2] += __ldcg(pz + nd * 4 + 2) * w1;
+        o[nd][3] += __ldcg(pz + nd * 4 + 3) * w1;
+      }
+    }
+    l0 = L0;
+    l1 = L1;
   }
   if (!wactive) return;
   const float i0f = 1.0f / l0, i1f = 1.0f / l1;
@@ -748,7 +802,8 @@ struct Sortformer::Impl {
       if (p) cudaFree(p);
     }
   };
-  Buf b_a, b_b, b_s1, b_s2, b_x, b_qkv, b_p, b_pe, b_pes, b_big, b_mel, b_out, b_emb, b_ws;
+  Buf b_a, b_b, b_s1, b_s2, b_x, b_qkv, b_p, b_pe, b_pes, b_big, b_mel, b_out, b_emb, b_ws, b_rpart, b_rtick;
+  size_t rtick_n = 0;  // tickets known to be zero
   std::vector<float> pe_host;
   int pe_T = -1;
 
@@ -1061,6 +1116,16 @@ void Sortformer::encode_decode_device(const float* d_emb, int T, int valid, floa
   sf_scale_kernel<<<grid_for((long long)T * kD), 256, 0, s>>>(d_emb, x, (long long)T * kD,
                                                               std::sqrt(static_cast<float>(kD)));
   check(cudaGetLastError(), "sortformer scale");
+  // relative-position attention: query tiles x heads x key ranges, about
+  // two CTAs per SM (each holds 94 KB of shared memory)
+  const int rt_tiles = (T + kRtRows - 1) / kRtRows, rt_nb = (T + kRtKeys - 1) / kRtKeys;
+  const int rt_ks = std::max(1, std::min({4, rt_nb, (2 * tc_sms()) / (rt_tiles * kHeads)}));
+  float* rt_part = p.b_rpart.get<float>((size_t)rt_tiles * kHeads * rt_ks * 128 * 36);
+  int* rt_tick = p.b_rtick.get<int>((size_t)rt_tiles * kHeads);
+  if ((size_t)rt_tiles * kHeads > p.rtick_n) {  // grown (or first use): tickets start at zero
+    ORX_CHECK(cudaMemsetAsync(rt_tick, 0, p.b_rtick.cap, s));
+    p.rtick_n = p.b_rtick.cap / sizeof(int);
+  }
   for (int li = 0; li < p.L; ++li) {
     const Impl::Conf& c = p.C[li];
     p.ln(x, c.ln1g, c.ln1b, nullptr, s1, T, kD, s);
@@ -1069,8 +1134,8 @@ void Sortformer::encode_decode_device(const float* d_emb, int T, int valid, floa
     p.ln(x, c.lnag, c.lnab, nullptr, s1, T, kD, s);
     p.gemm(s1, c.qkvw, T, kD, 3 * kD, c.qkvb, 0, qkv, nullptr, 0, s);
     p.gemm(pes, c.posw, P, kD, kD, nullptr, 0, pp, nullptr, 0, s);
-    sf_relattn_tc_kernel<<<dim3((T + kRtRows - 1) / kRtRows, kHeads), 128, sizeof(RtSmem), s>>>(
-        qkv, pp, c.bu, c.bv, T, valid, s2);
+    sf_relattn_tc_kernel<<<dim3(rt_tiles, kHeads, rt_ks), 128, sizeof(RtSmem), s>>>(
+        qkv, pp, c.bu, c.bv, T, valid, s2, rt_part, rt_tick);
     check(cudaGetLastError(), "sortformer attention");
     p.gemm(s2, c.ow, T, kD, kD, c.ob, 0, x, nullptr, 1, s);
     p.ln(x, c.lncg, c.lncb, nullptr, s1, T, kD, s);
