@@ -24,15 +24,32 @@ constexpr int kPfWarps = 2 * kKeyGroups;      // warp w: query head (w & 1), key
 constexpr int kPfThreads = kPfWarps * 32;
 constexpr int kPfRows = 16;  // query positions per tile
 constexpr int kTileB = kPage * kHeadDim * 2;  // 4 KiB K or V tile
-constexpr int kSlots = 2 * kKeyGroups;        // two groups of pages in flight
 constexpr int kPtStage = 1024;                // page ids staged in shared memory
 constexpr int kMergeFloats = 68;              // per lane: acc[16][4] + m0, m1, l0, l1
-constexpr int kPfSmem = kSlots * 2 * kTileB + 1024;
-static_assert((kPfWarps - 2) * 32 * kMergeFloats * 4 <= kSlots * 2 * kTileB,
+constexpr int kQFragB = 8 * 4 * 32 * 4 * 2;   // one warp's q fragments (hi + lo), bytes
+// Two shapes of the kernel:
+//  WIDE = false (launches of less than two waves): q fragments in registers,
+//    two groups of pages in flight, one CTA per SM -- the shortest path for
+//    one CTA;
+//  WIDE = true (many tiles, e.g. a batch of joining sessions): q fragments
+//    in shared memory and one group of pages in flight, so that two CTAs
+//    (16 warps) fit on an SM -- more throughput per SM.
+template <bool WIDE>
+struct PfShape {
+  static constexpr int kSlots = WIDE ? kKeyGroups : 2 * kKeyGroups;
+  static constexpr int kRingB = kSlots * 2 * kTileB;
+  static constexpr int kSmem = kRingB + (WIDE ? kPfWarps * kQFragB : 0) + 1024;
+};
+static_assert((kPfWarps - 2) * 32 * kMergeFloats * 4 <= PfShape<false>::kRingB,
               "merge buffer reuses the ring");
+static_assert((kPfWarps - 2) * 32 * kMergeFloats * 4 <= kPfWarps * kQFragB,
+              "merge buffer reuses the q fragments");
 
-__global__ void __launch_bounds__(kPfThreads, 1)
+template <bool WIDE>
+__global__ void __launch_bounds__(kPfThreads, WIDE ? 2 : 1)
     attn_prefill_kernel(const __grid_constant__ CUtensorMap kvmap, PrefillAttnArgs a) {
+  constexpr int kSlots = PfShape<WIDE>::kSlots;
+  constexpr int kRingB = PfShape<WIDE>::kRingB;
   extern __shared__ uint8_t pf_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(pf_raw) + 1023) & ~uintptr_t(1023));
@@ -73,7 +90,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   // Q fragments of this warp's 16 rows: hi and lo bf16 parts.
   const int hh = warp & 1, kg = warp >> 1, rbase = 0;
   const int g = lane >> 2, tig = lane & 3;
-  uint32_t qh[8][4], ql[8][4];
+  // q fragments: registers, or shared memory ([ks][r][lane], hi then lo)
+  uint32_t qh[WIDE ? 1 : 8][4], ql[WIDE ? 1 : 8][4];
+  uint32_t* qf = reinterpret_cast<uint32_t*>(sm + kRingB + warp * kQFragB);
   {
     const float* q0 = a.qkv + (long long)(ti.row0 + rbase + g) * a.qkv_stride + (2 * h + hh) * kHeadDim;
     const float* q1 = q0 + 8LL * a.qkv_stride;
@@ -88,8 +107,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       x[6] = v1 ? q1[c + 8] : 0.f; x[7] = v1 ? q1[c + 9] : 0.f;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        qh[ks][r] = pack_bf16(split_part(x[2 * r], false), split_part(x[2 * r + 1], false));
-        ql[ks][r] = pack_bf16(split_part(x[2 * r], true), split_part(x[2 * r + 1], true));
+        const uint32_t hv = pack_bf16(split_part(x[2 * r], false), split_part(x[2 * r + 1], false));
+        const uint32_t lv = pack_bf16(split_part(x[2 * r], true), split_part(x[2 * r + 1], true));
+        if constexpr (WIDE) {
+          qf[(ks * 4 + r) * 32 + lane] = hv;
+          qf[1024 + (ks * 4 + r) * 32 + lane] = lv;
+        } else {
+          qh[ks][r] = hv;
+          ql[ks][r] = lv;
+        }
       }
     }
   }
@@ -115,8 +141,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int r = nt * 8 + g, c = ks * 16 + tig * 2;
         const uint32_t b0 = *reinterpret_cast<const uint32_t*>(base + sw_off(r, c));
         const uint32_t b1 = *reinterpret_cast<const uint32_t*>(base + sw_off(r, c + 8));
-        mma_bf16(d[nt], qh[ks][0], qh[ks][1], qh[ks][2], qh[ks][3], b0, b1);
-        mma_bf16(d[nt], ql[ks][0], ql[ks][1], ql[ks][2], ql[ks][3], b0, b1);
+        if constexpr (WIDE) {
+          const uint32_t* qhk = qf + ks * 128 + lane;
+          const uint32_t* qlk = qhk + 1024;
+          mma_bf16(d[nt], qhk[0], qhk[32], qhk[64], qhk[96], b0, b1);
+          mma_bf16(d[nt], qlk[0], qlk[32], qlk[64], qlk[96], b0, b1);
+        } else {
+          mma_bf16(d[nt], qh[ks][0], qh[ks][1], qh[ks][2], qh[ks][3], b0, b1);
+          mma_bf16(d[nt], ql[ks][0], ql[ks][1], ql[ks][2], ql[ks][3], b0, b1);
+        }
       }
     float s0[4], s1[4];  // rows g and g + 8; columns nt * 2 + j
 #pragma unroll
@@ -192,7 +225,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   // Merge the key groups of each head in group order (deterministic): groups
   // 1..3 park their state in the (now idle) ring, group 0 combines.
   {
-    float* mb = reinterpret_cast<float*>(sm);
+    float* mb = reinterpret_cast<float*>(WIDE ? sm + kRingB : sm);
     if (kg > 0) {
       float* dst = mb + ((size_t)(warp - 2) * 32 + lane) * kMergeFloats;
 #pragma unroll
@@ -259,11 +292,18 @@ void launch_attn_prefill(const PrefillAttnArgs& a, int ntiles, const uint16_t* k
   if (ntiles <= 0) return;
   static std::atomic<unsigned long long> configured{0};
   once_per_device(configured, [] {
-    cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
+    cudaFuncSetAttribute(attn_prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         PfShape<false>::kSmem);
+    cudaFuncSetAttribute(attn_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         PfShape<true>::kSmem);
   });
   CUtensorMap map;
   if (!make_tmap_2d(&map, kv_pool, pool_rows, kHeadDim, 64, kPage)) return;
-  launch_pdl(attn_prefill_kernel, dim3(ntiles * kKvHeads), dim3(kPfThreads), kPfSmem, s, map, a);
+  const int items = ntiles * kKvHeads;
+  if (items >= 2 * tc_sms())
+    launch_pdl(attn_prefill_kernel<true>, dim3(items), dim3(kPfThreads), PfShape<true>::kSmem, s, map, a);
+  else
+    launch_pdl(attn_prefill_kernel<false>, dim3(items), dim3(kPfThreads), PfShape<false>::kSmem, s, map, a);
 }
 
 int prefill_tile_rows() { return kPfRows; }
