@@ -34,9 +34,15 @@ constexpr int kCtx = 64, kWin = 512, kIn = 576, kPad = 640;
 constexpr int kNfft = 256, kHop = 128, kBins = 129, kFrames = 4, kH = 128;
 constexpr int kFeWin = 32;   // windows per front-end CTA
 constexpr int kBinTile = 32; // STFT bins per basis slice
+constexpr int kBasisRows = 2 * kBinTile * ((kBins + kBinTile - 1) / kBinTile);  // 320 split rows
 
 struct VadW {
   const float* basis;  // [258][256]
+  // basis split for the tensor cores: [320][256] bf16 high parts and
+  // remainders, row 2b + 0 = the real row of bin b, 2b + 1 = its imaginary
+  // row (zero rows past bin 128)
+  const uint16_t* bh;
+  const uint16_t* bl;
   const float* w0; const float* b0;  // [128][129][3]
   const float* w1; const float* b1;  // [64][128][3]
   const float* w2; const float* b2;  // [64][64][3]
@@ -50,7 +56,6 @@ struct VadW {
 // Row strides padded so that the 32 lanes of a warp (32 windows, or 8 bin
 // groups) hit 32 different banks.
 constexpr int kXs = kPad + 4;         // padded input row
-constexpr int kBs = kNfft + 1;        // basis row
 constexpr int kMs = kBins * kFrames + 1;  // magnitude row [ci * 4 + t]
 constexpr int kE0s = 128 * 4 + 1;     // enc0 row [c * 4 + t]
 constexpr int kE1s = 64 * 2 + 1;      // enc1 row [c * 2 + t]
@@ -59,7 +64,10 @@ constexpr int kE2s = 64 + 1;          // enc2 row
 struct FeSmem {
   float x[kFeWin][kXs];               // 80.5 KiB padded inputs
   union {
-    float basis[2 * kBinTile][kBs];   // 64.3 KiB: re rows, then im rows, of a bin slice
+    struct {                          // 66 KiB: one slice of 32 bins (64 basis rows)
+      uint16_t bh[2 * kBinTile][kNfft + 8];
+      uint16_t bl[2 * kBinTile][kNfft + 8];
+    } sb;
     float e0[kFeWin][kE0s];           // 64.1 KiB
   };
   union {
@@ -99,51 +107,66 @@ __global__ void __launch_bounds__(256, 1) vad_frontend_kernel(const float* __res
     sm.x[wi][j] = v;
   }
 
-  // ---- STFT magnitude: thread = one window (4 frames) x 4 bins of a slice ----
+  // ---- STFT magnitude on tensor cores ----
+  // Rows = (window, frame) pairs, 128 per CTA: warp w takes rows 16w .. 16w+15
+  // (window r / 4, frame r % 4; row r reads x[window][128 frame + k]).
+  // Columns = basis rows of a 32-bin slice, (real, imaginary) interleaved, so
+  // a thread's accumulator pair is one bin's (re, im). Products are fp32-grade:
+  // x and the basis are split into bf16 high + remainder parts and each
+  // product is ah.bh + ah.bl + al.bh (mma.sync m16n8k16, fp32 accumulation).
   {
-    const int wsel = tid >> 3;
-    const int bsel = (tid & 7) * 4;
-    for (int f0 = 0; f0 < kBins; f0 += kBinTile) {
-      const int nb = kBins - f0 < kBinTile ? kBins - f0 : kBinTile;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int ra = warp * 16 + g, rb = ra + 8;
+    const float* xa = &sm.x[ra >> 2][(ra & 3) * kHop];
+    const float* xb = &sm.x[rb >> 2][(rb & 3) * kHop];
+    for (int sl = 0; sl < (kBins + kBinTile - 1) / kBinTile; ++sl) {
       __syncthreads();  // previous slice consumed (and inputs written)
-      for (int i = tid; i < 2 * kBinTile * kNfft; i += 256) {
-        const int r = i / kNfft, k = i % kNfft;
-        const int fr = r % kBinTile;
-        const int f = r < kBinTile ? f0 + fr : kBins + f0 + fr;
-        sm.basis[r][k] = fr < nb ? __ldg(w.basis + (long long)f * kNfft + k) : 0.f;
+      for (int i = tid; i < 2 * kBinTile * (kNfft / 8); i += 256) {
+        const int r = i / (kNfft / 8), c = i % (kNfft / 8);
+        const size_t src = (size_t)(sl * 2 * kBinTile + r) * kNfft;
+        reinterpret_cast<uint4*>(&sm.sb.bh[r][0])[c] = __ldg(reinterpret_cast<const uint4*>(w.bh + src) + c);
+        reinterpret_cast<uint4*>(&sm.sb.bl[r][0])[c] = __ldg(reinterpret_cast<const uint4*>(w.bl + src) + c);
       }
       __syncthreads();
-      float re[4][4], im[4][4];
+      float acc[8][4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t)
+      for (int nt = 0; nt < 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+#pragma unroll 2
+      for (int ks = 0; ks < kNfft / 16; ++ks) {
+        const int c = ks * 16 + 2 * t4;
+        const float2 a00 = *reinterpret_cast<const float2*>(xa + c);
+        const float2 a10 = *reinterpret_cast<const float2*>(xb + c);
+        const float2 a01 = *reinterpret_cast<const float2*>(xa + c + 8);
+        const float2 a11 = *reinterpret_cast<const float2*>(xb + c + 8);
+        const float f[8] = {a00.x, a00.y, a10.x, a10.y, a01.x, a01.y, a11.x, a11.y};
+        uint32_t ah[4], al[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) re[t][q] = im[t][q] = 0.f;
-      const float* xw = sm.x[wsel];
-#pragma unroll 4
-      for (int k = 0; k < kNfft; ++k) {
-        float xv[4], br[4], bi[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) xv[t] = xw[t * kHop + k];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          br[q] = sm.basis[bsel + q][k];
-          bi[q] = sm.basis[kBinTile + bsel + q][k];
+        for (int r = 0; r < 4; ++r) {
+          const uint16_t h0 = f2bf(f[2 * r]), h1 = f2bf(f[2 * r + 1]);
+          const uint16_t l0 = f2bf(f[2 * r] - bf2f(h0)), l1 = f2bf(f[2 * r + 1] - bf2f(h1));
+          ah[r] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
+          al[r] = static_cast<uint32_t>(l0) | (static_cast<uint32_t>(l1) << 16);
         }
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            re[t][q] = fmaf(xv[t], br[q], re[t][q]);
-            im[t][q] = fmaf(xv[t], bi[q], im[t][q]);
-          }
+        for (int nt = 0; nt < 8; ++nt) {
+          const int n = nt * 8 + g;
+          const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&sm.sb.bh[n][c]);
+          const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&sm.sb.bh[n][c + 8]);
+          const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&sm.sb.bl[n][c]);
+          const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&sm.sb.bl[n][c + 8]);
+          mma_bf16(acc[nt], al[0], al[1], al[2], al[3], bh0, bh1);
+          mma_bf16(acc[nt], ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+          mma_bf16(acc[nt], ah[0], ah[1], ah[2], ah[3], bh0, bh1);
+        }
       }
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (bsel + q < nb)
-#pragma unroll
-          for (int t = 0; t < 4; ++t)
-            sm.mag[wsel][(f0 + bsel + q) * 4 + t] =
-                sqrtf(re[t][q] * re[t][q] + im[t][q] * im[t][q]);
+      for (int nt = 0; nt < 8; ++nt) {
+        const int bin = sl * kBinTile + nt * 4 + t4;
+        if (bin < kBins) {
+          sm.mag[ra >> 2][bin * 4 + (ra & 3)] = sqrtf(acc[nt][0] * acc[nt][0] + acc[nt][1] * acc[nt][1]);
+          sm.mag[rb >> 2][bin * 4 + (rb & 3)] = sqrtf(acc[nt][2] * acc[nt][2] + acc[nt][3] * acc[nt][3]);
+        }
+      }
     }
   }
   __syncthreads();
@@ -364,6 +387,7 @@ struct BatchVad::Impl {
   std::vector<float> host[15];
   bool have[15] = {};
   float* d_w = nullptr;          // all weights, packed
+  uint16_t* d_bhl = nullptr;     // the split STFT basis
   size_t off[20] = {};
   float *d_h = nullptr, *d_c = nullptr, *d_ctx = nullptr, *d_xin = nullptr;
   float *d_pcm = nullptr, *d_probs = nullptr;
@@ -394,7 +418,7 @@ BatchVad::BatchVad(int streams) : p_(new Impl) {
 }
 
 BatchVad::~BatchVad() {
-  for (void* q : {(void*)p_->d_w, (void*)p_->d_h, (void*)p_->d_c, (void*)p_->d_ctx,
+  for (void* q : {(void*)p_->d_w, (void*)p_->d_bhl, (void*)p_->d_h, (void*)p_->d_c, (void*)p_->d_ctx,
                   (void*)p_->d_xin, (void*)p_->d_pcm, (void*)p_->d_probs})
     if (q) cudaFree(q);
   delete p_;
@@ -443,6 +467,34 @@ void BatchVad::upload() {
   for (int r = 0; r < 4 * kH; ++r) b[r] = p_->host[11][r] + p_->host[12][r];
   put(10, b.data(), b.size());
   put(11, p_->host[13].data(), kH);
+  // the basis split for the tensor-core STFT (see VadW::bh): rows 2b / 2b+1
+  std::vector<uint16_t> bhl((size_t)2 * kBasisRows * kNfft, 0);
+  auto to_bf = [](float f) {  // round to nearest even
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7f800000u) != 0x7f800000u) u += 0x7fffu + ((u >> 16) & 1u);
+    return static_cast<uint16_t>(u >> 16);
+  };
+  auto from_bf = [](uint16_t b) {
+    const uint32_t u = static_cast<uint32_t>(b) << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+  };
+  for (int bin = 0; bin < kBins; ++bin)
+    for (int part = 0; part < 2; ++part)
+      for (int k = 0; k < kNfft; ++k) {
+        const float v = p_->host[0][(size_t)(part * kBins + bin) * kNfft + k];
+        const uint16_t hi = to_bf(v);
+        const size_t row = (size_t)(2 * bin + part) * kNfft + k;
+        bhl[row] = hi;
+        bhl[(size_t)kBasisRows * kNfft + row] = to_bf(v - from_bf(hi));
+      }
+  if (p_->d_bhl) cudaFree(p_->d_bhl);
+  p_->d_bhl = dalloc<uint16_t>(bhl.size());
+  ORX_CHECK(cudaMemcpy(p_->d_bhl, bhl.data(), bhl.size() * 2, cudaMemcpyHostToDevice));
+  p_->w.bh = p_->d_bhl;
+  p_->w.bl = p_->d_bhl + (size_t)kBasisRows * kNfft;
   if (p_->d_w) cudaFree(p_->d_w);
   p_->d_w = dalloc<float>(pk.size());
   ORX_CHECK(cudaMemcpy(p_->d_w, pk.data(), pk.size() * 4, cudaMemcpyHostToDevice));
