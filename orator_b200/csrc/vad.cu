@@ -43,6 +43,9 @@ struct VadW {
   // row (zero rows past bin 128)
   const uint16_t* bh;
   const uint16_t* bl;
+  // enc0 weights split the same way: [128][400], k = 3 ci + tap (zero past 387)
+  const uint16_t* w0h;
+  const uint16_t* w0l;
   const float* w0; const float* b0;  // [128][129][3]
   const float* w1; const float* b1;  // [64][128][3]
   const float* w2; const float* b2;  // [64][64][3]
@@ -173,38 +176,74 @@ __global__ void __launch_bounds__(256, 1) vad_frontend_kernel(const float* __res
 
   // The conv blocks: lane = window, warp = a group of output channels, so a
   // warp's weight loads are uniform (broadcast) and read once per CTA.
-  // ---- enc0: 129 -> 128, 4 frames, k3 s1 p1, ReLU ----
+  // ---- enc0: 129 -> 128, 4 frames, k3 s1 p1, ReLU, on tensor cores ----
+  // Rows = (window, frame) as in the STFT, columns = output channels, depth
+  // k = 3 ci + tap (387, zero-padded to 400): A(row, k) = mag[ci][frame + tap
+  // - 1] (zero outside the 4 frames), B = the split weights staged in chunks
+  // of 80 k into the (now idle) input area.
   {
-    const int cg = warp * 16;
+    constexpr int kK0 = 400, kChunkK = 80, kLd = kChunkK + 8;
+    uint16_t* sbh = reinterpret_cast<uint16_t*>(&sm.x[0][0]);
+    uint16_t* sbl = sbh + 128 * kLd;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int ra = warp * 16 + g, rb = ra + 8;
+    const float* ma = sm.mag[ra >> 2];
+    const float* mb = sm.mag[rb >> 2];
+    const int fa = ra & 3, fb = rb & 3;
+    auto aval = [&](const float* m, int f, int k) {
+      const int ci = (k * 43691) >> 17, tap = k - 3 * ci;  // k / 3, k % 3 (k < 2^15)
+      const int tt = f + tap - 1;
+      return (k < 3 * kBins && tt >= 0 && tt < 4) ? m[ci * 4 + tt] : 0.f;
+    };
     float acc[16][4];
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const float b = __ldg(w.b0 + cg + c);
+    for (int nt = 0; nt < 16; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    for (int k0 = 0; k0 < kK0; k0 += kChunkK) {
+      __syncthreads();  // inputs / previous chunk no longer read
+      for (int i = tid; i < 128 * (kChunkK / 8); i += 256) {
+        const int n = i / (kChunkK / 8), c = i % (kChunkK / 8);
+        const size_t src = (size_t)n * kK0 + k0;
+        reinterpret_cast<uint4*>(sbh + n * kLd)[c] = __ldg(reinterpret_cast<const uint4*>(w.w0h + src) + c);
+        reinterpret_cast<uint4*>(sbl + n * kLd)[c] = __ldg(reinterpret_cast<const uint4*>(w.w0l + src) + c);
+      }
+      __syncthreads();
+#pragma unroll 1
+      for (int ks = 0; ks < kChunkK / 16; ++ks) {
+        const int cl = ks * 16 + 2 * t4, k = k0 + cl;
+        const float f[8] = {aval(ma, fa, k), aval(ma, fa, k + 1), aval(mb, fb, k), aval(mb, fb, k + 1),
+                            aval(ma, fa, k + 8), aval(ma, fa, k + 9), aval(mb, fb, k + 8), aval(mb, fb, k + 9)};
+        uint32_t ah[4], al[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) acc[c][t] = b;
-    }
-    const float* mw = sm.mag[lane];
-    for (int ci = 0; ci < kBins; ++ci) {
-      const float in[6] = {0.f, mw[ci * 4], mw[ci * 4 + 1], mw[ci * 4 + 2], mw[ci * 4 + 3], 0.f};
+        for (int r = 0; r < 4; ++r) {
+          const uint16_t h0 = f2bf(f[2 * r]), h1 = f2bf(f[2 * r + 1]);
+          const uint16_t l0 = f2bf(f[2 * r] - bf2f(h0)), l1 = f2bf(f[2 * r + 1] - bf2f(h1));
+          ah[r] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
+          al[r] = static_cast<uint32_t>(l0) | (static_cast<uint32_t>(l1) << 16);
+        }
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const float* wr = w.w0 + ((long long)(cg + c) * kBins + ci) * 3;
-        const float k0 = __ldg(wr), k1 = __ldg(wr + 1), k2 = __ldg(wr + 2);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          float a2 = acc[c][t];
-          a2 = fmaf(in[t], k0, a2);
-          a2 = fmaf(in[t + 1], k1, a2);
-          a2 = fmaf(in[t + 2], k2, a2);
-          acc[c][t] = a2;
+        for (int nt = 0; nt < 16; ++nt) {
+          const uint16_t* bh = sbh + (nt * 8 + g) * kLd + cl;
+          const uint16_t* bl = sbl + (nt * 8 + g) * kLd + cl;
+          const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(bh);
+          const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(bh + 8);
+          const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(bl);
+          const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(bl + 8);
+          mma_bf16(acc[nt], al[0], al[1], al[2], al[3], bh0, bh1);
+          mma_bf16(acc[nt], ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+          mma_bf16(acc[nt], ah[0], ah[1], ah[2], ah[3], bh0, bh1);
         }
       }
     }
     __syncthreads();  // e0 reuses the basis slice
 #pragma unroll
-    for (int c = 0; c < 16; ++c)
-#pragma unroll
-      for (int t = 0; t < 4; ++t) sm.e0[lane][(cg + c) * 4 + t] = fmaxf(acc[c][t], 0.f);
+    for (int nt = 0; nt < 16; ++nt) {
+      const int c = nt * 8 + 2 * t4;
+      const float b0 = __ldg(w.b0 + c), b1 = __ldg(w.b0 + c + 1);
+      sm.e0[ra >> 2][c * 4 + fa] = fmaxf(acc[nt][0] + b0, 0.f);
+      sm.e0[ra >> 2][(c + 1) * 4 + fa] = fmaxf(acc[nt][1] + b1, 0.f);
+      sm.e0[rb >> 2][c * 4 + fb] = fmaxf(acc[nt][2] + b0, 0.f);
+      sm.e0[rb >> 2][(c + 1) * 4 + fb] = fmaxf(acc[nt][3] + b1, 0.f);
+    }
   }
   __syncthreads();
   // ---- enc1: 128 -> 64, 4 -> 2, k3 s2 p1 (out t reads 2t-1, 2t, 2t+1) ----
@@ -490,11 +529,22 @@ void BatchVad::upload() {
         bhl[row] = hi;
         bhl[(size_t)kBasisRows * kNfft + row] = to_bf(v - from_bf(hi));
       }
+  const size_t w0_at = bhl.size();
+  bhl.resize(w0_at + (size_t)2 * 128 * 400, 0);
+  for (int n = 0; n < 128; ++n)
+    for (int k = 0; k < 3 * kBins; ++k) {
+      const float v = p_->host[1][(size_t)n * 3 * kBins + k];
+      const uint16_t hi = to_bf(v);
+      bhl[w0_at + (size_t)n * 400 + k] = hi;
+      bhl[w0_at + (size_t)128 * 400 + (size_t)n * 400 + k] = to_bf(v - from_bf(hi));
+    }
   if (p_->d_bhl) cudaFree(p_->d_bhl);
   p_->d_bhl = dalloc<uint16_t>(bhl.size());
   ORX_CHECK(cudaMemcpy(p_->d_bhl, bhl.data(), bhl.size() * 2, cudaMemcpyHostToDevice));
   p_->w.bh = p_->d_bhl;
   p_->w.bl = p_->d_bhl + (size_t)kBasisRows * kNfft;
+  p_->w.w0h = p_->d_bhl + w0_at;
+  p_->w.w0l = p_->d_bhl + w0_at + (size_t)128 * 400;
   if (p_->d_w) cudaFree(p_->d_w);
   p_->d_w = dalloc<float>(pk.size());
   ORX_CHECK(cudaMemcpy(p_->d_w, pk.data(), pk.size() * 4, cudaMemcpyHostToDevice));
