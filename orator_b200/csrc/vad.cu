@@ -97,15 +97,24 @@ __global__ void __launch_bounds__(256, 1) vad_frontend_kernel(const float* __res
   const long long row = (long long)steps * kWin;
 
   // ---- padded inputs: [context | window] then 64 reflected samples ----
+  // (each window's stream and step are worked out once, not per sample)
+  __shared__ long long wsrc[kFeWin];  // pcm offset of sample 0 of the window's context
+  __shared__ int wstream[kFeWin];
+  if (tid < kFeWin) {
+    const long long g = w0 + tid;
+    const int st = static_cast<int>(g / steps), k = static_cast<int>(g % steps);
+    wstream[tid] = st;
+    wsrc[tid] = st * row + (long long)k * kWin - kCtx;
+  }
+  __syncthreads();
   for (int i = tid; i < kFeWin * kPad; i += 256) {
     const int wi = i / kPad, j = i % kPad;
     float v = 0.f;
     if (wi < nw) {
-      const long long g = w0 + wi;
-      const int s = static_cast<int>(g / steps), k = static_cast<int>(g % steps);
       const int jj = j < kIn ? j : 2 * kIn - 2 - j;  // reflect right: out[576+i] = in[574-i]
-      const long long pos = (long long)k * kWin - kCtx + jj;
-      v = pos >= 0 ? pcm[s * row + pos] : ctx[(long long)s * kCtx + kCtx + pos];
+      const long long srow = (long long)wstream[wi] * row;
+      const long long pos = wsrc[wi] + jj;  // position kCtx + jj - kCtx within the stream
+      v = pos >= srow ? pcm[pos] : ctx[(long long)wstream[wi] * kCtx + kCtx + (pos - srow)];
     }
     sm.x[wi][j] = v;
   }
