@@ -46,6 +46,8 @@ struct VadW {
   // enc0 weights split the same way: [128][400], k = 3 ci + tap (zero past 387)
   const uint16_t* w0h;
   const uint16_t* w0l;
+  // LSTM [W_ih | W_hh] split and packed in mma fragment order (vad_lstm_kernel)
+  const uint16_t* lstm_b;
   const float* w0; const float* b0;  // [128][129][3]
   const float* w1; const float* b1;  // [64][128][3]
   const float* w2; const float* b2;  // [64][64][3]
@@ -331,101 +333,160 @@ __global__ void vad_ctx_kernel(const float* pcm, int S, int steps, float* ctx) {
 
 constexpr int kLstmStreams = 32;
 
+// LSTM scan on tensor cores. A CTA owns 32 streams and runs every step of
+// the chunk: gates[32][512] = [x_t | h] (32 x 256) . [W_ih | W_hh]^T + b as
+// mma.sync m16n8k16 with fp32-grade split-bf16 products (the weights are
+// pre-split and packed in fragment order, uint4 {bh0, bh1, bl0, bl1} per lane
+// and (warp, k-step, n-tile): one coalesced load each), then the cell update
+// and the head sigmoid(b + relu(h) . w). Warp w owns hidden units 16w ..
+// 16w+15: its 8 n-tiles are those units' columns of the i, f, g, o gates, so
+// a thread holds all four gates of its (stream, unit) pairs. h is double
+// buffered in shared memory: one barrier per step.
 // h, c: [S][128] carried state; xin: [steps][S][128]; probs: [S][steps].
+constexpr int kLsLd = kH + 4;
 __global__ void __launch_bounds__(256, 1) vad_lstm_kernel(const float* __restrict__ xin, int S,
                                                           int steps, VadW w, float* __restrict__ h,
                                                           float* __restrict__ c,
                                                           float* __restrict__ probs) {
-  __shared__ float xh[kLstmStreams][2 * kH];  // [x | h] per stream
-  __shared__ float red[kLstmStreams][kH / 2 + 1];
-  const int tid = threadIdx.x;
+  __shared__ __align__(16) float hs[2][kLstmStreams][kLsLd];
+  __shared__ float red[2][kLstmStreams][8];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
   const int s0 = blockIdx.x * kLstmStreams;
   const int ns = S - s0 < kLstmStreams ? S - s0 : kLstmStreams;
-  // thread: 8 streams x 2 hidden units x 4 gates
-  const int sg = (tid >> 6) * 8;      // streams sg .. sg+7
-  const int j0 = (tid & 63) * 2;      // hidden units j0, j0+1
-  float cst[8][2];
-#pragma unroll
-  for (int a = 0; a < 8; ++a)
-#pragma unroll
-    for (int u = 0; u < 2; ++u)
-      cst[a][u] = (sg + a < ns) ? c[(long long)(s0 + sg + a) * kH + j0 + u] : 0.f;
   for (int i = tid; i < kLstmStreams * kH; i += 256) {
     const int a = i / kH, j = i % kH;
-    xh[a][kH + j] = a < ns ? h[(long long)(s0 + a) * kH + j] : 0.f;
+    hs[0][a][j] = a < ns ? h[(long long)(s0 + a) * kH + j] : 0.f;
   }
-  float bias[4][2];
+  // this thread's (stream, unit) pairs: [mt][hlf][rh][e] -> stream mt*16 + g + 8 rh,
+  // unit 16 warp + 8 hlf + 2 t4 + e
+  float cst[2][2][2][2], bias[4][2][2], hw[2][2];
 #pragma unroll
-  for (int g = 0; g < 4; ++g)
+  for (int hlf = 0; hlf < 2; ++hlf)
 #pragma unroll
-    for (int u = 0; u < 2; ++u) bias[g][u] = __ldg(w.bias + g * kH + j0 + u);
-  const float hw0 = __ldg(w.head + j0), hw1 = __ldg(w.head + j0 + 1);
+    for (int e = 0; e < 2; ++e) {
+      const int u = 16 * warp + 8 * hlf + 2 * t4 + e;
+      hw[hlf][e] = __ldg(w.head + u);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) bias[q][hlf][e] = __ldg(w.bias + q * kH + u);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int rh = 0; rh < 2; ++rh) {
+          const int a = mt * 16 + g + 8 * rh;
+          cst[mt][hlf][rh][e] = a < ns ? c[(long long)(s0 + a) * kH + u] : 0.f;
+        }
+    }
+  const uint4* bp = reinterpret_cast<const uint4*>(w.lstm_b) + (size_t)warp * 16 * 8 * 32 + lane;
+  __syncthreads();
 
   for (int k = 0; k < steps; ++k) {
-    for (int i = tid; i < kLstmStreams * kH; i += 256) {
-      const int a = i / kH, j = i % kH;
-      xh[a][j] = a < ns ? __ldg(xin + ((long long)k * S + s0 + a) * kH + j) : 0.f;
-    }
-    __syncthreads();
-    float acc[8][4][2];
+    const int cur = k & 1;
+    float acc[2][8][4];
 #pragma unroll
-    for (int a = 0; a < 8; ++a)
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        acc[a][g][0] = bias[g][0];
-        acc[a][g][1] = bias[g][1];
-      }
-    for (int kk = 0; kk < 2 * kH; ++kk) {
-      const float* wr = w.wt + (long long)kk * 4 * kH + j0;
-      float2 wv[4];
+      for (int nt = 0; nt < 8; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.f;
+#pragma unroll 1
+    for (int ks = 0; ks < 16; ++ks) {
+      uint4 bq[8];
 #pragma unroll
-      for (int g = 0; g < 4; ++g) wv[g] = __ldg(reinterpret_cast<const float2*>(wr + g * kH));
+      for (int nt = 0; nt < 8; ++nt) bq[nt] = __ldg(bp + (ks * 8 + nt) * 32);
+      uint32_t ah[2][4], al[2][4];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) {
-        const float v = xh[sg + a][kk];
+      for (int mt = 0; mt < 2; ++mt) {
+        const int ra = mt * 16 + g, rb = ra + 8;
+        const int cc = (ks & 7) * 16 + 2 * t4;
+        float2 v[4];
+        if (ks < 8) {  // x_t
+          const float* xa = xin + ((long long)k * S + s0 + ra) * kH;
+          const float* xb = xin + ((long long)k * S + s0 + rb) * kH;
+          const bool oa = ra < ns, ob = rb < ns;
+          v[0] = oa ? *reinterpret_cast<const float2*>(xa + cc) : make_float2(0.f, 0.f);
+          v[1] = ob ? *reinterpret_cast<const float2*>(xb + cc) : make_float2(0.f, 0.f);
+          v[2] = oa ? *reinterpret_cast<const float2*>(xa + cc + 8) : make_float2(0.f, 0.f);
+          v[3] = ob ? *reinterpret_cast<const float2*>(xb + cc + 8) : make_float2(0.f, 0.f);
+        } else {        // h
+          v[0] = *reinterpret_cast<const float2*>(&hs[cur][ra][cc]);
+          v[1] = *reinterpret_cast<const float2*>(&hs[cur][rb][cc]);
+          v[2] = *reinterpret_cast<const float2*>(&hs[cur][ra][cc + 8]);
+          v[3] = *reinterpret_cast<const float2*>(&hs[cur][rb][cc + 8]);
+        }
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          acc[a][g][0] = fmaf(v, wv[g].x, acc[a][g][0]);
-          acc[a][g][1] = fmaf(v, wv[g].y, acc[a][g][1]);
+        for (int r = 0; r < 4; ++r) {
+          const uint16_t h0 = f2bf(v[r].x), h1 = f2bf(v[r].y);
+          const uint16_t l0 = f2bf(v[r].x - bf2f(h0)), l1 = f2bf(v[r].y - bf2f(h1));
+          ah[mt][r] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
+          al[mt][r] = static_cast<uint32_t>(l0) | (static_cast<uint32_t>(l1) << 16);
         }
       }
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          mma_bf16(acc[mt][nt], al[mt][0], al[mt][1], al[mt][2], al[mt][3], bq[nt].x, bq[nt].y);
+          mma_bf16(acc[mt][nt], ah[mt][0], ah[mt][1], ah[mt][2], ah[mt][3], bq[nt].z, bq[nt].w);
+          mma_bf16(acc[mt][nt], ah[mt][0], ah[mt][1], ah[mt][2], ah[mt][3], bq[nt].x, bq[nt].y);
+        }
     }
-    __syncthreads();  // every thread has read h of this step
-    float part[8];
+    // cell update: gate q of (mt, hlf, rh, e) is acc[mt][2q + hlf][2 rh + e]
+    const int nxt = cur ^ 1;
+    float part[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [mt][rh] head partials
 #pragma unroll
-    for (int a = 0; a < 8; ++a) {
-      float hs[2];
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const float gi = 1.0f / (1.0f + expf(-acc[a][0][u]));
-        const float gf = 1.0f / (1.0f + expf(-acc[a][1][u]));
-        const float gg = tanhf(acc[a][2][u]);
-        const float go = 1.0f / (1.0f + expf(-acc[a][3][u]));
-        cst[a][u] = gf * cst[a][u] + gi * gg;
-        hs[u] = go * tanhf(cst[a][u]);
-        xh[sg + a][kH + j0 + u] = hs[u];
+      for (int hlf = 0; hlf < 2; ++hlf)
+#pragma unroll
+        for (int rh = 0; rh < 2; ++rh)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float xi = acc[mt][hlf][2 * rh + e] + bias[0][hlf][e];
+            const float xf = acc[mt][2 + hlf][2 * rh + e] + bias[1][hlf][e];
+            const float xg = acc[mt][4 + hlf][2 * rh + e] + bias[2][hlf][e];
+            const float xo = acc[mt][6 + hlf][2 * rh + e] + bias[3][hlf][e];
+            const float gi = 1.0f / (1.0f + expf(-xi));
+            const float gf = 1.0f / (1.0f + expf(-xf));
+            const float gg = tanhf(xg);
+            const float go = 1.0f / (1.0f + expf(-xo));
+            float& cs = cst[mt][hlf][rh][e];
+            cs = gf * cs + gi * gg;
+            const float hv = go * tanhf(cs);
+            hs[nxt][mt * 16 + g + 8 * rh][16 * warp + 8 * hlf + 2 * t4 + e] = hv;
+            part[mt][rh] += fmaxf(hv, 0.f) * hw[hlf][e];
+          }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int rh = 0; rh < 2; ++rh) {
+        float v = part[mt][rh];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (t4 == 0) red[cur][mt * 16 + g + 8 * rh][warp] = v;
       }
-      part[a] = fmaxf(hs[0], 0.f) * hw0 + fmaxf(hs[1], 0.f) * hw1;
-    }
-#pragma unroll
-    for (int a = 0; a < 8; ++a) red[sg + a][tid & 63] = part[a];
     __syncthreads();
     if (tid < ns) {
       float d = w.head_b;
-      for (int q = 0; q < kH / 2; ++q) d += red[tid][q];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) d += red[cur][tid][q];
       probs[(long long)(s0 + tid) * steps + k] = 1.0f / (1.0f + expf(-d));
     }
   }
-  __syncthreads();
+  const int fin = steps & 1;
   for (int i = tid; i < kLstmStreams * kH; i += 256) {
     const int a = i / kH, j = i % kH;
-    if (a < ns) h[(long long)(s0 + a) * kH + j] = xh[a][kH + j];
+    if (a < ns) h[(long long)(s0 + a) * kH + j] = hs[fin][a][j];
   }
 #pragma unroll
-  for (int a = 0; a < 8; ++a)
+  for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
-      if (sg + a < ns) c[(long long)(s0 + sg + a) * kH + j0 + u] = cst[a][u];
+    for (int hlf = 0; hlf < 2; ++hlf)
+#pragma unroll
+      for (int rh = 0; rh < 2; ++rh)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int a = mt * 16 + g + 8 * rh;
+          if (a < ns) c[(long long)(s0 + a) * kH + 16 * warp + 8 * hlf + 2 * t4 + e] = cst[mt][hlf][rh][e];
+        }
 }
 
 }  // namespace
@@ -547,6 +608,34 @@ void BatchVad::upload() {
       bhl[w0_at + (size_t)n * 400 + k] = hi;
       bhl[w0_at + (size_t)128 * 400 + (size_t)n * 400 + k] = to_bf(v - from_bf(hi));
     }
+  // LSTM weights: uint4 {bh0, bh1, bl0, bl1} per (warp, k-step, n-tile, lane);
+  // n-tile nt of warp w covers gate nt / 2, units 16 w + 8 (nt % 2) + 0..7
+  const size_t ls_at = bhl.size();
+  bhl.resize(ls_at + (size_t)8 * 16 * 8 * 32 * 8, 0);
+  {
+    auto W = [&](int n, int k) {
+      return k < kH ? p_->host[9][(size_t)n * kH + k] : p_->host[10][(size_t)n * kH + k - kH];
+    };
+    size_t o = ls_at;
+    for (int wp = 0; wp < 8; ++wp)
+      for (int ks = 0; ks < 16; ++ks)
+        for (int nt = 0; nt < 8; ++nt)
+          for (int ln = 0; ln < 32; ++ln, o += 8) {
+            const int g = ln >> 2, t = ln & 3;
+            const int n = (nt >> 1) * kH + 16 * wp + (nt & 1) * 8 + g;
+            const int k = ks * 16 + 2 * t;
+            const int ks4[4] = {k, k + 1, k + 8, k + 9};
+            uint16_t hi[4], lo[4];
+            for (int q = 0; q < 4; ++q) {
+              const float v = W(n, ks4[q]);
+              hi[q] = to_bf(v);
+              lo[q] = to_bf(v - from_bf(hi[q]));
+            }
+            // {bh0, bh1, bl0, bl1}: (k, k+1) and (k+8, k+9), high then low parts
+            const uint16_t v8[8] = {hi[0], hi[1], hi[2], hi[3], lo[0], lo[1], lo[2], lo[3]};
+            for (int q = 0; q < 8; ++q) bhl[o + q] = v8[q];
+          }
+  }
   if (p_->d_bhl) cudaFree(p_->d_bhl);
   p_->d_bhl = dalloc<uint16_t>(bhl.size());
   ORX_CHECK(cudaMemcpy(p_->d_bhl, bhl.data(), bhl.size() * 2, cudaMemcpyHostToDevice));
@@ -554,6 +643,7 @@ void BatchVad::upload() {
   p_->w.bl = p_->d_bhl + (size_t)kBasisRows * kNfft;
   p_->w.w0h = p_->d_bhl + w0_at;
   p_->w.w0l = p_->d_bhl + w0_at + (size_t)128 * 400;
+  p_->w.lstm_b = p_->d_bhl + ls_at;
   if (p_->d_w) cudaFree(p_->d_w);
   p_->d_w = dalloc<float>(pk.size());
   ORX_CHECK(cudaMemcpy(p_->d_w, pk.data(), pk.size() * 4, cudaMemcpyHostToDevice));
