@@ -48,6 +48,9 @@ struct VadW {
   const uint16_t* w0l;
   // LSTM [W_ih | W_hh] split and packed in mma fragment order (vad_lstm_kernel)
   const uint16_t* lstm_b;
+  // enc1 [64][384] (k = 3 ci + tap), enc2 [64][128] (k = 2 ci + tap - 1, taps
+  // 1 and 2), enc3 [128][64] (centre tap): split like enc0
+  const uint16_t *w1h, *w1l, *w2h, *w2l, *w3h, *w3l;
   const float* w0; const float* b0;  // [128][129][3]
   const float* w1; const float* b1;  // [64][128][3]
   const float* w2; const float* b2;  // [64][64][3]
@@ -257,68 +260,113 @@ __global__ void __launch_bounds__(256, 1) vad_frontend_kernel(const float* __res
     }
   }
   __syncthreads();
-  // ---- enc1: 128 -> 64, 4 -> 2, k3 s2 p1 (out t reads 2t-1, 2t, 2t+1) ----
+  // ---- enc1 / enc2 / enc3 on tensor cores (split-bf16, as enc0) ----
+  // enc1: 128 -> 64, 4 -> 2 frames, k3 s2 p1: rows (window, t), k = 3 ci + tap,
+  //   A = e0[ci][2t + tap - 1] (zero at position -1);
+  // enc2: 64 -> 64, 2 -> 1, k3 s2 p1: rows = windows, k = 2 ci + (tap - 1) for
+  //   the taps that see data (positions 0, 1);
+  // enc3: 64 -> 128, 1 -> 1, k3 s1 p1: rows = windows, k = ci (centre tap).
   {
-    const int cg = warp * 8;
-    float acc[8][2];
+    const int g = lane >> 2, t4 = lane & 3;
+    uint16_t* sbh = reinterpret_cast<uint16_t*>(&sm.x[0][0]);
+    // stage rows [0, N) x cols [k0, k0 + KC) of a split [N][Kt] weight (hi then lo)
+    auto stage = [&](const uint16_t* wh, const uint16_t* wl, int N, int Kt, int k0, int KC, int ld) {
+      __syncthreads();
+      uint16_t* sbl = sbh + N * ld;
+      for (int i = tid; i < N * (KC / 8); i += 256) {
+        const int n = i / (KC / 8), c = i % (KC / 8);
+        const size_t src = (size_t)n * Kt + k0;
+        reinterpret_cast<uint4*>(sbh + n * ld)[c] = __ldg(reinterpret_cast<const uint4*>(wh + src) + c);
+        reinterpret_cast<uint4*>(sbl + n * ld)[c] = __ldg(reinterpret_cast<const uint4*>(wl + src) + c);
+      }
+      __syncthreads();
+    };
+    // acc[nt] += A(rows ra, rb; k0 + ...) . B(n-tiles n0 .., staged, ld) over KC
+    auto mma_chunk = [&](float (*acc)[4], int ntiles, int n0, int N, int ld, int KC, int k0, auto aval,
+                         int ra, int rb) {
+      const uint16_t* sbl = sbh + N * ld;
+      for (int ks = 0; ks < KC / 16; ++ks) {
+        const int cl = ks * 16 + 2 * t4, k = k0 + cl;
+        const float f[8] = {aval(ra, k), aval(ra, k + 1), aval(rb, k), aval(rb, k + 1),
+                            aval(ra, k + 8), aval(ra, k + 9), aval(rb, k + 8), aval(rb, k + 9)};
+        uint32_t ah[4], al[4];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) acc[c][0] = acc[c][1] = __ldg(w.b1 + cg + c);
-    const float* ew = sm.e0[lane];
-    for (int ci = 0; ci < 128; ++ci) {
-      const float i0 = ew[ci * 4], i1 = ew[ci * 4 + 1], i2 = ew[ci * 4 + 2], i3 = ew[ci * 4 + 3];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float* wr = w.w1 + ((long long)(cg + c) * 128 + ci) * 3;
-        const float k0 = __ldg(wr), k1 = __ldg(wr + 1), k2 = __ldg(wr + 2);
-        acc[c][0] = fmaf(i1, k2, fmaf(i0, k1, acc[c][0]));             // positions -1 (zero), 0, 1
-        acc[c][1] = fmaf(i3, k2, fmaf(i2, k1, fmaf(i1, k0, acc[c][1])));  // positions 1, 2, 3
+        for (int r = 0; r < 4; ++r) {
+          const uint16_t h0 = f2bf(f[2 * r]), h1 = f2bf(f[2 * r + 1]);
+          const uint16_t l0 = f2bf(f[2 * r] - bf2f(h0)), l1 = f2bf(f[2 * r + 1] - bf2f(h1));
+          ah[r] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
+          al[r] = static_cast<uint32_t>(l0) | (static_cast<uint32_t>(l1) << 16);
+        }
+        for (int nt = 0; nt < ntiles; ++nt) {
+          const int n = n0 + nt * 8 + g;
+          const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(sbh + n * ld + cl);
+          const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(sbh + n * ld + cl + 8);
+          const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(sbl + n * ld + cl);
+          const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(sbl + n * ld + cl + 8);
+          mma_bf16(acc[nt], al[0], al[1], al[2], al[3], bh0, bh1);
+          mma_bf16(acc[nt], ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+          mma_bf16(acc[nt], ah[0], ah[1], ah[2], ah[3], bh0, bh1);
+        }
+      }
+    };
+    // enc1: 64 rows = 4 m-tiles; warp -> m-tile warp % 4, n-tiles 4 (warp / 4) .. +3
+    {
+      const int ra = (warp & 3) * 16 + g, rb = ra + 8, n0 = (warp >> 2) * 32;
+      auto aval = [&](int r, int k) {
+        const int ci = (k * 43691) >> 17, tap = k - 3 * ci, p = 2 * (r & 1) + tap - 1;
+        return p >= 0 ? sm.e0[r >> 1][ci * 4 + p] : 0.f;
+      };
+      float acc[4][4] = {};
+      for (int k0 = 0; k0 < 384; k0 += 192) {
+        stage(w.w1h, w.w1l, 64, 384, k0, 192, 200);
+        mma_chunk(acc, 4, n0, 64, 200, 192, k0, aval, ra, rb);
+      }
+      for (int nt = 0; nt < 4; ++nt) {
+        const int c = n0 + nt * 8 + 2 * t4;
+        const float b0 = __ldg(w.b1 + c), b1 = __ldg(w.b1 + c + 1);
+        sm.e1[ra >> 1][c * 2 + (ra & 1)] = fmaxf(acc[nt][0] + b0, 0.f);
+        sm.e1[ra >> 1][(c + 1) * 2 + (ra & 1)] = fmaxf(acc[nt][1] + b1, 0.f);
+        sm.e1[rb >> 1][c * 2 + (rb & 1)] = fmaxf(acc[nt][2] + b0, 0.f);
+        sm.e1[rb >> 1][(c + 1) * 2 + (rb & 1)] = fmaxf(acc[nt][3] + b1, 0.f);
       }
     }
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      sm.e1[lane][(cg + c) * 2] = fmaxf(acc[c][0], 0.f);
-      sm.e1[lane][(cg + c) * 2 + 1] = fmaxf(acc[c][1], 0.f);
-    }
-  }
-  __syncthreads();
-  // ---- enc2: 64 -> 64, 2 -> 1, k3 s2 p1 (reads positions -1, 0, 1) ----
-  {
-    const int cg = warp * 8;
-    float acc[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[c] = __ldg(w.b2 + cg + c);
-    const float* ew = sm.e1[lane];
-    for (int ci = 0; ci < 64; ++ci) {
-      const float a0 = ew[ci * 2], a1 = ew[ci * 2 + 1];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float* wr = w.w2 + ((long long)(cg + c) * 64 + ci) * 3;
-        acc[c] = fmaf(a1, __ldg(wr + 2), fmaf(a0, __ldg(wr + 1), acc[c]));
+    // enc2: 32 rows = 2 m-tiles; warp -> m-tile warp % 2, n-tiles 2 (warp / 2) .. +1
+    {
+      const int ra = (warp & 1) * 16 + g, rb = ra + 8, n0 = (warp >> 1) * 16;
+      auto aval = [&](int r, int k) { return sm.e1[r][k]; };  // k = 2 ci + position
+      float acc[2][4] = {};
+      stage(w.w2h, w.w2l, 64, 128, 0, 128, 136);
+      mma_chunk(acc, 2, n0, 64, 136, 128, 0, aval, ra, rb);
+      for (int nt = 0; nt < 2; ++nt) {
+        const int c = n0 + nt * 8 + 2 * t4;
+        const float b0 = __ldg(w.b2 + c), b1 = __ldg(w.b2 + c + 1);
+        sm.e2[ra][c] = fmaxf(acc[nt][0] + b0, 0.f);
+        sm.e2[ra][c + 1] = fmaxf(acc[nt][1] + b1, 0.f);
+        sm.e2[rb][c] = fmaxf(acc[nt][2] + b0, 0.f);
+        sm.e2[rb][c + 1] = fmaxf(acc[nt][3] + b1, 0.f);
       }
     }
-#pragma unroll
-    for (int c = 0; c < 8; ++c) sm.e2[lane][cg + c] = fmaxf(acc[c], 0.f);
-  }
-  __syncthreads();
-  // ---- enc3: 64 -> 128, 1 -> 1, k3 s1 p1 (only the centre tap sees data) ----
-  {
-    const int cg = warp * 16;
-    float acc[16];
-#pragma unroll
-    for (int c = 0; c < 16; ++c) acc[c] = __ldg(w.b3 + cg + c);
-    const float* ew = sm.e2[lane];
-    for (int ci = 0; ci < 64; ++ci) {
-      const float a = ew[ci];
-#pragma unroll
-      for (int c = 0; c < 16; ++c)
-        acc[c] = fmaf(a, __ldg(w.w3 + ((long long)(cg + c) * 64 + ci) * 3 + 1), acc[c]);
-    }
-    if (lane < nw) {
-      const long long g = w0 + lane;
-      const int s = static_cast<int>(g / steps), k = static_cast<int>(g % steps);
-      float* o = out + ((long long)k * S + s) * kH + cg;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) o[c] = fmaxf(acc[c], 0.f);
+    // enc3: 32 rows = 2 m-tiles; warp -> m-tile warp % 2, n-tiles 4 (warp / 2) .. +3
+    {
+      const int ra = (warp & 1) * 16 + g, rb = ra + 8, n0 = (warp >> 1) * 32;
+      auto aval = [&](int r, int k) { return sm.e2[r][k]; };
+      float acc[4][4] = {};
+      stage(w.w3h, w.w3l, 128, 64, 0, 64, 72);
+      mma_chunk(acc, 4, n0, 128, 72, 64, 0, aval, ra, rb);
+      const int rows[2] = {ra, rb};
+      for (int rr = 0; rr < 2; ++rr) {
+        const int r = rows[rr];
+        if (r < nw) {
+          const long long gw = w0 + r;
+          const int st = static_cast<int>(gw / steps), k = static_cast<int>(gw % steps);
+          float* o = out + ((long long)k * S + st) * kH;
+          for (int nt = 0; nt < 4; ++nt) {
+            const int c = n0 + nt * 8 + 2 * t4;
+            o[c] = fmaxf(acc[nt][2 * rr] + __ldg(w.b3 + c), 0.f);
+            o[c + 1] = fmaxf(acc[nt][2 * rr + 1] + __ldg(w.b3 + c + 1), 0.f);
+          }
+        }
+      }
     }
   }
 }
@@ -636,6 +684,24 @@ void BatchVad::upload() {
             for (int q = 0; q < 8; ++q) bhl[o + q] = v8[q];
           }
   }
+  // enc1..3 weights, split
+  auto put_split = [&](int N, int Kt, auto val) {
+    const size_t at = bhl.size();
+    bhl.resize(at + (size_t)2 * N * Kt, 0);
+    for (int n = 0; n < N; ++n)
+      for (int k = 0; k < Kt; ++k) {
+        const float v = val(n, k);
+        const uint16_t hi = to_bf(v);
+        bhl[at + (size_t)n * Kt + k] = hi;
+        bhl[at + (size_t)N * Kt + (size_t)n * Kt + k] = to_bf(v - from_bf(hi));
+      }
+    return at;
+  };
+  const size_t w1_at = put_split(64, 384, [&](int n, int k) { return p_->host[3][(size_t)n * 384 + k]; });
+  const size_t w2_at = put_split(64, 128, [&](int n, int k) {
+    return p_->host[5][((size_t)n * 64 + k / 2) * 3 + 1 + (k & 1)];
+  });
+  const size_t w3_at = put_split(128, 64, [&](int n, int k) { return p_->host[7][((size_t)n * 64 + k) * 3 + 1]; });
   if (p_->d_bhl) cudaFree(p_->d_bhl);
   p_->d_bhl = dalloc<uint16_t>(bhl.size());
   ORX_CHECK(cudaMemcpy(p_->d_bhl, bhl.data(), bhl.size() * 2, cudaMemcpyHostToDevice));
@@ -644,6 +710,12 @@ void BatchVad::upload() {
   p_->w.w0h = p_->d_bhl + w0_at;
   p_->w.w0l = p_->d_bhl + w0_at + (size_t)128 * 400;
   p_->w.lstm_b = p_->d_bhl + ls_at;
+  p_->w.w1h = p_->d_bhl + w1_at;
+  p_->w.w1l = p_->d_bhl + w1_at + (size_t)64 * 384;
+  p_->w.w2h = p_->d_bhl + w2_at;
+  p_->w.w2l = p_->d_bhl + w2_at + (size_t)64 * 128;
+  p_->w.w3h = p_->d_bhl + w3_at;
+  p_->w.w3l = p_->d_bhl + w3_at + (size_t)128 * 64;
   if (p_->d_w) cudaFree(p_->d_w);
   p_->d_w = dalloc<float>(pk.size());
   ORX_CHECK(cudaMemcpy(p_->d_w, pk.data(), pk.size() * 4, cudaMemcpyHostToDevice));
