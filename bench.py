@@ -464,8 +464,8 @@ def run_config5(torch, cpu: bool, ref_gpu: bool, reps: int = 3):
                        "fp32, seed 4, LSTM state carried across steps",
            "value": windows / (ms * 1e-3), "unit": "windows/s", "ms_per_step": ms,
            "tflops": flops / (ms * 1e-3) / 1e12, "roofline": {
-               "bound": "fp32 FMA (SIMT)", "achieved": flops / (ms * 1e-3) / 1e12,
-               "peak": peak, "peak_kind": "nominal 148 SM x 128 FMA/clk x 1.965 GHz",
+               "bound": "fp32 work (split-bf16 tensor-core MMAs)", "achieved": flops / (ms * 1e-3) / 1e12,
+               "peak": peak, "peak_kind": "nominal fp32 issue rate, 148 SM x 128 FMA/clk x 1.965 GHz",
                "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / peak},
            "e2e": {"value": windows / e2e_s, "unit": "windows/s",
                    "h2d_bytes_per_step": S * steps * 512 * 4, "d2h_bytes_per_step": S * steps * 4}}
