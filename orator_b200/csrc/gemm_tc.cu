@@ -24,6 +24,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <utility>
@@ -570,11 +571,14 @@ bool make_tmap_2d(void* map, const void* base, long long rows, int cols, int box
 }
 
 int tc_sms() {
-  static int sms_of[64];
+  static std::atomic<int> sms_of[64];  // per device, filled on first use
   int dev = 0;
   cudaGetDevice(&dev);
-  int& v = sms_of[dev & 63];
-  if (v <= 0) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  int v = sms_of[dev & 63].load(std::memory_order_relaxed);
+  if (v <= 0) {
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    sms_of[dev & 63].store(v, std::memory_order_relaxed);
+  }
   return v > 0 ? v : 148;
 }
 
