@@ -276,6 +276,9 @@ def run_ragged(dec, torch, world, dist, rank=0, strong=False, steps=256):
     joins_pinned = torch.empty((8 * PROMPT_ROWS, HIDDEN), dtype=torch.float32, pin_memory=True)
     joins_pinned.copy_(torch.from_numpy(np.concatenate(joins, 0)))
     joins_cat = joins_pinned.numpy()
+    # a rank that takes only some of the joins stages their rows here (pinned,
+    # contiguous) so its prefill copy is asynchronous as in the full case
+    stage = torch.empty((8 * PROMPT_ROWS, HIDDEN), dtype=torch.float32, pin_memory=True).numpy()
 
     # warm-up join (untimed): sizes the row buffers and split-K workspace for
     # an 8 x 400-row prefill, as the W warm-up steps do for the decode step
@@ -321,7 +324,10 @@ def run_ragged(dec, torch, world, dist, rank=0, strong=False, steps=256):
             if len(mine) == 8:
                 bd.prefill([m[0] for m in mine], joins_cat, lens=[PROMPT_ROWS] * 8)
             elif mine:
-                bd.prefill([m[0] for m in mine], [m[1] for m in mine])
+                for i, (_, rows_i) in enumerate(mine):
+                    stage[i * PROMPT_ROWS:(i + 1) * PROMPT_ROWS] = rows_i
+                bd.prefill([m[0] for m in mine], stage[:len(mine) * PROMPT_ROWS],
+                           lens=[PROMPT_ROWS] * len(mine))
             p1.record(s0)
             p1.synchronize()
             pre_ms += p0.elapsed_time(p1)
